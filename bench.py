@@ -1,0 +1,264 @@
+"""Benchmark of the cPDE epoch on B200s (driver contract: one JSON line on rank 0).
+
+Workload: MLP 2->128->128->128->128->1 sigmoid,
+float32, weights N(0, 1/fan_in) from seed 0 with zero biases, 65,536 points
+uniform in [0,1]^2 (seed 1), every pure and mixed derivative through order 6
+(28 rows), squared-error matching against sin(2 pi x) exp(-y) and its
+derivatives with unit weights. One step = one fixed-weight epoch: forward of
+all rows, loss, output adjoints and the weight gradients of every layer (the
+reference's op-90 epoch, docs/benchmarks/fourier-timing.patch). Each rank
+processes its own 65,536 points (weak scaling); for N > 1 the ranks exchange
+gradients with one NCCL all-reduce per epoch.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+"""
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+LAYERS = [2, 128, 128, 128, 128, 1]
+ORDER = 6
+POINTS = 65536
+METRIC = 'points*derivs/s (2->128^4->1 sigmoid, order 6 all mixed, fixed-weight epoch)'
+UNIT = 'points*derivs/s'
+
+
+def workload(points=POINTS, order=ORDER, seed=1):
+    from cpde_b200.expressions import all_mixed, glorot_like, quadrature_inputs
+    t = all_mixed(order, 'xy')
+    pts = np.random.default_rng(seed).uniform(0, 1, (points, 2))
+    x = quadrature_inputs(pts, t)
+    targets = np.zeros((len(t), 1, points), np.float32)
+    for i, (_, a, b) in enumerate(t):
+        targets[i, 0] = ((2 * np.pi) ** a * np.sin(2 * np.pi * pts[:, 0] + a * np.pi / 2)
+                         * (-1.0) ** b * np.exp(-pts[:, 1]))
+    return t, x, targets, glorot_like(LAYERS, seed=0)
+
+
+def gemm_flops(points, rows):
+    """Algorithmic GEMM FLOPs of one epoch (forward, weight and input gradients)."""
+    pairs = list(zip(LAYERS[:-1], LAYERS[1:]))
+    fwd = sum(2 * a * b for a, b in pairs)
+    wgrad = sum(2 * (a + 1) * b for a, b in pairs)
+    dgrad = sum(2 * a * b for a, b in pairs[1:])
+    return points * rows * fwd, points * rows * dgrad, points * rows * wgrad
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    def __init__(self, index):
+        self.path = Path(tempfile.mkstemp(suffix='.csv')[1])
+        query = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
+                 'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
+                 'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
+        try:
+            self.proc = subprocess.Popen(['nvidia-smi', f'--id={index}', f'--query-gpu={query}',
+                                          '--format=csv,noheader,nounits', '-lms', '200'],
+                                         stdout=open(self.path, 'w'), stderr=subprocess.DEVNULL)
+        except FileNotFoundError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        self.proc.wait()
+        rows = [line.split(', ') for line in self.path.read_text().splitlines() if line.strip()]
+        self.path.unlink()
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace('.', '').isdigit()]
+        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.strip() == 'Active'})
+        return dict(sm_mhz=statistics.median(sm) if sm else None,
+                    sm_max_mhz=float(rows[0][2]) if rows[0][2].replace('.', '').isdigit() else None,
+                    samples=len(rows), reasons=reasons)
+
+
+def measured_peaks():
+    path = ROOT / 'MEASURED_PEAKS.json'
+    if path.exists():
+        return json.loads(path.read_text()), 'measured'
+    return {'hbm_gbs': 6650.0, 'bf16_tflops': 1590.0}, 'fallback'
+
+
+def cpu_baseline(points=128, steps=2):
+    """Reference CPU server (built from the reference's own sources) on a
+    bounded sample of the same workload; serial engine, 1 core."""
+    exe = ROOT / 'oracle' / '_ref' / 'cpde_ref_cpu_server'
+    if not exe.exists():
+        return None
+    from cpde_b200.client import Data, Network, Session
+    t, x, targets, weights = workload(points)
+    with Session(exe) as s:
+        net = Network(s, LAYERS, weights=weights)
+        inp = Data(s, x, t)
+        tgt = Data(s, targets, t)
+        cost = net.matching(inp, tgt, np.ones((1, len(t)), np.float32))
+        wall, _, _, _ = net.benchmark(cost, warm=0, iterations=1, batches=steps)
+    ms = float(np.median(wall))
+    return dict(value=points * len(t) / (ms / 1000), unit=UNIT, cores=1, kind='reference',
+                sample=f'{points} of the {POINTS} points, {steps} op-90 epochs, median; '
+                       'cpde_ref_cpu_server (oracle/Makefile), serial CPU backend',
+                ms_per_epoch_sample=ms)
+
+
+def run_reference(args):
+    rank = int(os.environ.get('RANK', '0'))
+    if rank != 0:
+        return
+    steps = max(1, args.steps)
+    base = cpu_baseline(points=args.reference_points, steps=steps)
+    if base is None:
+        print(json.dumps({'impl': 'reference', 'unavailable': 'oracle/_ref/cpde_ref_cpu_server is not built'}))
+        return
+    line = dict(metric=METRIC, value=base['value'], unit=UNIT, n_gpus=args.gpus, steps=steps, warmup=0,
+                ms_per_step=base['ms_per_epoch_sample'], higher_is_better=True, scaling='weak', vs_baseline=None,
+                dtype='f32', data='synthetic', impl='reference',
+                config=dict(workload='config 2 (65,536 pts, order 6, 2->128^4->1), bounded sample',
+                            sample_points=args.reference_points),
+                cpu_baseline=dict(value=base['value'], unit=UNIT, cores=1, kind='reference',
+                                  sample=base['sample']),
+                e2e=dict(value=base['value'], unit=UNIT, h2d_bytes_per_step=0, d2h_bytes_per_step=0))
+    print(json.dumps(line))
+
+
+def run_b200(args):
+    import torch
+    rank = int(os.environ.get('RANK', '0'))
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group('nccl', timeout=timedelta(seconds=120), device_id=torch.device('cuda', local))
+    from cpde_b200 import native
+    engine = native.Engine(local)
+    t, x, targets, weights = workload(args.points)
+    net = engine.network(LAYERS, weights)
+    inp = engine.data(x, t)
+    tgt = engine.data(targets, t)
+    R = len(t)
+    rows = list(range(R))
+    cost = engine.matching(net, inp, tgt, rows, rows, 1, np.ones((R, 1, 1), np.float32))
+    params = sum((a + 1) * b for a, b in zip(LAYERS[:-1], LAYERS[1:]))
+    stream = torch.cuda.ExternalStream(engine.stream())
+
+    def sync_all():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        engine.epoch(net, [cost])
+    sync_all()
+    engine.timing(True)
+    engine.timing_report()
+    clocks = Clocks(local)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sync_all()
+    start.record(stream)
+    for _ in range(args.steps):
+        engine.epoch(net, [cost])
+    stop.record(stream)
+    torch.cuda.synchronize()
+    clock = clocks.stop()
+    ms = start.elapsed_time(stop) / args.steps
+    kernels = engine.timing_report()
+    engine.timing(False)
+    if dist is not None:
+        m = torch.tensor([ms], device='cuda')
+        dist.all_reduce(m, op=dist.ReduceOp.MAX)
+        ms = float(m.item())
+    value = world * args.points * R / (ms / 1000)
+
+    # end to end through the public API: pinned host inputs in, objective and gradient out
+    # pinned host copies already in the engine's (derivative, sample, channel) layout
+    pinned_x = torch.from_numpy(np.ascontiguousarray(x.transpose(0, 2, 1))).pin_memory()
+    pinned_t = torch.from_numpy(np.ascontiguousarray(targets.transpose(0, 2, 1))).pin_memory()
+    host_grad = np.zeros(params, np.float32)
+    sync_all()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        engine.replace_raw(inp, pinned_x.data_ptr(), pinned_x.numel())
+        engine.replace_raw(tgt, pinned_t.data_ptr(), pinned_t.numel())
+        engine.epoch(net, [cost])
+        loss, host_grad = engine.epoch_result(net, params)
+    sync_all()
+    e2e_ms = (time.perf_counter() - t0) * 1000 / args.steps
+    if dist is not None:
+        m = torch.tensor([e2e_ms], device='cuda')
+        dist.all_reduce(m, op=dist.ReduceOp.MAX)
+        e2e_ms = float(m.item())
+
+    fwd, dgrad, wgrad = gemm_flops(args.points, R)
+    peaks, source = measured_peaks()
+    launches = sum(v[0] for v in kernels.values()) // args.steps
+    top = max(kernels.items(), key=lambda kv: kv[1][1])
+    # Algorithmic FLOPs per class: 'gemm' carries forward and input-gradient GEMMs.
+    class_flops = {'gemm': fwd + dgrad, 'gemm_wgrad': wgrad}
+    flops = class_flops.get(top[0])
+    fp32_peak = 148 * 128 * 2 * (clock['sm_max_mhz'] if clock and clock['sm_max_mhz'] else 1965.0) / 1e6
+    roofline = None
+    if flops is not None:
+        achieved = flops / (top[1][1] / args.steps / 1000) / 1e12
+        roofline = dict(kernel=top[0], bound='fp32-ffma', achieved=achieved, peak=fp32_peak, unit='TFLOP/s',
+                        frac=achieved / fp32_peak, traffic=None,
+                        peak_source='nominal FP32 CUDA-core peak (148 SMs x 128 lanes x 2 x max SM clock); '
+                                    f'MEASURED_PEAKS.json ({source}) has no FP32 figure',
+                        share=top[1][1] / sum(v[1] for v in kernels.values()))
+    if rank == 0:
+        line = dict(metric=METRIC, value=value, unit=UNIT, n_gpus=world, steps=args.steps, warmup=args.warmup,
+                    ms_per_step=ms, higher_is_better=True, scaling='weak', vs_baseline=None, dtype='f32',
+                    data='synthetic',
+                    config=dict(workload='config 2: 65,536 pts/GPU, order 6 (28 rows), 2->128^4->1 sigmoid',
+                                points_per_gpu=args.points, rows=R, l2='inputs larger than L2 (1 GB per layer)',
+                                parallelism=f'dp{world}'),
+                    e2e=dict(value=world * args.points * R / (e2e_ms / 1000), unit=UNIT,
+                             h2d_bytes_per_step=int(pinned_x.numel() * 4 + pinned_t.numel() * 4),
+                             d2h_bytes_per_step=int(params * 4 + 8), timer='host wall clock'),
+                    gpu_launches=int(launches), roofline=roofline, clocks=clock,
+                    kernels={k: dict(launches=v[0] // args.steps, ms_per_step=v[1] / args.steps)
+                             for k, v in sorted(kernels.items())},
+                    gemm_gflop_per_step=(fwd + dgrad + wgrad) / 1e9, loss=loss)
+        if world == 1 and not args.no_cpu_baseline:
+            line['cpu_baseline'] = cpu_baseline()
+        print(json.dumps(line))
+    engine.close()
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+def main():
+    p = argparse.ArgumentParser()
+    p.add_argument('--gpus', type=int, default=1)
+    p.add_argument('--steps', type=int, default=20)
+    p.add_argument('--warmup', type=int, default=3)
+    p.add_argument('--impl', default='b200', choices=['b200', 'reference'])
+    p.add_argument('--points', type=int, default=POINTS)
+    p.add_argument('--reference-points', type=int, default=128)
+    p.add_argument('--no-cpu-baseline', action='store_true')
+    args = p.parse_args()
+    if args.impl == 'reference':
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == '__main__':
+    main()

@@ -1,0 +1,1324 @@
+// Engine implementation: object commands, chunked passes, epochs, cost graphs.
+//
+// Command semantics (validation order and messages, pass ordering, reporting)
+// follow the reference server cuda/cpde_server.cu; each function cites the
+// lines it mirrors. Storage, kernels and reductions are this engine's own.
+#include <algorithm>
+#include <cfloat>
+#include <chrono>
+#include <cmath>
+#include <numeric>
+
+#include "engine.hpp"
+
+namespace cpde {
+
+// ---------------------------------------------------------------------------
+// kernel timing
+
+struct KernelTimer {
+    struct Mark {
+        const char* name;
+        cudaEvent_t start, stop;
+    };
+    std::vector<Mark> marks;
+    std::vector<cudaEvent_t> pool;
+    cudaEvent_t get() {
+        if (!pool.empty()) {
+            auto e = pool.back();
+            pool.pop_back();
+            return e;
+        }
+        cudaEvent_t e;
+        CPDE_CUDA(cudaEventCreate(&e));
+        return e;
+    }
+    struct Totals {
+        long launches = 0;
+        double ms = 0;
+    };
+    std::map<std::string, Totals> totals;
+    void collect() {
+        for (auto& m : marks) {
+            CPDE_CUDA(cudaEventSynchronize(m.stop));
+            float ms = 0;
+            CPDE_CUDA(cudaEventElapsedTime(&ms, m.start, m.stop));
+            auto& t = totals[m.name];
+            t.launches += 1;
+            t.ms += ms;
+            pool.push_back(m.start);
+            pool.push_back(m.stop);
+        }
+        marks.clear();
+    }
+    ~KernelTimer() {
+        for (auto& m : marks) {
+            cudaEventDestroy(m.start);
+            cudaEventDestroy(m.stop);
+        }
+        for (auto e : pool) cudaEventDestroy(e);
+    }
+};
+
+#define CPDE_RUN(engine, name, ...)                                           \
+    do {                                                                      \
+        KernelTimer* t_ = (engine).timer.get();                               \
+        cudaEvent_t a_ = nullptr, b_ = nullptr;                               \
+        if (t_) {                                                             \
+            a_ = t_->get();                                                   \
+            b_ = t_->get();                                                   \
+            CPDE_CUDA(cudaEventRecord(a_, (engine).stream));                  \
+        }                                                                     \
+        __VA_ARGS__;                                                          \
+        CPDE_LAUNCHED();                                                      \
+        if (t_) {                                                             \
+            CPDE_CUDA(cudaEventRecord(b_, (engine).stream));                  \
+            t_->marks.push_back({name, a_, b_});                              \
+        }                                                                     \
+    } while (0)
+
+void Engine::timing(bool enable) {
+    if (enable && !timer) timer.reset(new KernelTimer);
+    if (!enable) timer.reset();
+}
+
+std::string Engine::timing_report() {
+    std::string out;
+    if (!timer) return out;
+    timer->collect();
+    for (auto& kv : timer->totals)
+        out += kv.first + " " + std::to_string(kv.second.launches) + " " + std::to_string(kv.second.ms) + "\n";
+    timer->totals.clear();
+    return out;
+}
+
+static int grid_for(long count, int threads = 256, int cap = 148 * 16) {
+    long g = (count + threads - 1) / threads;
+    return int(std::max(1L, std::min<long>(g, cap)));
+}
+
+// ---------------------------------------------------------------------------
+// construction and lookup
+
+Engine::Engine(int dev) : device(dev) {
+    int count = 0;
+    CPDE_CUDA(cudaGetDeviceCount(&count));
+    require(dev >= 0 && dev < count, "invalid CUDA device");
+    CPDE_CUDA(cudaSetDevice(device));
+    CPDE_CUDA(cudaFree(nullptr));  // create the primary context
+    CPDE_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+}
+
+Engine::~Engine() {
+    cudaSetDevice(device);
+    if (stream) cudaStreamSynchronize(stream);
+    costs.clear();
+    nets.clear();
+    data.clear();
+    programs.clear();
+    contexts.clear();
+    timer.reset();
+    if (stream) cudaStreamDestroy(stream);
+}
+
+template <class M>
+static typename M::mapped_type::element_type& lookup(M& m, uint64_t id) {
+    auto p = m.find(id);
+    require(p != m.end(), "unknown or released object handle");
+    return *p->second;
+}
+DataRecord& Engine::dat(uint64_t id) { return lookup(data, id); }
+NetRecord& Engine::net(uint64_t id) { return lookup(nets, id); }
+CostRecord& Engine::cost(uint64_t id) { return lookup(costs, id); }
+
+// ---------------------------------------------------------------------------
+// data (cuda/cpde_server.cu:449-454, 475-476)
+
+uint64_t Engine::create_data(int d, int h, int w, int v, const int* table, size_t table_count, const float* values,
+                             size_t count) {
+    checked_size(d, h, w);
+    require(v > 0 && v <= 26, "invalid variable count");
+    require(table_count == size_t(d) * (v + 1) && count == size_t(d) * h * w, "data shape mismatch");
+    auto rec = std::unique_ptr<DataRecord>(new DataRecord);
+    rec->d = d;
+    rec->h = h;
+    rec->w = w;
+    rec->v = v;
+    rec->table.assign(table, table + table_count);
+    rec->values.upload(values, count, stream);
+    CPDE_CUDA(cudaStreamSynchronize(stream));
+    uint64_t id = next_id++;
+    data[id] = std::move(rec);
+    return id;
+}
+
+void Engine::replace_data(uint64_t id, const float* values, size_t count) {
+    auto& d = dat(id);
+    require(count == d.values.count, "replacement data shape mismatch");
+    CPDE_CUDA(cudaMemcpyAsync(d.values.ptr, values, count * sizeof(float), cudaMemcpyHostToDevice, stream));
+    CPDE_CUDA(cudaStreamSynchronize(stream));
+    ++d.version;
+}
+
+// ---------------------------------------------------------------------------
+// schema contexts (cuda/cpde_server.cu:109-127)
+
+std::vector<int> Engine::all_rows(DataRecord& d) {
+    std::vector<int> rows(d.d);
+    std::iota(rows.begin(), rows.end(), 0);
+    std::stable_sort(rows.begin(), rows.end(), [&](int a, int b) { return d.order(a) < d.order(b); });
+    return rows;
+}
+
+std::shared_ptr<Context> Engine::make_context(DataRecord& d, const std::vector<int>& rows, bool need_plan) {
+    require(!rows.empty(), "empty derivative closure");
+    int previous = -1;
+    std::string key = std::to_string(d.v) + ":";
+    for (int src : rows) {
+        require(src >= 0 && src < d.d, "invalid derivative row");
+        int order = d.order(src);
+        require(order >= previous && order <= 6, "derivative closure must be sorted, orders 0..6");
+        previous = order;
+        for (int x : d.counts(src)) key.push_back(char('0' + x));
+        key.push_back(',');
+    }
+    require(d.order(rows[0]) == 0, "value derivative must come first");
+    std::string full = key + "|" + std::to_string(need_plan);
+    // The context caches the copy-in row map too, so it is keyed by the data
+    // rows themselves, not only by their multi-indices.
+    for (int src : rows) full += std::to_string(src) + ";";
+    auto it = contexts.find(full);
+    if (it != contexts.end()) return it->second;
+    auto ctx = std::make_shared<Context>();
+    ctx->rows = rows;
+    ctx->rows_dev.upload(rows, stream);
+    if (need_plan) {
+        std::vector<std::vector<int>> counts;
+        for (int src : rows) counts.push_back(d.counts(src));
+        ctx->plan = JetPlan::build(counts);
+        ctx->tables.upload(ctx->plan.pack(), stream);
+        ctx->planned = true;
+    }
+    CPDE_CUDA(cudaStreamSynchronize(stream));
+    contexts[full] = ctx;
+    return ctx;
+}
+
+// ---------------------------------------------------------------------------
+// networks (cuda/cpde_server.cu:455-473; storage of cuda/cpde_engine.cuh:562-659)
+
+uint64_t Engine::create_net(const std::vector<int>& ns, const std::vector<int>& ls,
+                            const std::vector<std::vector<float>>& initial) {
+    require(ns.size() >= 2 && ns.size() <= 256 && ns.size() == ls.size(), "invalid architecture");
+    for (size_t i = 0; i < ns.size(); ++i) require(ns[i] > 0 && ls[i] >= 0 && ls[i] <= 2, "invalid layer");
+    require(ls.front() == 1 && ls.back() == 1, "input and output layers must be linear");
+    require(!initial.empty(), "initial weights required; update the Python wrapper");
+    require(initial.size() == ns.size() - 1, "initial weight shape mismatch");
+    for (size_t i = 1; i < ns.size(); ++i) {
+        checked_size(ns[i], ns[i - 1] + 1);
+        require(initial[i - 1].size() == size_t(ns[i]) * (size_t(ns[i - 1]) + 1), "initial weight shape mismatch");
+        for (float x : initial[i - 1]) require(std::isfinite(x), "nonfinite initial weight");
+    }
+    auto r = std::unique_ptr<NetRecord>(new NetRecord);
+    NetRecord& n = *r;
+    n.neurons = ns;
+    n.linear = ls;
+    n.layers = int(ns.size()) - 1;
+    long off = 0;
+    for (int l = 0; l < n.layers; ++l) {
+        n.offset.push_back(off);
+        n.count.push_back(ns[l + 1] * (ns[l] + 1));
+        off += n.count.back();
+    }
+    n.params = off;
+    for (auto& b : n.bank) b.resize(n.params);
+    std::vector<float> flat;
+    flat.reserve(n.params);
+    for (auto& a : initial) flat.insert(flat.end(), a.begin(), a.end());
+    CPDE_CUDA(cudaMemcpyAsync(n.bank[0].ptr, flat.data(), flat.size() * 4, cudaMemcpyHostToDevice, stream));
+    CPDE_CUDA(cudaMemsetAsync(n.bank[1].ptr, 0, n.params * 4, stream));
+    CPDE_CUDA(cudaMemsetAsync(n.bank[2].ptr, 0, n.params * 4, stream));
+    CPDE_RUN(*this, "fill", k_fill<<<grid_for(n.params), 256, 0, stream>>>(n.bank[3].ptr, n.params, .002f));
+    n.active.assign(n.layers, 1);
+    n.act.resize(n.layers + 1);
+    n.pre.resize(n.layers + 1);
+    std::vector<OptLayer> opt;
+    for (int l = 0; l < n.layers; ++l) opt.push_back({n.offset[l], n.count[l], 1});
+    n.opt_layers.upload(opt, stream);
+    n.grad_counts.upload(n.count, stream);
+    n.grad_ptrs.resize(n.layers);
+    CPDE_CUDA(cudaStreamSynchronize(stream));
+    uint64_t id = next_id++;
+    nets[id] = std::move(r);
+    return id;
+}
+
+static bool nonlinear_net(const NetRecord& n) {
+    for (int x : n.linear)
+        if (x != 1) return true;
+    return false;
+}
+
+void Engine::ensure_arena(NetRecord& n, long columns, bool backward) {
+    const int widest = *std::max_element(n.neurons.begin(), n.neurons.end());
+    if (columns > n.capacity) {
+        CPDE_CUDA(cudaStreamSynchronize(stream));
+        for (int l = 0; l <= n.layers; ++l) {
+            n.act[l].resize(size_t(n.neurons[l]) * columns);
+            if (n.linear[l] != 1) n.pre[l].resize(size_t(n.neurons[l]) * columns);
+        }
+        n.jet_scratch.resize(size_t(widest) * columns);
+        n.dz[0].release();
+        n.dz[1].release();
+        n.dy.release();
+        n.capacity = columns;
+        n.loaded_id = 0;
+    }
+    if (backward && n.dz[0].count < size_t(widest) * n.capacity) {
+        n.dz[0].resize(size_t(widest) * n.capacity);
+        n.dz[1].resize(size_t(widest) * n.capacity);
+        n.dy.resize(size_t(widest) * n.capacity);
+    }
+}
+
+void Engine::ensure_reductions(NetRecord& n, int count) {
+    if (!n.cost_partials.ptr) {
+        n.cost_partials.resize(1024);
+        n.cost_ticket.resize(1);
+        CPDE_CUDA(cudaMemsetAsync(n.cost_ticket.ptr, 0, sizeof(unsigned), stream));
+        n.grad_partials.resize(size_t(n.layers) * 256);
+        n.grad_tickets.resize(n.layers);
+        CPDE_CUDA(cudaMemsetAsync(n.grad_tickets.ptr, 0, n.layers * sizeof(unsigned), stream));
+        n.grad_totals.resize(n.layers);
+        n.host_grads.reserve(n.layers);
+    }
+    if (count > n.cost_capacity) {
+        n.cost_totals.resize(count);
+        n.host_costs.reserve(count);
+        n.cost_capacity = count;
+    }
+}
+
+void Engine::begin_costs(NetRecord& n, int count) {
+    CPDE_RUN(*this, "clear_costs", k_clear_costs<<<1, 256, 0, stream>>>(n.cost_totals.ptr, count));
+}
+
+// ---------------------------------------------------------------------------
+// chunk forward/backward (network::feedforward/backprop,
+// cuda/cpde_engine.cuh:889-991, with the jet combine of
+// cuda/derivative_kernels_v4.cu:349-745 replaced by the Leibniz tables)
+
+void Engine::activate(NetRecord& n, uint64_t data_id, Context& ctx, int width, int offset, int valid) {
+    auto& record = dat(data_id);
+    if (n.loaded_id == data_id && n.loaded_version == record.version && n.loaded_width == width &&
+        n.loaded_offset == offset && n.loaded_valid == valid && n.loaded_rows == ctx.rows)
+        return;
+    n.loaded_id = data_id;
+    n.loaded_version = record.version;
+    n.loaded_width = width;
+    n.loaded_offset = offset;
+    n.loaded_valid = valid;
+    n.loaded_rows = ctx.rows;
+    long total = long(valid) * ctx.R() * record.h;
+    CPDE_RUN(*this, "stage_input",
+             k_stage_input<<<grid_for(total), 256, 0, stream>>>(record.values.ptr, record.h, record.w,
+                                                                 ctx.rows_dev.ptr, ctx.R(), offset, valid,
+                                                                 n.act[0].ptr));
+}
+
+template <bool TA, bool TB, bool BIAS, bool IND>
+static void launch_gemm(Engine& e, int M, int N, int K, const float* A, int lda, const float* B, int ldb, float* C,
+                        int ldc, const float* bias, int R) {
+    dim3 grid((M + gemm::BM - 1) / gemm::BM, (N + gemm::BN - 1) / gemm::BN, 1);
+    CPDE_RUN(e, "gemm", (k_gemm<TA, TB, BIAS, IND><<<grid, gemm::THREADS, 0, e.stream>>>(M, N, K, A, lda, B, ldb, C,
+                                                                                          ldc, bias, R, K)));
+}
+
+void Engine::forward(NetRecord& n, Context& ctx, int points) {
+    const int R = ctx.R();
+    const int cols = points * R;
+    for (int l = 1; l <= n.layers; ++l) {
+        const int np = n.neurons[l - 1], nl = n.neurons[l];
+        const float* W = n.weights(l - 1);
+        const bool nonlin = n.linear[l] != 1;
+        float* Z = nonlin ? n.pre[l].ptr : n.act[l].ptr;
+        launch_gemm<false, false, true, false>(*this, nl, cols, np, W, nl, n.act[l - 1].ptr, np, Z, nl,
+                                               W + long(nl) * np, R);
+        if (!nonlin) continue;
+        long total = long(nl) * points;
+        if (n.linear[l] == kSigmoid)
+            CPDE_RUN(*this, "jet_forward",
+                     k_jet_forward_dyn<Sigmoid><<<grid_for(total), 256, 0, stream>>>(
+                         Z, n.act[l].ptr, n.jet_scratch.ptr, nl, points, R, ctx.tables.ptr));
+        else
+            CPDE_RUN(*this, "jet_forward",
+                     k_jet_forward_dyn<Tanh><<<grid_for(total), 256, 0, stream>>>(Z, n.act[l].ptr, n.jet_scratch.ptr,
+                                                                                  nl, points, R, ctx.tables.ptr));
+    }
+}
+
+void Engine::backward(NetRecord& n, Context& ctx, int points, float* target) {
+    const int R = ctx.R();
+    const long cols = long(points) * R;
+    float* cur = n.dz[0].ptr;
+    for (int l = n.layers; l >= 1; --l) {
+        const int np = n.neurons[l - 1], nl = n.neurons[l];
+        // weight gradient with the bias column appended: (nl x np+1) += dZ (nl x cols) . [A; 1_value]^T
+        const int M = nl, N = np + 1;
+        long base = long((M + gemm::BM - 1) / gemm::BM) * ((N + gemm::BN - 1) / gemm::BN);
+        long splits = std::max(1L, std::min((2L * 148 + base - 1) / base, (cols + 255) / 256));
+        long per = ((cols + splits - 1) / splits + gemm::BK - 1) / gemm::BK * gemm::BK;
+        splits = (cols + per - 1) / per;
+        n.partial.reserve(size_t(splits) * M * N);
+        dim3 grid((M + gemm::BM - 1) / gemm::BM, (N + gemm::BN - 1) / gemm::BN, unsigned(splits));
+        CPDE_RUN(*this, "gemm_wgrad",
+                 (k_gemm<false, true, false, true><<<grid, gemm::THREADS, 0, stream>>>(
+                     M, N, int(cols), cur, nl, n.act[l - 1].ptr, np, n.partial.ptr, M, nullptr, R, int(per))));
+        CPDE_RUN(*this, "splitk_reduce",
+                 k_splitk_reduce<<<grid_for(long(M) * N), 256, 0, stream>>>(
+                     n.partial.ptr, int(splits), M, N, n.gradient_base(l - 1, target), nl, 1));
+        if (l == 1) break;
+        float* next = cur == n.dz[0].ptr ? n.dz[1].ptr : n.dz[0].ptr;
+        const float* W = n.weights(l - 1);
+        if (n.linear[l - 1] == 1) {
+            launch_gemm<true, false, false, false>(*this, np, int(cols), nl, W, nl, cur, nl, next, np, nullptr, R);
+        } else {
+            launch_gemm<true, false, false, false>(*this, np, int(cols), nl, W, nl, cur, nl, n.dy.ptr, np, nullptr, R);
+            long total = long(np) * points;
+            if (n.linear[l - 1] == kSigmoid)
+                CPDE_RUN(*this, "jet_adjoint",
+                         k_jet_adjoint_dyn<Sigmoid><<<grid_for(total), 256, 0, stream>>>(
+                             n.dy.ptr, n.act[l - 1].ptr, n.jet_scratch.ptr, next, np, points, R, ctx.tables.ptr));
+            else
+                CPDE_RUN(*this, "jet_adjoint",
+                         k_jet_adjoint_dyn<Tanh><<<grid_for(total), 256, 0, stream>>>(
+                             n.dy.ptr, n.act[l - 1].ptr, n.jet_scratch.ptr, next, np, points, R, ctx.tables.ptr));
+        }
+        cur = next;
+    }
+}
+
+void Engine::run_cost(NetRecord& n, CostRecord& c, int cost_index, int points, int offset, bool collect,
+                      bool gradient, const double* multiplier) {
+    const int outputs = n.neurons.back();
+    const int R = c.context ? c.context->R() : 0;
+    const float* y = n.act[n.layers].ptr;
+    float* g = gradient ? n.dz[0].ptr : nullptr;
+    CostReduce red{n.cost_partials.ptr, n.cost_ticket.ptr, n.cost_totals.ptr + cost_index};
+    const int blocks = std::max(1, std::min(1024, (points + kReduceThreads - 1) / kReduceThreads));
+    if (c.kind == 0) {
+        auto& t = dat(c.target_id);
+        CPDE_RUN(*this, "cost_matching",
+                 k_cost_matching<<<blocks, kReduceThreads, 0, stream>>>(y, g, t.values.ptr, t.w, c.target_rows.ptr,
+                                                                        c.weights.ptr, c.weight_samples, outputs, R,
+                                                                        points, offset, collect, gradient, red));
+    } else if (c.kind == 1) {
+        CPDE_RUN(*this, "cost_polynomial",
+                 k_cost_polynomial<<<blocks, kReduceThreads, 0, stream>>>(
+                     y, g, c.terms.ptr, c.coefficients.ptr, c.term_count, c.rhs.ptr, c.weights.ptr, outputs, R,
+                     c.equations, dat(c.input_id).w, points, offset, collect, gradient, red));
+    } else {
+        c.program->compile();
+        int RO = R * outputs, samples = c.samples, col = collect, grad = gradient;
+        const double* fields = c.fields.ptr;
+        const double* weights = c.quadrature_weights.ptr;
+        float* gp = g ? g : n.dz[0].ptr;
+        if (!gp) gp = n.act[n.layers].ptr;  // never written when gradient == 0
+        void* args[] = {(void*)&y,       (void*)&gp,      (void*)&fields, (void*)&weights, &RO,
+                        &samples,        &points,         &offset,        (void*)&multiplier, &col,
+                        &grad,           (void*)&red.partials, (void*)&red.ticket, (void*)&red.total};
+        CPDE_RUN(*this, "cost_integral",
+                 driver_check(driver_api().launch(c.program->kernel, blocks, 1, 1, kReduceThreads, 1, 1, 0, stream, args,
+                                             nullptr),
+                              "cuLaunchKernel"));
+    }
+    if (gradient && multiplier && c.kind != 2) {
+        long count = long(points) * R * outputs;
+        CPDE_RUN(*this, "scale", k_scale<<<grid_for(count), 256, 0, stream>>>(g, count, multiplier));
+    }
+}
+
+// One cost over its chunks (Server::pass, cuda/cpde_server.cu:223-257).
+void Engine::pass(NetRecord& n, CostRecord& c, int cost_index, bool bwd, bool collect, const double* multiplier,
+                  int begin, int end, bool reuse_forward, bool backward_storage, float* target) {
+    if (!c.input_id) return;
+    bwd = bwd && c.has_gradient;
+    backward_storage = backward_storage && c.has_gradient;
+    auto& input = dat(c.input_id);
+    end = std::min(end, input.w);
+    require(begin >= 0 && begin % c.width == 0 && (!reuse_forward || long(end) - begin <= c.width),
+            "invalid cost pass range");
+    Context& ctx = *c.context;
+    for (int offset = begin; offset < end; offset += c.width) {
+        int valid = std::min(c.width, input.w - offset);
+        if (reuse_forward) {
+            require(n.loaded_id == c.input_id && n.loaded_version == input.version && n.loaded_width == c.width &&
+                        n.loaded_offset == offset && n.loaded_valid == valid && n.loaded_rows == c.rows,
+                    "forward context is no longer current");
+        } else {
+            activate(n, c.input_id, ctx, c.width, offset, valid);
+            if (c.has_components) forward(n, ctx, valid);
+        }
+        run_cost(n, c, cost_index, valid, offset, collect, bwd, multiplier);
+        if (bwd) backward(n, ctx, valid, target);
+    }
+}
+
+void Engine::prepare_costs(NetRecord& n, const std::vector<uint64_t>& ids, uint64_t ni, bool bwd) {
+    long columns = 1;
+    for (auto id : ids) {
+        auto& c = cost(id);
+        require(c.network_id == ni, "cost belongs to another network");
+        if (c.input_id) columns = std::max(columns, long(c.width) * long(c.rows.size()));
+        if (c.program) c.program->compile();
+    }
+    (void)bwd;
+    ensure_arena(n, columns, true);  // output adjoints are written even by value-only integral passes
+    ensure_reductions(n, int(ids.size()));
+}
+
+// ---------------------------------------------------------------------------
+// evaluation (cuda/cpde_server.cu:171-183)
+
+uint64_t Engine::evaluate(uint64_t ni, uint64_t di, int chunk) {
+    auto& n = net(ni);
+    auto& input = dat(di);
+    require(input.h == n.neurons.front(), "input channel mismatch");
+    int width = chunk ? std::min(chunk, input.w) : input.w;
+    require(width > 0, "invalid chunk size");
+    auto rows = all_rows(input);
+    auto ctx = make_context(input, rows, nonlinear_net(n));
+    ensure_arena(n, long(width) * ctx->R(), false);
+    auto out = std::unique_ptr<DataRecord>(new DataRecord);
+    out->d = input.d;
+    out->h = n.neurons.back();
+    out->w = input.w;
+    out->v = input.v;
+    out->table = input.table;
+    out->values.resize(size_t(out->d) * out->h * out->w);
+    for (int offset = 0; offset < input.w; offset += width) {
+        int valid = std::min(width, input.w - offset);
+        activate(n, di, *ctx, width, offset, valid);
+        forward(n, *ctx, valid);
+        long total = long(valid) * ctx->R() * out->h;
+        CPDE_RUN(*this, "scatter_output",
+                 k_scatter_output<<<grid_for(total), 256, 0, stream>>>(n.act[n.layers].ptr, out->h, ctx->R(),
+                                                                        ctx->rows_dev.ptr, offset, valid, out->w,
+                                                                        out->values.ptr));
+    }
+    CPDE_CUDA(cudaStreamSynchronize(stream));
+    uint64_t id = next_id++;
+    data[id] = std::move(out);
+    return id;
+}
+
+// ---------------------------------------------------------------------------
+// costs (cuda/cpde_server.cu:477-482, 489-533)
+
+uint64_t Engine::cost_matching(uint64_t ni, uint64_t in, uint64_t tgt, int chunk, std::vector<int> rows,
+                               std::vector<int> tr, int ws, std::vector<float> w) {
+    auto c = std::unique_ptr<CostRecord>(new CostRecord);
+    c->network_id = ni;
+    c->input_id = in;
+    c->target_id = tgt;
+    c->kind = 0;
+    c->rows = rows;
+    auto& n = net(ni);
+    auto& d = dat(in);
+    require(d.h == n.neurons.front(), "input channel mismatch");
+    c->width = chunk ? std::min(chunk, d.w) : d.w;
+    require(c->width > 0, "invalid chunk size");
+    c->context = make_context(d, rows, nonlinear_net(n));
+    auto& t = dat(tgt);
+    require(t.h == n.neurons.back() && t.w == d.w, "target shape mismatch");
+    c->weight_samples = ws;
+    require(tr.size() == rows.size() && (ws == 1 || ws == d.w) && w.size() == rows.size() * size_t(ws) * t.h,
+            "matching weight shape mismatch");
+    for (int r : tr) require(r >= 0 && r < t.d, "target derivative mismatch");
+    for (float x : w) require(std::isfinite(x) && x >= 0, "invalid matching weight");
+    c->target_rows.upload(tr, stream);
+    c->weights.upload(w, stream);
+    CPDE_CUDA(cudaStreamSynchronize(stream));
+    uint64_t id = next_id++;
+    costs[id] = std::move(c);
+    return id;
+}
+
+uint64_t Engine::cost_polynomial(uint64_t ni, uint64_t in, int chunk, std::vector<int> rows, int equations,
+                                 std::vector<int> raw, std::vector<float> co, std::vector<float> rhs,
+                                 std::vector<float> w) {
+    auto c = std::unique_ptr<CostRecord>(new CostRecord);
+    c->network_id = ni;
+    c->input_id = in;
+    c->kind = 1;
+    c->rows = rows;
+    auto& n = net(ni);
+    auto& d = dat(in);
+    require(d.h == n.neurons.front(), "input channel mismatch");
+    c->width = chunk ? std::min(chunk, d.w) : d.w;
+    require(c->width > 0, "invalid chunk size");
+    c->context = make_context(d, rows, nonlinear_net(n));
+    c->equations = equations;
+    require(equations > 0 && raw.size() % 3 == 0 && co.size() == raw.size() / 3 * size_t(d.w) &&
+                rhs.size() == size_t(equations) * d.w && w.size() == rhs.size(),
+            "equation data shape mismatch");
+    const long limit = long(rows.size()) * n.neurons.back();
+    std::vector<PolyTerm> terms;
+    for (size_t i = 0; i < raw.size(); i += 3) {
+        require(raw[i] >= 0 && raw[i] < equations && raw[i + 1] >= 0 && raw[i + 1] < limit && raw[i + 2] >= -1 &&
+                    raw[i + 2] < limit,
+                "invalid polynomial term");
+        terms.push_back({raw[i], raw[i + 1], raw[i + 2]});
+    }
+    for (float x : w) require(std::isfinite(x) && x >= 0, "invalid equation weight");
+    for (float x : co) require(std::isfinite(x), "invalid coefficient");
+    for (float x : rhs) require(std::isfinite(x), "invalid right-hand side");
+    c->term_count = int(terms.size());
+    c->terms.upload(terms, stream);
+    c->coefficients.upload(co, stream);
+    c->rhs.upload(rhs, stream);
+    c->weights.upload(w, stream);
+    CPDE_CUDA(cudaStreamSynchronize(stream));
+    uint64_t id = next_id++;
+    costs[id] = std::move(c);
+    return id;
+}
+
+uint64_t Engine::cost_integral(uint64_t ni, uint64_t in, int chunk, int samples, std::vector<int> raw,
+                               std::vector<double> constants, int fields, std::vector<double> numeric,
+                               std::vector<double> weights) {
+    auto c = std::unique_ptr<CostRecord>(new CostRecord);
+    c->kind = 2;
+    c->network_id = ni;
+    c->input_id = in;
+    c->samples = samples;
+    auto& n = net(ni);
+    const int outputs = n.neurons.back();
+    require(samples >= 0 && chunk >= 0 && fields >= 0 && fields <= 512 && weights.size() == size_t(samples) &&
+                numeric.size() == size_t(fields) * samples,
+            "invalid integral field shape");
+    require(!constants.empty() && constants.size() <= 512 && raw.size() == constants.size() * 3,
+            "invalid expression IR size");
+    if (samples) {
+        auto& d = dat(in);
+        require(d.h == n.neurons.front() && d.w == samples, "integral input shape mismatch");
+        std::vector<int> requested;
+        for (size_t i = 0; i < constants.size(); ++i)
+            if (raw[3 * i] == 1) {
+                int component = raw[3 * i + 1];
+                require(component >= 0 && long(component) < long(d.d) * outputs, "component outside derivative schema");
+                requested.push_back(component / outputs);
+            }
+        for (int row : all_rows(d)) {
+            bool needed = d.order(row) == 0;
+            for (int target : requested) {
+                bool dependency = true;
+                auto a = d.counts(row), b = d.counts(target);
+                for (size_t v = 0; v < a.size(); ++v)
+                    if (a[v] > b[v]) {
+                        dependency = false;
+                        break;
+                    }
+                needed = needed || dependency;
+            }
+            if (needed) c->rows.push_back(row);
+        }
+        c->context = make_context(d, c->rows, nonlinear_net(n));
+        c->width = chunk ? std::min(chunk, d.w) : d.w;
+    } else {
+        require(!in, "empty integral must not have input data");
+        c->width = 0;
+    }
+    std::vector<ScalarNode> ir;
+    for (int i = 0; i < int(constants.size()); ++i) {
+        int op = raw[3 * i], a = raw[3 * i + 1], mask = raw[3 * i + 2];
+        require(op >= 0 && op <= 14 && std::isfinite(constants[i]), "invalid expression node");
+        if (op == 1) {
+            require(a >= 0 && (mask == 0 || mask == 1), "invalid component");
+            if (samples) {
+                auto row = std::find(c->rows.begin(), c->rows.end(), a / outputs);
+                require(row != c->rows.end(), "component outside derivative closure");
+                a = int(row - c->rows.begin()) * outputs + a % outputs;
+            }
+        }
+        if (op == 2) require(a >= 0 && a < fields, "invalid field index");
+        if (op >= 3) {
+            require(a >= 0 && a < i, "invalid expression dependency");
+            if (op <= 6) require(mask >= 0 && mask < i, "invalid expression dependency");
+        }
+        ir.push_back({op, a, mask, constants[i]});
+    }
+    for (double x : numeric) require(std::isfinite(x), "nonfinite integral field");
+    for (double x : weights) require(std::isfinite(x), "nonfinite quadrature weight");
+    c->has_components = false;
+    c->has_gradient = false;
+    for (const auto& node : ir)
+        if (node.op == 1) {
+            c->has_components = true;
+            if (node.b == 0) c->has_gradient = true;
+        }
+    auto source = expression_source(ir);
+    auto found = programs.find(source);
+    if (found == programs.end())
+        found = programs.emplace(source, std::make_shared<ExpressionProgram>(std::move(ir))).first;
+    c->program = found->second;
+    c->fields.upload(numeric, stream);
+    c->quadrature_weights.upload(weights, stream);
+    CPDE_CUDA(cudaStreamSynchronize(stream));
+    uint64_t id = next_id++;
+    costs[id] = std::move(c);
+    return id;
+}
+
+void Engine::release(int kind, uint64_t id) {
+    if (kind == 0) {
+        for (auto& c : costs)
+            require(c.second->input_id != id && c.second->target_id != id,
+                    "data is retained by a cost; close that cost first");
+        data.erase(id);
+    } else if (kind == 1) {
+        for (auto& c : costs)
+            require(c.second->network_id != id, "network is retained by a cost; close that cost first");
+        nets.erase(id);
+    } else if (kind == 2) {
+        costs.erase(id);
+    } else {
+        require(false, "invalid object kind");
+    }
+}
+
+// ---------------------------------------------------------------------------
+// optimizer state (cuda/cpde_server.cu:184-222; cuda/cpde_engine.cuh:916-945,993-1014)
+
+void Engine::reset_optimizer(NetRecord& n, int method) {
+    CPDE_CUDA(cudaStreamSynchronize(stream));
+    for (int l = 0; l < n.layers; ++l) n.active[l] = 1;
+    for (int b = 1; b < 4; ++b) CPDE_CUDA(cudaMemsetAsync(n.bank[b].ptr, 0, n.params * 4, stream));
+    if (method == 0) set_steps(n, n.initial_step);
+    n.optimizer = method;
+    n.adam_step = 0;
+}
+
+static std::vector<OptLayer> opt_table(NetRecord& n) {
+    std::vector<OptLayer> t;
+    for (int l = 0; l < n.layers; ++l) t.push_back({n.offset[l], n.count[l], n.active[l]});
+    return t;
+}
+
+void Engine::set_steps(NetRecord& n, float value) {
+    CPDE_RUN(*this, "fill", k_fill<<<grid_for(n.params), 256, 0, stream>>>(n.bank[3].ptr, n.params, value));
+    CPDE_CUDA(cudaMemsetAsync(n.bank[1].ptr, 0, n.params * 4, stream));
+    CPDE_CUDA(cudaMemsetAsync(n.bank[2].ptr, 0, n.params * 4, stream));
+}
+
+void Engine::floor_steps(NetRecord& n, float value) {
+    int widest = *std::max_element(n.count.begin(), n.count.end());
+    dim3 grid(grid_for(widest, 256, 256), n.layers);
+    CPDE_RUN(*this, "rprop_floor",
+             k_rprop_floor<<<grid, 256, 0, stream>>>(n.bank[1].ptr, n.bank[2].ptr, n.bank[3].ptr, n.opt_layers.ptr,
+                                                      value));
+}
+
+void Engine::optimizer_step(NetRecord& n, int method) {
+    n.opt_layers.upload(opt_table(n), stream);
+    int widest = *std::max_element(n.count.begin(), n.count.end());
+    dim3 grid(grid_for(widest, 256, 256), n.layers);
+    if (method == 0) {
+        CPDE_RUN(*this, "rprop",
+                 k_rprop<<<grid, 256, 0, stream>>>(n.bank[0].ptr, n.bank[1].ptr, n.bank[2].ptr, n.bank[3].ptr,
+                                                   n.opt_layers.ptr));
+        for (int l = 0; l < n.layers; ++l) n.active[l] = 3 - n.active[l];
+    } else {
+        require(n.adam_step < uint64_t(INT_MAX), "Adam counter exceeds supported range");
+        int step = int(++n.adam_step);
+        float b1t = std::pow(0.9f, float(step)), b2t = std::pow(0.999f, float(step));
+        CPDE_RUN(*this, "adam",
+                 k_adam<<<grid, 256, 0, stream>>>(n.bank[0].ptr, n.bank[1].ptr, n.bank[2].ptr, n.bank[3].ptr,
+                                                  n.opt_layers.ptr, n.learning_rate, 0.9f, 0.999f, b1t, b2t));
+    }
+}
+
+Payload Engine::metadata(NetRecord& n) {
+    Payload b;
+    b.put<uint32_t>(1);
+    b.put_array(n.neurons);
+    b.put_array(n.linear);
+    b.put<int32_t>(n.optimizer);
+    b.put<uint64_t>(n.updates);
+    b.put<uint64_t>(n.adam_step);
+    b.put<uint64_t>(n.stage_done);
+    b.put<uint64_t>(n.remaining);
+    b.put<float>(n.learning_rate);
+    b.put<float>(n.initial_step);
+    b.put_string(n.stage);
+    return b;
+}
+
+Payload Engine::snapshot(NetRecord& n) {
+    CPDE_CUDA(cudaStreamSynchronize(stream));
+    Payload b = metadata(n);
+    std::vector<float> host(n.params);
+    std::vector<std::vector<float>> banks(4, std::vector<float>(n.params));
+    for (int j = 0; j < 4; ++j)
+        CPDE_CUDA(cudaMemcpy(banks[j].data(), n.bank[j].ptr, n.params * 4, cudaMemcpyDeviceToHost));
+    for (int l = 0; l < n.layers; ++l) {
+        b.put<int32_t>(n.active[l]);
+        for (int j = 0; j < 4; ++j) b.put_array(banks[j].data() + n.offset[l], size_t(n.count[l]));
+    }
+    return b;
+}
+
+void Engine::restore(NetRecord& n, Payload& b) {
+    require(b.get<uint32_t>() == 1, "unsupported state version");
+    require(b.array<int>() == n.neurons && b.array<int>() == n.linear, "state architecture mismatch");
+    int optimizer = b.get<int32_t>();
+    require(optimizer >= -1 && optimizer <= 1, "invalid optimizer state");
+    uint64_t updates = b.get<uint64_t>(), adam = b.get<uint64_t>(), done = b.get<uint64_t>(),
+             remaining = b.get<uint64_t>();
+    float lr = b.get<float>(), step = b.get<float>();
+    auto stage = b.string();
+    require(std::isfinite(lr) && lr > 0 && std::isfinite(step) && step > 0, "invalid optimizer settings");
+    std::vector<int> active;
+    std::vector<std::vector<float>> banks(4, std::vector<float>(n.params));
+    for (int l = 0; l < n.layers; ++l) {
+        int a = b.get<int32_t>();
+        require(a == 1 || a == 2, "invalid active gradient buffer");
+        active.push_back(a);
+        for (int j = 0; j < 4; ++j) {
+            auto v = b.array<float>();
+            require(v.size() == size_t(n.count[l]), "state buffer shape mismatch");
+            std::copy(v.begin(), v.end(), banks[j].begin() + n.offset[l]);
+        }
+    }
+    b.end();
+    CPDE_CUDA(cudaStreamSynchronize(stream));
+    n.active = active;
+    for (int j = 0; j < 4; ++j)
+        CPDE_CUDA(cudaMemcpy(n.bank[j].ptr, banks[j].data(), n.params * 4, cudaMemcpyHostToDevice));
+    n.optimizer = optimizer;
+    n.updates = updates;
+    n.adam_step = adam;
+    n.stage_done = done;
+    n.remaining = remaining;
+    n.learning_rate = lr;
+    n.initial_step = step;
+    n.stage = stage;
+}
+
+// ---------------------------------------------------------------------------
+// reductions and validation (cuda/cpde_server.cu:323-352; cuda/reduction_kernels.cuh:252-267)
+
+void Engine::inspect_gradients(NetRecord& n, float* target) {
+    std::vector<const float*> ptrs;
+    for (int l = 0; l < n.layers; ++l) ptrs.push_back(n.gradient_base(l, target));
+    n.grad_ptrs.upload(ptrs, stream);
+    int widest = *std::max_element(n.count.begin(), n.count.end());
+    dim3 grid(grid_for(widest, 256, 256), n.layers);
+    GradReduce red{n.grad_partials.ptr, n.grad_tickets.ptr, n.grad_totals.ptr};
+    std::vector<GradStats> empty(n.layers, grad_empty());
+    CPDE_CUDA(cudaMemcpyAsync(n.grad_totals.ptr, empty.data(), n.layers * sizeof(GradStats), cudaMemcpyHostToDevice,
+                              stream));
+    CPDE_RUN(*this, "inspect_gradients",
+             k_inspect_gradients<<<grid, 256, 0, stream>>>(n.grad_ptrs.ptr, n.grad_counts.ptr, red));
+    CPDE_CUDA(cudaStreamSynchronize(stream));  // keeps `empty` alive until the copy completes
+}
+
+void Engine::download(NetRecord& n, int count, int layers) {
+    if (count)
+        CPDE_CUDA(cudaMemcpyAsync(n.host_costs.ptr, n.cost_totals.ptr, count * sizeof(CostStats),
+                                  cudaMemcpyDeviceToHost, stream));
+    if (layers)
+        CPDE_CUDA(cudaMemcpyAsync(n.host_grads.ptr, n.grad_totals.ptr, layers * sizeof(GradStats),
+                                  cudaMemcpyDeviceToHost, stream));
+    CPDE_CUDA(cudaStreamSynchronize(stream));
+}
+
+void Engine::validate_costs(NetRecord& n, size_t count, std::vector<double>& values, bool before_update) {
+    const std::string phase = before_update ? "; no optimizer update performed for this iteration"
+                                            : " during objective evaluation";
+    for (size_t i = 0; i < count; ++i) {
+        const auto& c = n.host_costs.ptr[i];
+        values[i] = c.value;
+        if (c.bad_sample != INT_MAX) {
+            std::string what = c.bad_component < 0 ? "objective" : "dE/dY component " + std::to_string(c.bad_component);
+            throw RequestError("non-finite " + what + " at cost index " + std::to_string(i) + ", sample " +
+                               std::to_string(c.bad_sample) + phase);
+        }
+        if (!std::isfinite(c.value)) throw RequestError("non-finite reduced objective" + phase);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// cost graphs (cuda/cpde_server.cu:38-70, cuda/cost_graph.cuh:6-27,
+// cuda/graph_schedule.hpp:18-55)
+
+__global__ void k_graph_execute(const ScalarNode* nodes, int count, int root, const CostStats* integrals, int leaves,
+                                double* values, double* adjoints, double* multipliers, int* active,
+                                GraphRecord::Summary* summary, int gradient) {
+    if (blockIdx.x || threadIdx.x) return;
+    int bad = -1;
+    for (int i = 0; i < leaves; ++i) multipliers[i] = 0;
+    for (int i = 0; i < count; ++i) {
+        ScalarNode n = nodes[i];
+        adjoints[i] = 0;
+        active[i] = n.op == kLeaf;
+        if (n.op == kLeaf) {
+            values[i] = integrals[n.a].value;
+        } else {
+            values[i] = scalar_value(n.op, n.a < 0 ? 0 : values[n.a], n.b < 0 ? 0 : values[n.b], n.parameter);
+            if (n.op > kField)
+                active[i] = active[n.a] || ((n.op <= kDiv || n.op == kAttach) && active[n.b]);
+        }
+        if (!isfinite(values[i]) && bad < 0) bad = i;
+    }
+    summary->value = values[root];
+    summary->bad_node = bad;
+    if (!gradient || bad >= 0) return;
+    adjoints[root] = 1;
+    for (int i = count - 1; i >= 0; --i) {
+        ScalarNode n = nodes[i];
+        double seed = adjoints[i];
+        if (seed == 0 || !active[i]) continue;
+        if (n.op == kLeaf) {
+            multipliers[n.a] += seed;
+        } else if (n.op > kField) {
+            double da, db;
+            scalar_partials(n.op, values[n.a], n.b < 0 ? 0 : values[n.b], values[i], n.parameter, da, db);
+            if (active[n.a]) adjoints[n.a] += seed * da;
+            if ((n.op <= kDiv || n.op == kAttach) && active[n.b]) adjoints[n.b] += seed * db;
+        }
+        if (!isfinite(seed) && bad < 0) bad = i;
+    }
+    for (int i = 0; i < leaves; ++i)
+        if (!isfinite(multipliers[i])) bad = root;
+    summary->bad_node = bad;
+}
+
+// Which leaf multipliers are known before any integral is evaluated.
+static std::vector<GraphRecord::Known> graph_schedule(const std::vector<ScalarNode>& nodes, int root, int leaves) {
+    using K = GraphRecord::Known;
+    auto known = [](double v) { return K{std::isfinite(v), v}; };
+    const K unknown{false, 0};
+    auto sum = [&](K a, K b) { return a.known && b.known ? known(a.value + b.value) : unknown; };
+    auto product = [&](K a, K b) {
+        if ((a.known && a.value == 0) || (b.known && b.value == 0)) return known(0);
+        return a.known && b.known ? known(a.value * b.value) : unknown;
+    };
+    size_t count = nodes.size();
+    std::vector<K> values(count, unknown), da(count, unknown), db(count, unknown);
+    std::vector<bool> active(count, false);
+    for (size_t i = 0; i < count; ++i) {
+        auto n = nodes[i];
+        if (n.op == kConstant) {
+            values[i] = known(n.parameter);
+            continue;
+        }
+        if (n.op == kLeaf) {
+            active[i] = true;
+            continue;
+        }
+        bool binary = n.op <= kDiv || n.op == kAttach;
+        K a = values[n.a], b = binary ? values[n.b] : known(0);
+        active[i] = active[n.a] || (binary && active[n.b]);
+        if (a.known && (b.known || n.op == kAttach)) values[i] = known(scalar_value(n.op, a.value, b.value, n.parameter));
+        if (n.op == kAdd || n.op == kAttach) {
+            da[i] = db[i] = known(1);
+        } else if (n.op == kSub) {
+            da[i] = known(1);
+            db[i] = known(-1);
+        } else if (n.op == kMul) {
+            da[i] = b;
+            db[i] = a;
+        } else if (n.op == kDiv) {
+            if (b.known && b.value != 0) {
+                da[i] = known(1 / b.value);
+                if (a.known) db[i] = known(-(a.value / b.value) / b.value);
+            }
+        } else if (n.op == kNeg) {
+            da[i] = known(-1);
+        } else if (n.op == kPower && (n.parameter == 0 || n.parameter == 1)) {
+            da[i] = known(n.parameter);
+        } else if (a.known && values[i].known) {
+            double x, y;
+            scalar_partials(n.op, a.value, b.value, values[i].value, n.parameter, x, y);
+            da[i] = known(x);
+        }
+    }
+    std::vector<K> adjoints(count, known(0)), multipliers(leaves, known(0));
+    adjoints[root] = known(1);
+    for (int i = int(count) - 1; i >= 0; --i) {
+        auto n = nodes[i];
+        K seed = adjoints[i];
+        if (!active[i] || (seed.known && seed.value == 0)) continue;
+        if (n.op == kLeaf) {
+            multipliers[n.a] = sum(multipliers[n.a], seed);
+        } else {
+            if (active[n.a]) adjoints[n.a] = sum(adjoints[n.a], product(seed, da[i]));
+            if ((n.op <= kDiv || n.op == kAttach) && active[n.b]) adjoints[n.b] = sum(adjoints[n.b], product(seed, db[i]));
+        }
+    }
+    return multipliers;
+}
+
+void Engine::read_graph(GraphRecord& g, Payload& b, int leaves) {
+    auto raw = b.array<int>();
+    auto constants = b.array<double>();
+    g.root = b.get<int>();
+    require(!constants.empty() && constants.size() <= 4096 && raw.size() == 3 * constants.size() && g.root >= 0 &&
+                g.root < int(constants.size()),
+            "invalid cost graph size");
+    for (int i = 0; i < int(constants.size()); ++i) {
+        int op = raw[3 * i], a = raw[3 * i + 1], c = raw[3 * i + 2];
+        require(std::isfinite(constants[i]), "nonfinite graph constant");
+        require(op == 0 || op == 1 || (op >= 3 && op <= 15), "invalid graph opcode");
+        if (op == 1) require(a >= 0 && a < leaves, "invalid graph leaf");
+        if (op >= 3) {
+            require(a >= 0 && a < i, "graph must be topologically ordered");
+            if (op <= 6 || op == 15) require(c >= 0 && c < i, "invalid graph child");
+        }
+        g.nodes.push_back({op, a, c, constants[i]});
+    }
+    size_t count = g.nodes.size();
+    g.nodes_dev.upload(g.nodes, stream);
+    g.values.resize(count);
+    g.adjoints.resize(count);
+    g.active.resize(count);
+    g.multipliers.resize(std::max(1, leaves));
+    g.summary.resize(1);
+    g.host.reserve(1);
+    g.host.ptr[0] = {0, -1, 0};
+    g.schedule = graph_schedule(g.nodes, g.root, leaves);
+    std::vector<double> fixed(std::max(1, leaves), 0.0);
+    for (int i = 0; i < leaves; ++i)
+        if (g.schedule[i].known) fixed[i] = g.schedule[i].value;
+    g.fixed_multipliers.upload(fixed, stream);
+    CPDE_CUDA(cudaStreamSynchronize(stream));
+}
+
+void Engine::run_graph(GraphRecord& g, NetRecord& n, int leaves, bool gradient) {
+    CPDE_RUN(*this, "graph_execute",
+             k_graph_execute<<<1, 1, 0, stream>>>(g.nodes_dev.ptr, int(g.nodes.size()), g.root, n.cost_totals.ptr,
+                                                  leaves, g.values.ptr, g.adjoints.ptr, g.multipliers.ptr,
+                                                  g.active.ptr, g.summary.ptr, gradient));
+}
+
+// Server::graph_pass (cuda/cpde_server.cu:273-318): leaves whose multiplier is
+// known run forward+backward at once; the others contribute values first, the
+// graph runs on device, then they run backward with device multipliers. The
+// most expensive such leaf runs last so its final chunk's forward is reused.
+void Engine::graph_pass(NetRecord& n, const std::vector<uint64_t>& ids, GraphRecord& g, bool bwd, float* target) {
+    begin_costs(n, int(ids.size()));
+    int reuse = -1, last_offset = 0;
+    double best_work = -1;
+    if (bwd) {
+        for (int l = 0; l < n.layers; ++l)
+            CPDE_CUDA(cudaMemsetAsync(n.gradient_base(l, target), 0, n.count[l] * 4, stream));
+        for (size_t i = 0; i < ids.size(); ++i) {
+            if (g.schedule[i].known) continue;
+            auto& c = cost(ids[i]);
+            if (!c.input_id || !c.has_gradient || !c.has_components) continue;
+            auto& d = dat(c.input_id);
+            double derivative_work = 0, work = 0;
+            for (int r : c.rows) derivative_work += std::ldexp(1.0, d.order(r));
+            for (int l = 0; l < n.layers; ++l) {
+                work += 2.0 * n.neurons[l] * n.neurons[l + 1] * c.rows.size();
+                if (n.linear[l] != 1) work += n.neurons[l] * derivative_work;
+            }
+            work *= c.width;
+            if (work > best_work) {
+                best_work = work;
+                reuse = int(i);
+            }
+        }
+    }
+    for (size_t i = 0; i < ids.size(); ++i) {
+        if (int(i) == reuse) continue;
+        bool immediate = bwd && g.schedule[i].known && g.schedule[i].value != 0;
+        pass(n, cost(ids[i]), int(i), immediate, true, immediate ? g.fixed_multipliers.ptr + i : nullptr, 0, INT_MAX,
+             false, bwd, target);
+    }
+    if (reuse >= 0) {
+        auto& c = cost(ids[reuse]);
+        last_offset = ((dat(c.input_id).w - 1) / c.width) * c.width;
+        pass(n, c, reuse, false, true, nullptr, 0, INT_MAX, false, true, target);
+    }
+    run_graph(g, n, int(ids.size()), bwd);
+    if (bwd) {
+        if (reuse >= 0)
+            pass(n, cost(ids[reuse]), reuse, true, false, g.multipliers.ptr + reuse, last_offset, INT_MAX, true, true,
+                 target);
+        for (size_t i = 0; i < ids.size(); ++i)
+            if (!g.schedule[i].known)
+                pass(n, cost(ids[i]), int(i), true, false, g.multipliers.ptr + i, 0,
+                     int(i) == reuse ? last_offset : INT_MAX, false, true, target);
+    }
+    CPDE_CUDA(cudaMemcpyAsync(g.host.ptr, g.summary.ptr, sizeof(GraphRecord::Summary), cudaMemcpyDeviceToHost,
+                              stream));
+}
+
+static void graph_validate(GraphRecord& g) {
+    if (g.host.ptr[0].bad_node >= 0)
+        throw RequestError("invalid value or derivative in cost graph node " + std::to_string(g.host.ptr[0].bad_node));
+}
+
+void Engine::evaluate_costs(NetRecord& n, const std::vector<uint64_t>& ids, std::vector<double>& values,
+                            GraphRecord* g) {
+    if (g) {
+        graph_pass(n, ids, *g, false, nullptr);
+        download(n, int(ids.size()), 0);
+        validate_costs(n, ids.size(), values, false);
+        graph_validate(*g);
+        return;
+    }
+    begin_costs(n, int(ids.size()));
+    for (size_t i = 0; i < ids.size(); ++i)
+        pass(n, cost(ids[i]), int(i), false, true, nullptr, 0, INT_MAX, false, false, nullptr);
+    download(n, int(ids.size()), 0);
+    validate_costs(n, ids.size(), values, false);
+}
+
+void Engine::report_values(NetRecord& n, uint64_t completed, int after, const std::vector<double>& values,
+                           GraphRecord* g, const EventSink& emit) {
+    Payload r;
+    r.put<uint64_t>(completed);
+    r.put<uint64_t>(n.updates);
+    r.put<int32_t>(after);
+    r.put_array(values);
+    if (g) r.put<double>(g->host.ptr[0].value);
+    emit(g ? 6 : 2, r);
+}
+
+void Engine::gradient_report(NetRecord& n, uint64_t epoch, const EventSink& emit) {
+    Payload r;
+    r.put<uint64_t>(epoch);
+    r.put<uint64_t>(n.updates);
+    r.put<int32_t>(n.layers);
+    for (int i = 0; i < n.layers; ++i) {
+        const auto& g = n.host_grads.ptr[i];
+        r.put<double>(g.squared_norm);
+        r.put<double>(g.max_abs);
+        r.put<uint64_t>(g.nonfinite);
+        r.put<int32_t>(g.first_nonfinite == INT_MAX ? -1 : g.first_nonfinite);
+    }
+    emit(5, r);
+}
+
+// ---------------------------------------------------------------------------
+// training (Server::train, cuda/cpde_server.cu:364-435)
+
+void Engine::train(Payload& b, bool graph_mode, const EventSink& emit, const volatile int32_t* stop) {
+    uint64_t ni = b.get<uint64_t>();
+    auto& n = net(ni);
+    auto ids = b.array<uint64_t>();
+    uint64_t epochs = b.get<uint64_t>();
+    int method = b.get<int32_t>(), fresh = b.get<int32_t>();
+    float steps = b.get<float>();
+    int moments = b.get<int32_t>();
+    float lr = b.get<float>();
+    int verbose = b.get<int32_t>(), log = b.get<int32_t>(), eval = b.get<int32_t>(), outputs = b.get<int32_t>(),
+        save = b.get<int32_t>();
+    (void)verbose;
+    auto stage = b.string();
+    int diagnostics = b.get<int32_t>();
+    std::unique_ptr<GraphRecord> graph;
+    if (graph_mode) {
+        graph.reset(new GraphRecord);
+        read_graph(*graph, b, int(ids.size()));
+    }
+    uint64_t restore_every = 0;
+    float restore_step = 0;
+    if (b.more()) {
+        restore_every = b.get<uint64_t>();
+        restore_step = b.get<float>();
+    }
+    b.end();
+    require(!ids.empty() && epochs > 0, "training needs costs and positive epochs");
+    require(method == 0 || method == 1, "unknown optimizer");
+    require(ids.size() <= INT_MAX && log >= 0 && eval >= 0 && save >= 0 && diagnostics >= 0 && std::isfinite(lr) &&
+                lr >= 0 && std::isfinite(steps) && steps >= 0,
+            "invalid training controls");
+    require((restore_every == 0 && restore_step == 0) ||
+                (restore_every > 0 && method == 0 && std::isfinite(restore_step) && restore_step >= FLT_MIN),
+            "invalid periodic RPROP restoration controls");
+    prepare_costs(n, ids, ni, true);
+    if (fresh || n.optimizer != method) reset_optimizer(n, method);
+    if (lr > 0) n.learning_rate = lr;
+    if (steps > 0) {
+        require(method == 0, "reset_steps requires RPROP");
+        set_steps(n, steps);
+    }
+    if (moments) {
+        require(method == 1, "reset_moments requires Adam");
+        reset_optimizer(n, 1);
+    }
+    if (graph) {
+        if (n.stage.substr(0, n.stage.find('|')) != stage.substr(0, stage.find('|'))) n.stage_done = 0;
+        n.stage = stage;
+    } else if (n.stage != stage) {
+        n.stage = stage;
+        n.stage_done = 0;
+    }
+    n.remaining = epochs;
+    std::vector<double> values(ids.size());
+    uint64_t completed = 0, last_saved = UINT64_MAX, last_eval = UINT64_MAX;
+    auto stopped = [&]() { return stop && *stop; };
+    while (completed < epochs && !stopped()) {
+        const bool collect = (log && (completed + 1) % log == 0) || completed + 1 == epochs;
+        if (graph) {
+            graph_pass(n, ids, *graph, true, nullptr);
+        } else {
+            begin_costs(n, int(ids.size()));
+            for (int l = 0; l < n.layers; ++l)
+                CPDE_CUDA(cudaMemsetAsync(n.gradient(l), 0, n.count[l] * 4, stream));
+            for (size_t i = 0; i < ids.size(); ++i)
+                pass(n, cost(ids[i]), int(i), true, collect, nullptr, 0, INT_MAX, false, true, nullptr);
+        }
+        inspect_gradients(n, nullptr);
+        download(n, int(ids.size()), n.layers);
+        bool bad_gradient = false;
+        for (int i = 0; i < n.layers; ++i) bad_gradient = bad_gradient || n.host_grads.ptr[i].nonfinite != 0;
+        if (bad_gradient || (diagnostics && ((completed + 1) % diagnostics == 0 || completed + 1 == epochs)))
+            gradient_report(n, completed + 1, emit);
+        validate_costs(n, ids.size(), values, true);
+        if (graph) graph_validate(*graph);
+        if (bad_gradient)
+            for (int i = 0; i < n.layers; ++i) {
+                const auto& g = n.host_grads.ptr[i];
+                if (g.nonfinite)
+                    throw RequestError("non-finite weight gradient in layer " + std::to_string(i) +
+                                       ", flattened index " + std::to_string(g.first_nonfinite) +
+                                       "; no optimizer update performed for this iteration");
+            }
+        optimizer_step(n, method);
+        CPDE_CUDA(cudaStreamSynchronize(stream));
+        ++completed;
+        ++n.updates;
+        ++n.stage_done;
+        n.remaining = epochs - completed;
+        if (restore_every && n.updates % restore_every == 0) {
+            floor_steps(n, restore_step);
+            CPDE_CUDA(cudaStreamSynchronize(stream));
+        }
+        bool last = completed == epochs || stopped();
+        if (collect) report_values(n, completed, 0, values, graph.get(), emit);
+        if (eval && (completed % eval == 0 || last)) {
+            evaluate_costs(n, ids, values, graph.get());
+            report_values(n, completed, 1, values, graph.get(), emit);
+            last_eval = completed;
+            if (outputs)
+                for (auto id : ids) {
+                    auto& c = cost(id);
+                    uint64_t output = evaluate(ni, c.input_id, c.width);
+                    auto& d = dat(output);
+                    std::vector<float> a(d.values.count);
+                    CPDE_CUDA(cudaMemcpy(a.data(), d.values.ptr, a.size() * 4, cudaMemcpyDeviceToHost));
+                    Payload r;
+                    r.put<uint64_t>(id);
+                    r.put_array(a);
+                    data.erase(output);
+                    emit(4, r);
+                }
+        }
+        if (save && (completed % save == 0 || last)) {
+            emit(3, snapshot(n));
+            last_saved = completed;
+        }
+    }
+    if (last_eval != completed) {
+        evaluate_costs(n, ids, values, graph.get());
+        report_values(n, completed, 1, values, graph.get(), emit);
+    }
+    if (save && last_saved != completed) emit(3, snapshot(n));
+    Payload result;
+    result.put<uint64_t>(completed);
+    result.put<int32_t>(completed < epochs);
+    auto meta = metadata(n);
+    result.put_array(meta.bytes);
+    emit(0, result);
+}
+
+// Op 14 (cuda/cpde_server.cu:535-551). Gradients go to a scratch bank, so the
+// optimizer state is untouched without a snapshot/restore round trip.
+Payload Engine::graph_evaluate(Payload& b) {
+    uint64_t ni = b.get<uint64_t>();
+    auto& n = net(ni);
+    auto ids = b.array<uint64_t>();
+    bool gradient = b.get<int>() != 0;
+    require(!ids.empty(), "cost graph needs at least one integral");
+    GraphRecord graph;
+    read_graph(graph, b, int(ids.size()));
+    b.end();
+    prepare_costs(n, ids, ni, gradient);
+    n.eval_gradient.reserve(n.params);
+    float* target = gradient ? n.eval_gradient.ptr : nullptr;
+    std::vector<double> values(ids.size());
+    graph_pass(n, ids, graph, gradient, target);
+    if (gradient) inspect_gradients(n, target);
+    download(n, int(ids.size()), gradient ? n.layers : 0);
+    validate_costs(n, ids.size(), values, false);
+    graph_validate(graph);
+    Payload out;
+    out.put<double>(graph.host.ptr[0].value);
+    if (gradient) {
+        out.put<int>(n.layers);
+        std::vector<float> g(n.params);
+        CPDE_CUDA(cudaMemcpy(g.data(), target, n.params * 4, cudaMemcpyDeviceToHost));
+        for (int l = 0; l < n.layers; ++l) {
+            require(!n.host_grads.ptr[l].nonfinite, "nonfinite weight gradient during evaluation");
+            out.put_array(g.data() + n.offset[l], size_t(n.count[l]));
+        }
+    }
+    return out;
+}
+
+// One fixed-weight epoch without synchronisation (op 90's step).
+void Engine::epoch(uint64_t ni, const std::vector<uint64_t>& ids) {
+    auto& n = net(ni);
+    begin_costs(n, int(ids.size()));
+    for (int l = 0; l < n.layers; ++l) CPDE_CUDA(cudaMemsetAsync(n.gradient(l), 0, n.count[l] * 4, stream));
+    for (size_t i = 0; i < ids.size(); ++i)
+        pass(n, cost(ids[i]), int(i), true, true, nullptr, 0, INT_MAX, false, true, nullptr);
+}
+
+Payload Engine::benchmark(uint64_t ni, uint64_t ci, int warm, int iterations, int batches) {
+    auto& n = net(ni);
+    require(warm >= 0 && iterations > 0 && batches > 0, "invalid benchmark controls");
+    std::vector<uint64_t> ids{ci};
+    prepare_costs(n, ids, ni, true);
+    for (int i = 0; i < warm; ++i) epoch(ni, ids);
+    CPDE_CUDA(cudaStreamSynchronize(stream));
+    cudaEvent_t start, stop;
+    CPDE_CUDA(cudaEventCreate(&start));
+    CPDE_CUDA(cudaEventCreate(&stop));
+    std::vector<double> wall, gpu;
+    for (int batch = 0; batch < batches; ++batch) {
+        auto t0 = std::chrono::steady_clock::now();
+        CPDE_CUDA(cudaEventRecord(start, stream));
+        for (int i = 0; i < iterations; ++i) epoch(ni, ids);
+        CPDE_CUDA(cudaEventRecord(stop, stream));
+        CPDE_CUDA(cudaEventSynchronize(stop));
+        auto t1 = std::chrono::steady_clock::now();
+        float ms = 0;
+        CPDE_CUDA(cudaEventElapsedTime(&ms, start, stop));
+        wall.push_back(std::chrono::duration<double, std::milli>(t1 - t0).count() / iterations);
+        gpu.push_back(double(ms) / iterations);
+    }
+    cudaEventDestroy(start);
+    cudaEventDestroy(stop);
+    Payload out;
+    out.put_array(wall);
+    out.put_array(gpu);
+    inspect_gradients(n, nullptr);
+    download(n, 1, n.layers);
+    std::vector<double> values(1);
+    validate_costs(n, 1, values, false);
+    out.put<double>(values[0]);
+    std::vector<float> g(n.params);
+    for (int l = 0; l < n.layers; ++l) {
+        CPDE_CUDA(cudaMemcpy(g.data() + n.offset[l], n.gradient(l), n.count[l] * 4, cudaMemcpyDeviceToHost));
+        out.put_array(g.data() + n.offset[l], size_t(n.count[l]));
+    }
+    return out;
+}
+
+}  // namespace cpde

@@ -1,0 +1,240 @@
+// Compiled integral costs: the scalar IR of a cost is turned into one
+// straight-line CUDA kernel (forward values and a reverse sweep in double per
+// sample) and compiled at run time with NVRTC for this device's sm_XXXa
+// target. The per-sample semantics follow the reference's generated kernel
+// (cuda/expression_program.hpp:31-66): zero adjoints for padded or zero-weight
+// samples, loss = weight * root, stop-gradient components, aliased components
+// summed in double before the float store, and the "bad" code (-1 for a
+// non-finite value, else the last non-finite component index). The kernel
+// here also folds the per-block loss reduction in (cuda/cost_graph.cuh:35-43
+// is a separate launch in the reference) and reads the engine's interleaved
+// output layout.
+#pragma once
+#include <cuda.h>
+#include <nvrtc.h>
+
+#include <iomanip>
+#include <map>
+#include <sstream>
+#include <string>
+#include <vector>
+
+#include "common.hpp"
+#include "scalar.hpp"
+
+namespace cpde {
+
+inline std::string fmt_double(double x) {
+    std::ostringstream s;
+    s << std::setprecision(17) << x;
+    std::string t = s.str();
+    if (t.find_first_of(".eEn") == std::string::npos) t += ".0";
+    return t;
+}
+
+// Device prelude of every generated kernel: cost statistics and the
+// deterministic block/grid reduction (mirrors kernels_generic.cuh).
+static const char* kExpressionPrelude = R"PRELUDE(
+struct CostStats { double value; int bad_sample; int bad_component; };
+__device__ inline CostStats cs_combine(CostStats a, CostStats b) {
+  a.value += b.value;
+  if (b.bad_sample < a.bad_sample || (b.bad_sample == a.bad_sample && b.bad_component < a.bad_component)) {
+    a.bad_sample = b.bad_sample; a.bad_component = b.bad_component; }
+  return a; }
+__device__ inline CostStats cs_empty() { CostStats e; e.value = 0.0; e.bad_sample = 0x7fffffff; e.bad_component = 0x7fffffff; return e; }
+__device__ inline CostStats cs_warp(CostStats v) {
+  for (int o = 16; o; o >>= 1) { CostStats w;
+    w.value = __shfl_down_sync(0xffffffffu, v.value, o);
+    w.bad_sample = __shfl_down_sync(0xffffffffu, v.bad_sample, o);
+    w.bad_component = __shfl_down_sync(0xffffffffu, v.bad_component, o);
+    v = cs_combine(v, w); }
+  return v; }
+__device__ inline void cs_finish(CostStats v, CostStats* partials, unsigned* ticket, CostStats* total) {
+  __shared__ CostStats lanes[32]; __shared__ bool last;
+  int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = cs_warp(v); if (lane == 0) lanes[warp] = v; __syncthreads();
+  if (warp == 0) { v = lane < (int)(blockDim.x >> 5) ? lanes[lane] : cs_empty(); v = cs_warp(v); }
+  if (threadIdx.x == 0) { partials[blockIdx.x] = v; __threadfence();
+    last = atomicAdd(ticket, 1u) == gridDim.x - 1; }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  if (threadIdx.x == 0) { CostStats acc = cs_empty();
+    for (unsigned b = 0; b < gridDim.x; ++b) { volatile CostStats* q = partials + b; CostStats t;
+      t.value = q->value; t.bad_sample = q->bad_sample; t.bad_component = q->bad_component; acc = cs_combine(acc, t); }
+    *total = cs_combine(*total, acc); *ticket = 0; } }
+)PRELUDE";
+
+inline std::string expression_source(const std::vector<ScalarNode>& nodes) {
+    std::ostringstream s;
+    s << kExpressionPrelude;
+    s << "extern \"C\" __global__ void __launch_bounds__(256) cpde_integral(const float* __restrict__ y, "
+         "float* __restrict__ g, const double* __restrict__ fields, const double* __restrict__ weights, "
+         "int RO, int samples, int points, int offset, const double* __restrict__ multiplier, int collect, "
+         "int gradient, CostStats* partials, unsigned* ticket, CostStats* total) {\n";
+    s << "CostStats local = cs_empty();\n";
+    s << "for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < points; p += blockDim.x * gridDim.x) {\n";
+    s << "  const float* yp = y + (size_t)p * RO; float* gp = g + (size_t)p * RO;\n";
+    s << "  if (gradient) for (int i = 0; i < RO; ++i) gp[i] = 0.f;\n";
+    s << "  const double w = weights[offset + p]; if (w == 0) continue;\n";
+    s << "  const double scale = multiplier ? *multiplier : 1.0;\n";
+    s << "  if (gradient && scale == 0 && !collect) continue;\n";
+    s << "  int bad = -2;\n";
+    std::vector<bool> active;
+    const int count = int(nodes.size());
+    for (int i = 0; i < count; ++i) {
+        const auto& n = nodes[i];
+        std::string a = "v" + std::to_string(n.a), b = "v" + std::to_string(n.b), e;
+        switch (n.op) {
+            case kConstant: e = fmt_double(n.parameter); break;
+            case kLeaf: e = "(double)yp[" + std::to_string(n.a) + "]"; break;
+            case kField: e = "fields[(size_t)" + std::to_string(n.a) + " * samples + offset + p]"; break;
+            case kAdd: e = a + " + " + b; break;
+            case kSub: e = a + " - " + b; break;
+            case kMul: e = a + " * " + b; break;
+            case kDiv: e = "(" + b + " == 0 ? nan(\"\") : " + a + " / " + b + ")"; break;
+            case kPower: e = "pow(" + a + ", " + fmt_double(n.parameter) + ")"; break;
+            case kNeg: e = "-" + a; break;
+            case kExp: e = "exp(" + a + ")"; break;
+            case kLog: e = "log(" + a + ")"; break;
+            case kSqrt: e = "sqrt(" + a + ")"; break;
+            case kSin: e = "sin(" + a + ")"; break;
+            case kCos: e = "cos(" + a + ")"; break;
+            case kTanh: e = "tanh(" + a + ")"; break;
+            default: throw RequestError("invalid expression node");
+        }
+        s << "  const double v" << i << " = " << e << "; if (!isfinite(v" << i << ")) bad = -1;\n";
+        bool act = n.op == kLeaf ? n.b == 0 : (n.op <= kField ? false : (active[n.a] || (n.op <= kDiv && active[n.b])));
+        active.push_back(act);
+    }
+    s << "  double loss = 0; if (collect) { loss = w * v" << count - 1 << "; if (!isfinite(loss)) bad = -1; }\n";
+    s << "  local.value += loss;\n";
+    s << "  if (gradient && scale != 0 && bad == -2) {\n";
+    for (int i = 0; i < count; ++i) s << "    double d" << i << " = " << (i + 1 == count ? "1.0" : "0.0") << ";\n";
+    for (int i = count - 1; i >= 0; --i) {
+        const auto& n = nodes[i];
+        if (n.op <= kField || !active[i]) continue;
+        std::string a = "v" + std::to_string(n.a), b = "v" + std::to_string(n.b), v = "v" + std::to_string(i);
+        std::string da = "0", db = "0";
+        switch (n.op) {
+            case kAdd: da = db = "1.0"; break;
+            case kSub: da = "1.0"; db = "-1.0"; break;
+            case kMul: da = b; db = a; break;
+            case kDiv: da = "1.0 / " + b; db = "-" + v + " / " + b; break;
+            case kPower:
+                da = n.parameter == 0 ? "0.0"
+                                      : (n.parameter == 1 ? "1.0"
+                                                          : fmt_double(n.parameter) + " * pow(" + a + ", " +
+                                                                fmt_double(n.parameter - 1) + ")");
+                break;
+            case kNeg: da = "-1.0"; break;
+            case kExp: da = v; break;
+            case kLog: da = "1.0 / " + a; break;
+            case kSqrt: da = "0.5 / " + v; break;
+            case kSin: da = "cos(" + a + ")"; break;
+            case kCos: da = "-sin(" + a + ")"; break;
+            case kTanh: da = "1.0 - " + v + " * " + v; break;
+            default: break;
+        }
+        s << "    if (d" << i << " != 0) {";
+        if (active[n.a]) s << " d" << n.a << " += d" << i << " * (" << da << ");";
+        if (n.op <= kDiv && active[n.b]) s << " d" << n.b << " += d" << i << " * (" << db << ");";
+        s << " }\n";
+    }
+    std::map<int, std::vector<int>> components;
+    for (int i = 0; i < count; ++i)
+        if (nodes[i].op == kLeaf && nodes[i].b == 0) components[nodes[i].a].push_back(i);
+    for (const auto& entry : components) {
+        s << "    { double t = 0";
+        for (int i : entry.second) s << " + d" << i;
+        s << "; const float o = (float)(t * w * scale); gp[" << entry.first << "] = o; if (!isfinite(o)) bad = "
+          << entry.first << "; }\n";
+    }
+    s << "  }\n";
+    s << "  if (bad != -2) { CostStats e; e.value = 0.0; e.bad_sample = offset + p; e.bad_component = bad; "
+         "local = cs_combine(local, e); }\n";
+    s << "}\n";
+    s << "cs_finish(local, partials, ticket, total);\n}\n";
+    return s.str();
+}
+
+// Driver-API entry points are fetched through the runtime, so the library has
+// no link-time dependency on libcuda (it loads on machines without a driver).
+struct DriverApi {
+    decltype(&cuModuleLoadData) module_load = nullptr;
+    decltype(&cuModuleUnload) module_unload = nullptr;
+    decltype(&cuModuleGetFunction) get_function = nullptr;
+    decltype(&cuLaunchKernel) launch = nullptr;
+    decltype(&cuGetErrorString) error_string = nullptr;
+};
+
+inline DriverApi& driver_api() {
+    static DriverApi api = [] {
+        DriverApi d;
+        auto get = [](const char* name, void** fn) {
+            cudaDriverEntryPointQueryResult status;
+            if (cudaGetDriverEntryPoint(name, fn, cudaEnableDefault, &status) != cudaSuccess ||
+                status != cudaDriverEntryPointSuccess)
+                throw DeviceError(std::string("CUDA driver entry point unavailable: ") + name);
+        };
+        get("cuModuleLoadData", (void**)&d.module_load);
+        get("cuModuleUnload", (void**)&d.module_unload);
+        get("cuModuleGetFunction", (void**)&d.get_function);
+        get("cuLaunchKernel", (void**)&d.launch);
+        get("cuGetErrorString", (void**)&d.error_string);
+        return d;
+    }();
+    return api;
+}
+
+inline void driver_check(CUresult r, const char* what) {
+    if (r == CUDA_SUCCESS) return;
+    const char* msg = nullptr;
+    driver_api().error_string(r, &msg);
+    throw DeviceError(std::string(what) + ": " + (msg ? msg : "CUDA driver error"));
+}
+
+struct ExpressionProgram {
+    std::vector<ScalarNode> nodes;
+    std::string code, log;
+    CUmodule module = nullptr;
+    CUfunction kernel = nullptr;
+
+    explicit ExpressionProgram(std::vector<ScalarNode> ir) : nodes(std::move(ir)), code(expression_source(nodes)) {}
+    ExpressionProgram(const ExpressionProgram&) = delete;
+    ~ExpressionProgram() {
+        if (module) driver_api().module_unload(module);
+    }
+
+    void compile() {
+        if (module) return;
+        int device = 0;
+        CPDE_CUDA(cudaGetDevice(&device));
+        cudaDeviceProp prop;
+        CPDE_CUDA(cudaGetDeviceProperties(&prop, device));
+        std::string arch = "--gpu-architecture=sm_" + std::to_string(prop.major) + std::to_string(prop.minor) +
+                           (prop.major >= 9 ? "a" : "");
+        const char* options[] = {"--std=c++17", arch.c_str()};
+        nvrtcProgram program;
+        nvrtcResult r = nvrtcCreateProgram(&program, code.c_str(), "cpde_integral.cu", 0, nullptr, nullptr);
+        if (r != NVRTC_SUCCESS) throw DeviceError(nvrtcGetErrorString(r));
+        r = nvrtcCompileProgram(program, 2, options);
+        size_t size = 0;
+        nvrtcGetProgramLogSize(program, &size);
+        log.assign(size, '\0');
+        if (size) nvrtcGetProgramLog(program, &log[0]);
+        while (!log.empty() && log.back() == '\0') log.pop_back();
+        if (r != NVRTC_SUCCESS) {
+            nvrtcDestroyProgram(&program);
+            throw RequestError("expression compile failed: " + log);
+        }
+        nvrtcGetCUBINSize(program, &size);
+        std::vector<char> cubin(size);
+        nvrtcGetCUBIN(program, cubin.data());
+        nvrtcDestroyProgram(&program);
+        driver_check(driver_api().module_load(&module, cubin.data()), "cuModuleLoadData");
+        driver_check(driver_api().get_function(&kernel, module, "cpde_integral"), "cuModuleGetFunction");
+    }
+};
+
+}  // namespace cpde

@@ -1,0 +1,574 @@
+// Generic-tier kernels: correct for every network shape and derivative schema.
+//
+// Activation layout (engine-internal, per layer): column c = p*R + r holds the
+// n values of neuron 0..n-1 for point p and derivative row r, so element
+// (neuron m, point p, row r) lives at (p*R + r)*n + m. A point's R rows are
+// adjacent columns, which lets a tile of whole points carry every derivative a
+// jet combine needs. The reference stores rows channel-major instead
+// (cuda/cpde_engine.cuh:365); conversion happens only at copy-in/copy-out.
+#pragma once
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+
+namespace cpde {
+
+constexpr int kReduceThreads = 256;
+
+struct CostStats {
+    double value;
+    int bad_sample;     // INT_MAX when none
+    int bad_component;  // -1: objective; otherwise row*outputs+output
+};
+
+struct GradStats {
+    double squared_norm;
+    double max_abs;
+    unsigned long long nonfinite;
+    int first_nonfinite;  // INT_MAX when none
+    int pad;
+};
+
+__host__ __device__ inline CostStats cost_empty() { return {0.0, INT_MAX, INT_MAX}; }
+__host__ __device__ inline CostStats cost_combine(CostStats a, const CostStats& b) {
+    a.value += b.value;
+    if (b.bad_sample < a.bad_sample || (b.bad_sample == a.bad_sample && b.bad_component < a.bad_component)) {
+        a.bad_sample = b.bad_sample;
+        a.bad_component = b.bad_component;
+    }
+    return a;
+}
+__host__ __device__ inline GradStats grad_empty() { return {0.0, 0.0, 0ull, INT_MAX, 0}; }
+__host__ __device__ inline GradStats grad_combine(GradStats a, const GradStats& b) {
+    a.squared_norm += b.squared_norm;
+    if (b.max_abs > a.max_abs) a.max_abs = b.max_abs;
+    a.nonfinite += b.nonfinite;
+    if (b.first_nonfinite < a.first_nonfinite) a.first_nonfinite = b.first_nonfinite;
+    return a;
+}
+
+__device__ inline void mark_bad(CostStats& s, int sample, int component) {
+    s = cost_combine(s, CostStats{0.0, sample, component});
+}
+
+// ---------------------------------------------------------------------------
+// Block-wide reductions with warp shuffles, then a deterministic last-block
+// finish: every block stores its partial; the block that arrives last (atomic
+// ticket) combines all partials in block order and folds them into *total.
+
+__device__ inline CostStats warp_reduce(CostStats v) {
+    for (int o = 16; o; o >>= 1) {
+        CostStats w;
+        w.value = __shfl_down_sync(0xffffffffu, v.value, o);
+        w.bad_sample = __shfl_down_sync(0xffffffffu, v.bad_sample, o);
+        w.bad_component = __shfl_down_sync(0xffffffffu, v.bad_component, o);
+        v = cost_combine(v, w);
+    }
+    return v;
+}
+__device__ inline GradStats warp_reduce(GradStats v) {
+    for (int o = 16; o; o >>= 1) {
+        GradStats w;
+        w.squared_norm = __shfl_down_sync(0xffffffffu, v.squared_norm, o);
+        w.max_abs = __shfl_down_sync(0xffffffffu, v.max_abs, o);
+        w.nonfinite = __shfl_down_sync(0xffffffffu, v.nonfinite, o);
+        w.first_nonfinite = __shfl_down_sync(0xffffffffu, v.first_nonfinite, o);
+        v = grad_combine(v, w);
+    }
+    return v;
+}
+
+template <class T, class Empty>
+__device__ T block_reduce(T v, Empty empty) {
+    __shared__ T lanes[32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    v = warp_reduce(v);
+    if (lane == 0) lanes[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+        v = lane < (int)(blockDim.x >> 5) ? lanes[lane] : empty();
+        v = warp_reduce(v);
+    }
+    __syncthreads();
+    return v;
+}
+
+// Folds this block's value into *total once all blocks have arrived.
+// Loads that bypass L1: partials are written by other SMs during this launch.
+__device__ inline CostStats load_cg(const CostStats* p) {
+    return {__ldcg(&p->value), __ldcg(&p->bad_sample), __ldcg(&p->bad_component)};
+}
+__device__ inline GradStats load_cg(const GradStats* p) {
+    return {__ldcg(&p->squared_norm), __ldcg(&p->max_abs), __ldcg(&p->nonfinite), __ldcg(&p->first_nonfinite), 0};
+}
+
+template <class T, class Combine, class Empty>
+__device__ void finish_blocks(T mine, T* partials, unsigned* ticket, T* total, Combine combine, Empty empty) {
+    __shared__ bool last;
+    if (threadIdx.x == 0) {
+        partials[blockIdx.x] = mine;
+        __threadfence();
+        unsigned arrived = atomicAdd(ticket, 1u);
+        last = arrived == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    if (threadIdx.x == 0) {
+        T acc = empty();
+        for (unsigned b = 0; b < gridDim.x; ++b) acc = combine(acc, load_cg(partials + b));
+        *total = combine(*total, acc);
+        *ticket = 0;
+    }
+}
+
+__global__ void k_clear_costs(CostStats* totals, int count) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < count; i += blockDim.x * gridDim.x)
+        totals[i] = cost_empty();
+}
+
+// ---------------------------------------------------------------------------
+// Activation jets: value and derivative at the value row.
+
+struct Sigmoid {
+    static constexpr int id = 0;
+    // y = sigma(z), s = sigma'(z) evaluated without cancellation on both tails.
+    __device__ static void value(float z, float& y, float& s) {
+        float e = __expf(-fabsf(z));
+        float big = 1.0f / (1.0f + e);  // sigma(|z|) >= 1/2
+        float small = e * big;          // 1 - sigma(|z|)
+        y = z >= 0.f ? big : small;
+        s = big * small;
+    }
+    __device__ static float slope_from_value(float y) { return y * (1.0f - y); }
+    __device__ static float lead(float y) { return 1.0f - 2.0f * y; }
+};
+
+struct Tanh {
+    static constexpr int id = 1;
+    __device__ static void value(float z, float& y, float& s) {
+        y = tanhf(z);
+        s = (1.0f - y) * (1.0f + y);
+    }
+    __device__ static float slope_from_value(float y) { return (1.0f - y) * (1.0f + y); }
+    __device__ static float lead(float y) { return -2.0f * y; }
+};
+
+// ---------------------------------------------------------------------------
+// Copy-in: inputs of one chunk from the data record's (row, sample, channel)
+// layout into the interleaved layer-0 layout.
+
+__global__ void k_stage_input(const float* __restrict__ data, int channels, int data_samples,
+                              const int* __restrict__ rows, int R, int offset, int points,
+                              float* __restrict__ out) {
+    long total = (long)points * R * channels;
+    for (long e = blockIdx.x * (long)blockDim.x + threadIdx.x; e < total; e += (long)blockDim.x * gridDim.x) {
+        int c = int(e % channels);
+        long col = e / channels;
+        int r = int(col % R);
+        long p = col / R;
+        out[e] = data[((long)rows[r] * data_samples + offset + p) * channels + c];
+    }
+}
+
+// Copy-out of evaluation outputs into the (row, sample, output) layout.
+__global__ void k_scatter_output(const float* __restrict__ z, int outputs, int R, const int* __restrict__ rows,
+                                 int offset, int points, int data_samples, float* __restrict__ out) {
+    long total = (long)points * R * outputs;
+    for (long e = blockIdx.x * (long)blockDim.x + threadIdx.x; e < total; e += (long)blockDim.x * gridDim.x) {
+        int o = int(e % outputs);
+        long col = e / outputs;
+        int r = int(col % R);
+        long p = col / R;
+        out[((long)rows[r] * data_samples + offset + p) * outputs + o] = z[e];
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Generic FP32 GEMM, column-major: C = op(A) * op(B) (+ bias / split-K).
+// 64x64 tile, 16-deep K slab, 256 threads, 4x4 outputs per thread.
+//  * BIAS_ROWS: add bias[m] to columns with n % R == 0 (the value row).
+//  * INDICATOR: op(B) has one extra virtual column N-1 equal to 1 where
+//    k % R == 0, so the last output column is the bias gradient.
+//  * split-K (gridDim.z > 1): each z-slice writes its own dense M x N partial.
+
+namespace gemm {
+constexpr int BM = 64, BN = 64, BK = 16, THREADS = 256;
+}
+
+template <bool TA, bool TB, bool BIAS_ROWS, bool INDICATOR>
+__global__ void __launch_bounds__(gemm::THREADS)
+k_gemm(int M, int N, int K, const float* __restrict__ A, int lda, const float* __restrict__ B, int ldb,
+       float* __restrict__ C, int ldc, const float* __restrict__ bias, int R, int k_per_split) {
+    using namespace gemm;
+    __shared__ float As[BK][BM + 4];
+    __shared__ float Bs[BK][BN + 4];
+    const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+    const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
+    const long k_begin = (long)blockIdx.z * k_per_split;
+    const long k_end = min((long)K, k_begin + k_per_split);
+    float acc[4][4] = {};
+    const int nreal = INDICATOR ? N - 1 : N;
+    for (long k0 = k_begin; k0 < k_end; k0 += BK) {
+        for (int i = threadIdx.x; i < BM * BK; i += THREADS) {
+            int mm, kk;
+            if (TA) { kk = i % BK; mm = i / BK; } else { mm = i % BM; kk = i / BM; }
+            long k = k0 + kk;
+            int m = m0 + mm;
+            float v = 0.f;
+            if (m < M && k < k_end) v = TA ? A[k + (long)m * lda] : A[m + k * (long)lda];
+            As[kk][mm] = v;
+        }
+        for (int i = threadIdx.x; i < BN * BK; i += THREADS) {
+            int nn, kk;
+            if (TB) { nn = i % BN; kk = i / BN; } else { kk = i % BK; nn = i / BK; }
+            long k = k0 + kk;
+            int n = n0 + nn;
+            float v = 0.f;
+            if (k < k_end) {
+                if (n < nreal) v = TB ? B[n + k * (long)ldb] : B[k + (long)n * ldb];
+                else if (INDICATOR && n == nreal) v = (k % R) == 0 ? 1.f : 0.f;
+            }
+            Bs[kk][nn] = v;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int kk = 0; kk < BK; ++kk) {
+            float a[4], b[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) a[i] = As[kk][ty * 4 + i];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) b[j] = Bs[kk][tx * 4 + j];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+    float* out = C + (size_t)blockIdx.z * (gridDim.z > 1 ? (size_t)M * N : 0);
+    const int ld = gridDim.z > 1 ? M : ldc;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        int m = m0 + ty * 4 + i;
+        if (m >= M) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            int n = n0 + tx * 4 + j;
+            if (n >= N) continue;
+            float v = acc[i][j];
+            if (BIAS_ROWS && (n % R) == 0) v += bias[m];
+            out[m + (size_t)n * ld] = v;
+        }
+    }
+}
+
+// out[m + n*ldc] (+)= sum_z partial[z][m + n*M], summed in z order (deterministic).
+__global__ void k_splitk_reduce(const float* __restrict__ partial, int splits, int M, int N, float* __restrict__ out,
+                                int ldc, int accumulate) {
+    long total = (long)M * N;
+    for (long e = blockIdx.x * (long)blockDim.x + threadIdx.x; e < total; e += (long)blockDim.x * gridDim.x) {
+        float acc = 0.f;
+        for (int z = 0; z < splits; ++z) acc += partial[(size_t)z * total + e];
+        int m = int(e % M);
+        long n = e / M;
+        float* dst = out + m + n * ldc;
+        *dst = accumulate ? *dst + acc : acc;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Table-driven jets (any schema). Thread per (neuron, point); the rows of that
+// element are strided by n in the interleaved layout, so a warp's accesses
+// for one row are contiguous. ``tab`` is JetPlan::pack().
+
+__device__ inline float tcoef(const int* t, int i) { return __int_as_float(t[i]); }
+
+template <class Act>
+__global__ void k_jet_forward_dyn(const float* __restrict__ Z, float* __restrict__ Y, float* __restrict__ S, int n,
+                                  long points, int R, const int* __restrict__ tab) {
+    const int* fwd = tab;
+    const int* sq = tab + (R + 1);
+    long total = (long)n * points;
+    for (long e = blockIdx.x * (long)blockDim.x + threadIdx.x; e < total; e += (long)blockDim.x * gridDim.x) {
+        int m = int(e % n);
+        long p = e / n;
+        size_t base = (size_t)p * R * n + m;
+        float y0, s0;
+        Act::value(Z[base], y0, s0);
+        Y[base] = y0;
+        S[base] = s0;
+        float lead = Act::lead(y0);
+        for (int r = 1; r < R; ++r) {
+            float acc = 0.f;
+            for (int t = fwd[r]; t < fwd[r + 1]; t += 3)
+                acc = fmaf(tcoef(tab, t) * S[base + (size_t)tab[t + 1] * n], Z[base + (size_t)tab[t + 2] * n], acc);
+            Y[base + (size_t)r * n] = acc;
+            float sacc = lead * acc;
+            for (int t = sq[r]; t < sq[r + 1]; t += 3)
+                sacc = fmaf(-tcoef(tab, t) * Y[base + (size_t)tab[t + 1] * n], Y[base + (size_t)tab[t + 2] * n], sacc);
+            S[base + (size_t)r * n] = sacc;
+        }
+    }
+}
+
+template <class Act>
+__global__ void k_jet_adjoint_dyn(const float* __restrict__ dY, const float* __restrict__ Y, float* __restrict__ S,
+                                  float* __restrict__ dZ, int n, long points, int R, const int* __restrict__ tab) {
+    const int* sq = tab + (R + 1);
+    const int* adj = tab + 2 * (R + 1);
+    long total = (long)n * points;
+    for (long e = blockIdx.x * (long)blockDim.x + threadIdx.x; e < total; e += (long)blockDim.x * gridDim.x) {
+        int m = int(e % n);
+        long p = e / n;
+        size_t base = (size_t)p * R * n + m;
+        float y0 = Y[base];
+        S[base] = Act::slope_from_value(y0);
+        float lead = Act::lead(y0);
+        for (int r = 1; r < R; ++r) {
+            float sacc = lead * Y[base + (size_t)r * n];
+            for (int t = sq[r]; t < sq[r + 1]; t += 3)
+                sacc = fmaf(-tcoef(tab, t) * Y[base + (size_t)tab[t + 1] * n], Y[base + (size_t)tab[t + 2] * n], sacc);
+            S[base + (size_t)r * n] = sacc;
+        }
+        for (int r = 0; r < R; ++r) {
+            float acc = 0.f;
+            for (int t = adj[r]; t < adj[r + 1]; t += 3)
+                acc = fmaf(tcoef(tab, t) * S[base + (size_t)tab[t + 1] * n], dY[base + (size_t)tab[t + 2] * n], acc);
+            dZ[base + (size_t)r * n] = acc;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Costs. One thread per point of the chunk; every output component of the
+// point is handled by that thread, so equations that share components add
+// into dE/dY without atomics (same contract as cuda/cost_kernels.cuh:4-5).
+
+struct CostReduce {
+    CostStats* partials;
+    unsigned* ticket;
+    CostStats* total;
+};
+
+__device__ inline void cost_finish(CostStats local, const CostReduce& red) {
+    CostStats b = block_reduce(local, cost_empty);
+    finish_blocks(b, red.partials, red.ticket, red.total, cost_combine, cost_empty);
+}
+
+// Squared-error matching: sum over rows d and outputs o of w*(y-t)^2, with
+// dE/dy = 2w(y-t) (cuda/cost_kernels.cuh:6-35 semantics). ``y``/``g`` use the
+// interleaved layout with n = outputs.
+__global__ void k_cost_matching(const float* __restrict__ y, float* __restrict__ g, const float* __restrict__ target,
+                                int target_samples, const int* __restrict__ target_rows,
+                                const float* __restrict__ weights, int weight_samples, int outputs, int R, int points,
+                                int offset, int collect, int gradient, CostReduce red) {
+    CostStats local = cost_empty();
+    for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < points; p += blockDim.x * gridDim.x) {
+        float value = 0.f;
+        const int wp = weight_samples == 1 ? 0 : offset + p;
+        for (int d = 0; d < R; ++d)
+            for (int o = 0; o < outputs; ++o) {
+                size_t i = ((size_t)p * R + d) * outputs + o;
+                float w = weights[((size_t)d * weight_samples + wp) * outputs + o];
+                float grad = 0.f;
+                if (w != 0.f) {
+                    float r = y[i] - target[((size_t)target_rows[d] * target_samples + offset + p) * outputs + o];
+                    value += w * r * r;
+                    grad = 2.0f * w * r;
+                }
+                if (gradient) g[i] = grad;
+            }
+        if (!isfinite(value)) mark_bad(local, offset + p, -1);
+        if (collect) local.value += double(value);
+        if (gradient)
+            for (int d = 0; d < R; ++d)
+                for (int o = 0; o < outputs; ++o)
+                    if (!isfinite(g[((size_t)p * R + d) * outputs + o])) mark_bad(local, offset + p, d * outputs + o);
+    }
+    cost_finish(local, red);
+}
+
+struct PolyTerm {
+    int equation, a, b;  // b = -1: linear term
+};
+
+__device__ inline float component(const float* y, int index, int outputs, int R, int p) {
+    return y[((size_t)p * R + index / outputs) * outputs + index % outputs];
+}
+
+// Polynomial residuals r_e = sum_t c_t y_a (y_b or 1) - rhs_e, loss w r^2
+// (cuda/cost_kernels.cuh:37-90 semantics).
+__global__ void k_cost_polynomial(const float* __restrict__ y, float* __restrict__ g, const PolyTerm* __restrict__ terms,
+                                  const float* __restrict__ coefficients, int term_count, const float* __restrict__ rhs,
+                                  const float* __restrict__ weights, int outputs, int R, int equations, int samples,
+                                  int points, int offset, int collect, int gradient, CostReduce red) {
+    CostStats local = cost_empty();
+    for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < points; p += blockDim.x * gridDim.x) {
+        if (gradient)
+            for (int i = 0; i < R * outputs; ++i) g[(size_t)p * R * outputs + i] = 0.f;
+        float total = 0.f;
+        const int sample = offset + p;
+        for (int e = 0; e < equations; ++e) {
+            float w = weights[(size_t)e * samples + sample];
+            if (w == 0.f) continue;
+            float r = -rhs[(size_t)e * samples + sample];
+            for (int t = 0; t < term_count; ++t) {
+                if (terms[t].equation != e) continue;
+                float c = coefficients[(size_t)t * samples + sample];
+                if (c == 0.f) continue;
+                float a = component(y, terms[t].a, outputs, R, p);
+                r += c * a * (terms[t].b < 0 ? 1.0f : component(y, terms[t].b, outputs, R, p));
+            }
+            total += w * r * r;
+            float scale = 2.0f * w * r;
+            if (!gradient) continue;
+            for (int t = 0; t < term_count; ++t) {
+                if (terms[t].equation != e) continue;
+                float c = coefficients[(size_t)t * samples + sample];
+                if (c == 0.f) continue;
+                int ia = terms[t].a, ib = terms[t].b;
+                size_t ga = ((size_t)p * R + ia / outputs) * outputs + ia % outputs;
+                if (ib < 0) {
+                    g[ga] += scale * c;
+                } else {
+                    size_t gb = ((size_t)p * R + ib / outputs) * outputs + ib % outputs;
+                    g[ga] += scale * c * component(y, ib, outputs, R, p);
+                    g[gb] += scale * c * component(y, ia, outputs, R, p);
+                }
+            }
+        }
+        if (!isfinite(total)) mark_bad(local, sample, -1);
+        if (collect) local.value += double(total);
+        if (gradient)
+            for (int i = 0; i < R * outputs; ++i)
+                if (!isfinite(g[(size_t)p * R * outputs + i])) mark_bad(local, sample, i);
+    }
+    cost_finish(local, red);
+}
+
+// dE/dy *= multiplier (graph leaf multiplier), zero when the multiplier is 0
+// (cuda/cost_graph.cuh:29-34).
+__global__ void k_scale(float* __restrict__ g, long count, const double* __restrict__ multiplier) {
+    double m = *multiplier;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < count; i += (long)blockDim.x * gridDim.x)
+        g[i] = m == 0 ? 0.f : float(g[i] * m);
+}
+
+// ---------------------------------------------------------------------------
+// Gradient inspection: per layer L2^2, max |g|, non-finite count and first
+// index (cuda/reduction_kernels.cuh:81-98 semantics). blockIdx.y = layer.
+
+struct GradReduce {
+    GradStats* partials;  // [layers][gridDim.x]
+    unsigned* tickets;    // [layers]
+    GradStats* totals;    // [layers]
+};
+
+__global__ void k_inspect_gradients(const float* const* __restrict__ grads, const int* __restrict__ counts,
+                                    GradReduce red) {
+    const int layer = blockIdx.y;
+    const float* g = grads[layer];
+    const int count = counts[layer];
+    GradStats local = grad_empty();
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < count; i += blockDim.x * gridDim.x) {
+        double v = g[i];
+        if (!isfinite(v)) {
+            ++local.nonfinite;
+            if (i < local.first_nonfinite) local.first_nonfinite = i;
+        } else {
+            local.squared_norm += v * v;
+            double a = fabs(v);
+            if (a > local.max_abs) local.max_abs = a;
+        }
+    }
+    GradStats b = block_reduce(local, grad_empty);
+    finish_blocks(b, red.partials + (size_t)layer * gridDim.x, red.tickets + layer, red.totals + layer, grad_combine,
+                  grad_empty);
+}
+
+// ---------------------------------------------------------------------------
+// Optimizers over every layer in one launch; blockIdx.y = layer. Banks hold
+// the flat parameters of all layers: 0 weights, 1/2 gradient history,
+// 3 RPROP steps or Adam first moment.
+
+struct OptLayer {
+    long offset;
+    int count;
+    int active;  // 1 or 2: bank holding the current gradient
+};
+
+// RPROP (cuda/derivative_kernels_v4.cu:752-778): grow x1.2 on agreeing signs,
+// roll back and halve on a sign change, |W| <= 20 guard restarting at 0.1.
+__global__ void k_rprop(float* __restrict__ w, float* __restrict__ bank1, float* __restrict__ bank2,
+                        float* __restrict__ steps, const OptLayer* __restrict__ layers) {
+    const OptLayer L = layers[blockIdx.y];
+    float* cur = (L.active == 1 ? bank1 : bank2) + L.offset;
+    float* prev = (L.active == 1 ? bank2 : bank1) + L.offset;
+    float* W = w + L.offset;
+    float* D = steps + L.offset;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < L.count; i += blockDim.x * gridDim.x) {
+        float a = cur[i], b = prev[i], d = D[i], wi = W[i];
+        if (a * b > 0) d *= 1.2f;
+        float nw = wi - copysignf(d, a);
+        if (a * b < 0) {
+            wi += copysignf(d, b);
+            d *= 0.5f;
+            cur[i] = 0.0f;
+        } else if (a != 0.0f) {
+            if (fabsf(nw) <= 20.0f) wi = nw;
+            else {
+                d = 0.1f;
+                cur[i] = 0.0f;
+            }
+        }
+        W[i] = wi;
+        D[i] = d;
+    }
+}
+
+// Adam (cuda/derivative_kernels_v4.cu:780-799), including the reference's
+// double-precision denominator from the 1e-8 literal.
+__global__ void k_adam(float* __restrict__ w, float* __restrict__ bank1, float* __restrict__ bank2,
+                       float* __restrict__ first, const OptLayer* __restrict__ layers, float alpha, float beta1,
+                       float beta2, float beta1t, float beta2t) {
+    const OptLayer L = layers[blockIdx.y];
+    const float* grad = (L.active == 1 ? bank1 : bank2) + L.offset;
+    float* V = (L.active == 1 ? bank2 : bank1) + L.offset;
+    float* M = first + L.offset;
+    float* W = w + L.offset;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < L.count; i += blockDim.x * gridDim.x) {
+        float g = grad[i];
+        float m = __fadd_rn(__fmul_rn(beta1, M[i]), __fmul_rn(1 - beta1, g));
+        float v = __fadd_rn(__fmul_rn(beta2, V[i]), __fmul_rn(__fmul_rn(1 - beta2, g), g));
+        M[i] = m;
+        V[i] = v;
+        float mh = __fdiv_rn(m, 1 - beta1t);
+        float vh = __fdiv_rn(v, 1 - beta2t);
+        double step = double(__fmul_rn(alpha, mh)) / (double(sqrtf(vh)) + 1e-8);
+        float nw = float(double(W[i]) - step);
+        if (fabsf(nw) <= 20.0f) W[i] = nw;
+    }
+}
+
+// Steps below the floor are raised to it and that entry's history cleared
+// (cuda/derivative_kernels_v4.cu:801-814).
+__global__ void k_rprop_floor(float* __restrict__ bank1, float* __restrict__ bank2, float* __restrict__ steps,
+                              const OptLayer* __restrict__ layers, float floor_value) {
+    const OptLayer L = layers[blockIdx.y];
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < L.count; i += blockDim.x * gridDim.x) {
+        long j = L.offset + i;
+        if (steps[j] < floor_value) {
+            steps[j] = floor_value;
+            bank1[j] = 0.f;
+            bank2[j] = 0.f;
+        }
+    }
+}
+
+__global__ void k_fill(float* __restrict__ dst, long count, float value) {
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < count; i += (long)blockDim.x * gridDim.x)
+        dst[i] = value;
+}
+
+}  // namespace cpde
