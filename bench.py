@@ -116,6 +116,28 @@ def cpu_baseline(points=128, steps=2):
                 ms_per_epoch_sample=ms)
 
 
+def reference_cuda(device, points=POINTS, iterations=3, batches=3):
+    """The reference's own CUDA server, built for sm_100a from its sources by
+    oracle/Makefile, timed with its op-90 command on the same GPU and workload."""
+    exe = ROOT / 'oracle' / '_ref' / 'cpde_ref_cuda_server'
+    if not exe.exists():
+        return None
+    from cpde_b200.client import Data, Network, Session
+    t, x, targets, weights = workload(points)
+    env = dict(os.environ)
+    env.pop('NVIDIA_TF32_OVERRIDE', None)
+    with Session(exe, device=device, env=env) as s:
+        net = Network(s, LAYERS, weights=weights)
+        inp = Data(s, x, t)
+        tgt = Data(s, targets, t)
+        cost = net.matching(inp, tgt, np.ones((1, len(t)), np.float32))
+        wall, gpu, loss, _ = net.benchmark(cost, warm=1, iterations=iterations, batches=batches)
+    ms = float(np.median(gpu))
+    return dict(ms_per_epoch=ms, value=points * len(t) / (ms / 1000), unit=UNIT, loss=loss,
+                how='oracle/_ref/cpde_ref_cuda_server (reference sources, nvcc sm_100a, cuBLAS FP32), '
+                    f'op 90, median of {batches} batches x {iterations} epochs, device time')
+
+
 def run_reference(args):
     rank = int(os.environ.get('RANK', '0'))
     if rank != 0:
@@ -238,6 +260,12 @@ def run_b200(args):
                     gemm_gflop_per_step=(fwd + dgrad + wgrad) / 1e9, loss=loss)
         if world == 1 and not args.no_cpu_baseline:
             line['cpu_baseline'] = cpu_baseline()
+        if world == 1 and not args.no_reference_cuda:
+            engine.close()
+            ref = reference_cuda(local, args.points)
+            if ref is not None:
+                ref['speedup_of_value'] = value / ref['value']
+                line['reference_cuda_same_gpu'] = ref
         print(json.dumps(line))
     engine.close()
     if dist is not None:
@@ -253,6 +281,7 @@ def main():
     p.add_argument('--points', type=int, default=POINTS)
     p.add_argument('--reference-points', type=int, default=128)
     p.add_argument('--no-cpu-baseline', action='store_true')
+    p.add_argument('--no-reference-cuda', action='store_true')
     args = p.parse_args()
     if args.impl == 'reference':
         run_reference(args)

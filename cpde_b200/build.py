@@ -31,8 +31,11 @@ def _stale(target, sources):
 
 
 def build(force=False, verbose_ptxas=False):
+    from . import codegen
+    codegen.write()
     nvcc = os.environ.get('NVCC', 'nvcc')
     sources = sorted(CSRC.glob('*.cu')) + sorted(CSRC.glob('*.cuh')) + sorted(CSRC.glob('*.hpp'))
+    sources += sorted((CSRC / 'generated').glob('*.cuh'))
     sources.append(PACKAGE.parent / 'include' / 'cpde_b200.h')
     if force or _stale(LIBRARY, sources):
         cmd = [nvcc, *ARCH, '-lineinfo', '-O3', '-std=c++17', '-Xcompiler', '-fPIC', '-shared',

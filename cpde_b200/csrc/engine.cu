@@ -198,6 +198,15 @@ std::shared_ptr<Context> Engine::make_context(DataRecord& d, const std::vector<i
         ctx->plan = JetPlan::build(counts);
         ctx->tables.upload(ctx->plan.pack(), stream);
         ctx->planned = true;
+        for (int sid = 0; sid < kStaticSchemas; ++sid) {
+            const auto& info = kStaticSchemaInfo[sid];
+            if (info.variables != d.v || info.rows != int(rows.size())) continue;
+            bool same = true;
+            for (int r = 0; r < info.rows && same; ++r)
+                for (int v = 0; v < d.v; ++v)
+                    same = same && kStaticSchemaCounts[info.offset + r * d.v + v] == counts[r][v];
+            if (same) ctx->static_id = sid;
+        }
     }
     CPDE_CUDA(cudaStreamSynchronize(stream));
     contexts[full] = ctx;
@@ -329,12 +338,13 @@ void Engine::activate(NetRecord& n, uint64_t data_id, Context& ctx, int width, i
 template <bool TA, bool TB, bool BIAS, bool IND>
 static void launch_gemm(Engine& e, int M, int N, int K, const float* A, int lda, const float* B, int ldb, float* C,
                         int ldc, const float* bias, int R) {
-    dim3 grid((M + gemm::BM - 1) / gemm::BM, (N + gemm::BN - 1) / gemm::BN, 1);
+    dim3 grid((N + gemm::BN - 1) / gemm::BN, (M + gemm::BM - 1) / gemm::BM, 1);
     CPDE_RUN(e, "gemm", (k_gemm<TA, TB, BIAS, IND><<<grid, gemm::THREADS, 0, e.stream>>>(M, N, K, A, lda, B, ldb, C,
                                                                                           ldc, bias, R, K)));
 }
 
 void Engine::forward(NetRecord& n, Context& ctx, int points) {
+    if (fast_ok(n, ctx)) return fast_forward(n, ctx, points);
     const int R = ctx.R();
     const int cols = points * R;
     for (int l = 1; l <= n.layers; ++l) {
@@ -358,6 +368,7 @@ void Engine::forward(NetRecord& n, Context& ctx, int points) {
 }
 
 void Engine::backward(NetRecord& n, Context& ctx, int points, float* target) {
+    if (fast_ok(n, ctx)) return fast_backward(n, ctx, points, target);
     const int R = ctx.R();
     const long cols = long(points) * R;
     float* cur = n.dz[0].ptr;
@@ -370,7 +381,7 @@ void Engine::backward(NetRecord& n, Context& ctx, int points, float* target) {
         long per = ((cols + splits - 1) / splits + gemm::BK - 1) / gemm::BK * gemm::BK;
         splits = (cols + per - 1) / per;
         n.partial.reserve(size_t(splits) * M * N);
-        dim3 grid((M + gemm::BM - 1) / gemm::BM, (N + gemm::BN - 1) / gemm::BN, unsigned(splits));
+        dim3 grid((N + gemm::BN - 1) / gemm::BN, (M + gemm::BM - 1) / gemm::BM, unsigned(splits));
         CPDE_RUN(*this, "gemm_wgrad",
                  (k_gemm<false, true, false, true><<<grid, gemm::THREADS, 0, stream>>>(
                      M, N, int(cols), cur, nl, n.act[l - 1].ptr, np, n.partial.ptr, M, nullptr, R, int(per))));
@@ -396,6 +407,173 @@ void Engine::backward(NetRecord& n, Context& ctx, int points, float* target) {
         }
         cur = next;
     }
+}
+
+
+// ---------------------------------------------------------------------------
+// fast tier dispatch
+
+static_assert(kStaticSchemas == 10, "update CPDE_STATIC_CASES after changing the generated schemas");
+#define CPDE_STATIC_CASES(X) X(0) X(1) X(2) X(3) X(4) X(5) X(6) X(7) X(8) X(9)
+
+template <class F>
+static void with_schema(int sid, F&& f) {
+    switch (sid) {
+#define CPDE_CASE(i) \
+    case i:          \
+        f.template run<i>(); \
+        return;
+        CPDE_STATIC_CASES(CPDE_CASE)
+#undef CPDE_CASE
+    }
+    throw DeviceError("unknown static schema");
+}
+
+template <class K>
+static void allow_smem(K kernel, size_t bytes) {
+    CPDE_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes)));
+}
+
+bool Engine::fast_ok(NetRecord& n, Context& ctx) const {
+    if (tier == 1 || ctx.static_id < 0) return false;
+    const int L = n.layers;
+    if (L < 3 || n.neurons[0] > 8 || n.neurons[L] > 8) return false;
+    for (int l = 1; l < L; ++l)
+        if (n.linear[l] == 1 || n.linear[l] != n.linear[1] || n.neurons[l] % 32 != 0) return false;
+    return true;
+}
+
+namespace {
+struct FastForward {
+    Engine& e;
+    NetRecord& n;
+    long P;
+    template <int SID, class Act>
+    void layers() {
+        using namespace fast;
+        constexpr int R = StaticJet<SID>::R;
+        using T = Tiling<R>;
+        const size_t smem = Smem<T::BN>::FLOATS * sizeof(float);
+        static bool ready[64] = {};
+        if (!ready[e.device & 63]) {
+            allow_smem(k_forward<SID, Act>, smem);
+            ready[e.device & 63] = true;
+        }
+        const int L = n.layers;
+        for (int l = 1; l < L; ++l) {
+            const int M = n.neurons[l], K = n.neurons[l - 1];
+            const float* W = n.weights(l - 1);
+            const float* b = W + long(M) * K;
+            if (l == 1) {
+                CPDE_RUN(e, "input_forward",
+                         (k_input_forward<SID, Act><<<grid_for(long(M) * P, THREADS, 148 * 32), THREADS, 0,
+                                                      e.stream>>>(M, K, P, W, b, n.act[0].ptr, n.act[1].ptr)));
+            } else {
+                dim3 grid(unsigned((P + T::PTS - 1) / T::PTS), unsigned((M + BM - 1) / BM));
+                CPDE_RUN(e, "forward",
+                         (k_forward<SID, Act><<<grid, THREADS, smem, e.stream>>>(M, K, P, W, b, n.act[l - 1].ptr,
+                                                                                  n.act[l].ptr)));
+            }
+        }
+        const int O = n.neurons[L], K = n.neurons[L - 1];
+        const float* W = n.weights(L - 1);
+        CPDE_RUN(e, "output_forward",
+                 (k_output_forward<<<grid_for(P * R * 32, THREADS, 148 * 64), THREADS, 0, e.stream>>>(
+                     O, K, P, R, W, W + long(O) * K, n.act[L - 1].ptr, n.act[L].ptr)));
+    }
+    template <int SID>
+    void run() {
+        if (n.linear[1] == kTanhAct) layers<SID, Tanh>();
+        else layers<SID, Sigmoid>();
+    }
+};
+
+struct FastBackward {
+    Engine& e;
+    NetRecord& n;
+    long P;
+    float* target;
+    template <int SID, class Act>
+    void layers() {
+        using namespace fast;
+        constexpr int R = StaticJet<SID>::R;
+        using T = Tiling<R>;
+        const size_t smem = Smem<T::BN>::FLOATS * sizeof(float);
+        static bool ready[64] = {};
+        if (!ready[e.device & 63]) {
+            allow_smem(k_backward<SID, Act, false>, smem);
+            allow_smem(k_backward<SID, Act, true>, smem);
+            ready[e.device & 63] = true;
+        }
+        const int L = n.layers;
+        const long cols = P * R;
+        // output layer: adjoint into the last hidden layer, output weight gradient
+        {
+            const int O = n.neurons[L], K = n.neurons[L - 1];
+            const int bx = int(std::min<long>(148 * 4, (P + 1) / 2));
+            dim3 grid(bx, (K + BM - 1) / BM);
+            n.partial.reserve(size_t(bx) * O * (K + 1));
+            CPDE_RUN(e, "output_backward",
+                     (k_output_backward<SID, Act><<<grid, THREADS, 0, e.stream>>>(
+                         O, K, P, n.weights(L - 1), n.dz[0].ptr, n.act[L - 1].ptr, n.dz[1].ptr, n.partial.ptr)));
+            long size = long(O) * (K + 1);
+            CPDE_RUN(e, "sum_partials", (k_sum_partials<<<grid_for(size), 256, 0, e.stream>>>(
+                                            n.partial.ptr, bx, size, n.gradient_base(L - 1, target))));
+        }
+        float* cur = n.dz[1].ptr;
+        for (int l = L - 1; l >= 2; --l) {
+            const int M = n.neurons[l], N = n.neurons[l - 1];
+            // weight gradient of layer l (M x N plus bias), split over columns
+            const int tiles = ((N + BM - 1) / BM) * ((M + BM - 1) / BM);
+            long splits = std::max(1L, std::min<long>((2L * 148 + tiles - 1) / tiles, (cols + 1023) / 1024));
+            long per = ((cols + splits - 1) / splits + BK - 1) / BK * BK;
+            splits = (cols + per - 1) / per;
+            n.partial.reserve(size_t(splits) * M * (N + 1));
+            dim3 wg(unsigned(splits), (N + BM - 1) / BM, (M + BM - 1) / BM);
+            CPDE_RUN(e, "weight_gradient", (k_weight_gradient<<<wg, THREADS, 0, e.stream>>>(
+                                               M, N, cols, R, per, cur, n.act[l - 1].ptr, n.partial.ptr)));
+            long size = long(M) * (N + 1);
+            CPDE_RUN(e, "sum_partials", (k_sum_partials<<<grid_for(size), 256, 0, e.stream>>>(
+                                            n.partial.ptr, int(splits), size, n.gradient_base(l - 1, target))));
+            // adjoint into layer l-1
+            const float* W = n.weights(l - 1);
+            const long tiles_p = (P + T::PTS - 1) / T::PTS;
+            if (l - 1 == 1) {
+                const int K0 = n.neurons[0];
+                const int bx = int(std::min<long>(tiles_p, 148 * 2));
+                dim3 grid(bx, (N + BM - 1) / BM);
+                n.input_partial.reserve(size_t(bx) * N * (K0 + 1));
+                CPDE_RUN(e, "backward_input",
+                         (k_backward<SID, Act, true><<<grid, THREADS, smem, e.stream>>>(
+                             N, M, P, W, cur, n.act[1].ptr, nullptr, n.act[0].ptr, K0, n.input_partial.ptr)));
+                long isize = long(N) * (K0 + 1);
+                CPDE_RUN(e, "sum_partials", (k_sum_partials<<<grid_for(isize), 256, 0, e.stream>>>(
+                                                n.input_partial.ptr, bx, isize, n.gradient_base(0, target))));
+            } else {
+                float* next = cur == n.dz[0].ptr ? n.dz[1].ptr : n.dz[0].ptr;
+                const int bx = int(std::min<long>(tiles_p, 148 * 8));
+                dim3 grid(bx, (N + BM - 1) / BM);
+                CPDE_RUN(e, "backward",
+                         (k_backward<SID, Act, false><<<grid, THREADS, smem, e.stream>>>(
+                             N, M, P, W, cur, n.act[l - 1].ptr, next, nullptr, 0, nullptr)));
+                cur = next;
+            }
+        }
+    }
+    template <int SID>
+    void run() {
+        if (n.linear[1] == kTanhAct) layers<SID, Tanh>();
+        else layers<SID, Sigmoid>();
+    }
+};
+}  // namespace
+
+void Engine::fast_forward(NetRecord& n, Context& ctx, int points) {
+    with_schema(ctx.static_id, FastForward{*this, n, points});
+}
+
+void Engine::fast_backward(NetRecord& n, Context& ctx, int points, float* target) {
+    with_schema(ctx.static_id, FastBackward{*this, n, points, target});
 }
 
 void Engine::run_cost(NetRecord& n, CostRecord& c, int cost_index, int points, int offset, bool collect,
@@ -449,6 +627,8 @@ void Engine::pass(NetRecord& n, CostRecord& c, int cost_index, bool bwd, bool co
     require(begin >= 0 && begin % c.width == 0 && (!reuse_forward || long(end) - begin <= c.width),
             "invalid cost pass range");
     Context& ctx = *c.context;
+    require(n.capacity >= long(c.width) * long(c.rows.size()) && n.dz[0].ptr && n.cost_totals.ptr,
+            "internal error: network storage was not prepared for this cost");
     for (int offset = begin; offset < end; offset += c.width) {
         int valid = std::min(c.width, input.w - offset);
         if (reuse_forward) {
@@ -1274,6 +1454,7 @@ Payload Engine::graph_evaluate(Payload& b) {
 // One fixed-weight epoch without synchronisation (op 90's step).
 void Engine::epoch(uint64_t ni, const std::vector<uint64_t>& ids) {
     auto& n = net(ni);
+    prepare_costs(n, ids, ni, true);
     begin_costs(n, int(ids.size()));
     for (int l = 0; l < n.layers; ++l) CPDE_CUDA(cudaMemsetAsync(n.gradient(l), 0, n.count[l] * 4, stream));
     for (size_t i = 0; i < ids.size(); ++i)

@@ -15,6 +15,7 @@
 
 #include "common.hpp"
 #include "expression.hpp"
+#include "kernels_fast.cuh"
 #include "kernels_generic.cuh"
 #include "scalar.hpp"
 #include "schema.hpp"
@@ -40,6 +41,7 @@ struct Context {
     std::vector<int> rows;  // data-table rows in propagation order
     JetPlan plan;
     bool planned = false;
+    int static_id = -1;  // generated register-resident jet code for exactly these rows, if any
     DeviceBuffer<int> rows_dev;
     DeviceBuffer<int> tables;
     int R() const { return int(rows.size()); }
@@ -96,7 +98,7 @@ struct NetRecord {
     long capacity = 0;
     std::vector<DeviceBuffer<float>> act;  // act[l]: A_l (l < L) or Z_L
     std::vector<DeviceBuffer<float>> pre;  // pre[l]: Z_l of nonlinear layers
-    DeviceBuffer<float> dz[2], dy, jet_scratch, partial;
+    DeviceBuffer<float> dz[2], dy, jet_scratch, partial, input_partial;
     DeviceBuffer<float> eval_gradient;  // gradient target of op 14 (keeps history intact)
 
     // which chunk's forward is resident (cuda/cpde_server.cu:163)
@@ -182,6 +184,9 @@ class Engine {
     void activate(NetRecord& n, uint64_t data_id, Context& ctx, int width, int offset, int valid);
     void forward(NetRecord& n, Context& ctx, int points);
     void backward(NetRecord& n, Context& ctx, int points, float* target);
+    bool fast_ok(NetRecord& n, Context& ctx) const;
+    void fast_forward(NetRecord& n, Context& ctx, int points);
+    void fast_backward(NetRecord& n, Context& ctx, int points, float* target);
     void run_cost(NetRecord& n, CostRecord& c, int cost_index, int points, int offset, bool collect, bool gradient,
                   const double* multiplier);
     void pass(NetRecord& n, CostRecord& c, int cost_index, bool backward, bool collect, const double* multiplier,

@@ -1,0 +1,502 @@
+// Fast tier: fused kernels for networks whose hidden widths are multiples of
+// 32 and whose derivative schema has register-resident jet code
+// (generated/jets_static.cuh).
+//
+// Every GEMM tile covers 128 neurons x Pt whole points, i.e. Pt*R adjacent
+// columns of the interleaved activation layout, so the epilogue owns all R
+// derivative rows of each (neuron, point) and applies the jet combine (forward)
+// or its adjoint (backward) in registers before a single coalesced store.
+// The reference instead runs one launch per derivative row for the combine
+// and another for the adjoint (cuda/cpde_engine.cuh:852-866,973).
+#pragma once
+#include "generated/jets_static.cuh"
+#include "kernels_generic.cuh"
+
+namespace cpde {
+namespace fast {
+
+constexpr int THREADS = 256;
+constexpr int BM = 128;  // neurons per tile
+constexpr int BK = 16;   // K slab
+
+// Points per tile and padded column count for R derivative rows: as many whole
+// points as fit in 128 columns, rounded up to a multiple of 16 columns.
+template <int R>
+struct Tiling {
+    static constexpr int PTS = (128 / R) > 0 ? (128 / R) : 1;
+    static constexpr int COLS = PTS * R;
+    static constexpr int BN = ((COLS + 15) / 16) * 16;
+    static constexpr int TN = BN / 16;  // columns per thread
+};
+
+// Shared memory of the GEMM main loop, reused by the epilogue as a Z tile.
+template <int BN>
+struct Smem {
+    static constexpr int LDA = BM + 4, LDB = BN + 4, LDZ = BM + 4;
+    static constexpr int MAIN = 2 * BK * LDA + 2 * BK * LDB;
+    static constexpr int EPI = BN * LDZ;
+    static constexpr int FLOATS = MAIN > EPI ? MAIN : EPI;
+};
+
+// ---------------------------------------------------------------------------
+// Main loop: acc[8][TN] += A (128 x K) * B (K x BN); thread (ty, tx) owns rows
+// ty*8..ty*8+7 and columns tx + 16 j. A and B slabs are staged through
+// registers so the next slab's global loads overlap the current FMAs.
+//   A loader: a(m, k) for m < 128, k < K (zero outside)
+//   B loader: b4(c, k4) returns float4 of b(k4*4 .. k4*4+3, c) (zero outside)
+
+template <int BN, class ALoad, class BLoad>
+__device__ __forceinline__ void gemm_main(float (&acc)[8][BN / 16], float* smem, int K, const ALoad& aload,
+                                          const BLoad& bload) {
+    using S = Smem<BN>;
+    constexpr int TN = BN / 16;
+    float* As = smem;                   // [2][BK][LDA]
+    float* Bs = smem + 2 * BK * S::LDA;  // [2][BK][LDB]
+    const int t = threadIdx.x, tx = t & 15, ty = t >> 4;
+    // A slab: 16 x 128 = 2048 values, 8 per thread: k = t/16 (0..15), m = (t%16)*8 + i
+    constexpr int BLOADS = (BN * 4 + THREADS - 1) / THREADS;  // float4 loads of the B slab per thread
+    float ra[8];
+    float4 rb[BLOADS];
+    auto fetch = [&](int k0) {
+        const int k = t >> 4, m0 = (t & 15) * 8;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ra[i] = aload(m0 + i, k0 + k);
+#pragma unroll
+        for (int j = 0; j < BLOADS; ++j) {
+            int idx = t + j * THREADS;  // (column, k-quad)
+            int c = idx >> 2, q = idx & 3;
+            rb[j] = c < BN ? bload(c, (k0 >> 2) + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    };
+    auto store = [&](int buf) {
+        float* a = As + buf * BK * S::LDA;
+        float* b = Bs + buf * BK * S::LDB;
+        const int k = t >> 4, m0 = (t & 15) * 8;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) a[k * S::LDA + m0 + i] = ra[i];
+#pragma unroll
+        for (int j = 0; j < BLOADS; ++j) {
+            int idx = t + j * THREADS;
+            int c = idx >> 2, q = idx & 3;
+            if (c < BN) {
+                b[(4 * q + 0) * S::LDB + c] = rb[j].x;
+                b[(4 * q + 1) * S::LDB + c] = rb[j].y;
+                b[(4 * q + 2) * S::LDB + c] = rb[j].z;
+                b[(4 * q + 3) * S::LDB + c] = rb[j].w;
+            }
+        }
+    };
+    const int slabs = (K + BK - 1) / BK;
+    fetch(0);
+    store(0);
+    __syncthreads();
+    for (int s = 0; s < slabs; ++s) {
+        const int buf = s & 1;
+        if (s + 1 < slabs) fetch((s + 1) * BK);
+        const float* a = As + buf * BK * S::LDA;
+        const float* b = Bs + buf * BK * S::LDB;
+#pragma unroll
+        for (int k = 0; k < BK; ++k) {
+            const float4 a0 = *reinterpret_cast<const float4*>(a + k * S::LDA + ty * 8);
+            const float4 a1 = *reinterpret_cast<const float4*>(a + k * S::LDA + ty * 8 + 4);
+            const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            float bv[TN];
+#pragma unroll
+            for (int j = 0; j < TN; ++j) bv[j] = b[k * S::LDB + tx + 16 * j];
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+#pragma unroll
+                for (int j = 0; j < TN; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+        }
+        if (s + 1 < slabs) {
+            store(buf ^ 1);
+            __syncthreads();
+        }
+    }
+    __syncthreads();  // smem is reused by the epilogue
+}
+
+template <int BN>
+__device__ __forceinline__ void stage_tile(const float (&acc)[8][BN / 16], float* smem) {
+    using S = Smem<BN>;
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+#pragma unroll
+    for (int j = 0; j < BN / 16; ++j) {
+        float* z = smem + (tx + 16 * j) * S::LDZ + ty * 8;
+        *reinterpret_cast<float4*>(z) = make_float4(acc[0][j], acc[1][j], acc[2][j], acc[3][j]);
+        *reinterpret_cast<float4*>(z + 4) = make_float4(acc[4][j], acc[5][j], acc[6][j], acc[7][j]);
+    }
+    __syncthreads();
+}
+
+// Column loader of an interleaved activation matrix (K rows per column).
+struct ColumnLoad {
+    const float* base;  // first column of the tile
+    int K;
+    long columns;  // valid columns from base
+    __device__ float4 operator()(int c, int k4) const {
+        if (c >= columns || k4 * 4 >= K) return make_float4(0.f, 0.f, 0.f, 0.f);
+        return __ldg(reinterpret_cast<const float4*>(base + (size_t)c * K) + k4);
+    }
+};
+
+// ---------------------------------------------------------------------------
+// Hidden layer forward: Y = f(W X + b) with the jet combine in the epilogue.
+// grid = (ceil(P / PTS), ceil(M / 128)). Requires K % 4 == 0.
+
+template <int SID, class Act>
+__global__ void __launch_bounds__(THREADS, 2) k_forward(int M, int K, long P, const float* __restrict__ W,
+                                                     const float* __restrict__ bias, const float* __restrict__ X,
+                                                     float* __restrict__ Y) {
+    constexpr int R = StaticJet<SID>::R;
+    using T = Tiling<R>;
+    using S = Smem<T::BN>;
+    extern __shared__ float4 smem4[];
+    float* smem = reinterpret_cast<float*>(smem4);
+    const long p0 = (long)blockIdx.x * T::PTS;
+    const int m_base = blockIdx.y * BM;
+    const long points = min((long)T::PTS, P - p0);
+    float acc[8][T::TN] = {};
+    auto aload = [&](int m, int k) -> float {
+        int mm = m_base + m;
+        return (mm < M && k < K) ? __ldg(W + mm + (size_t)k * M) : 0.f;
+    };
+    ColumnLoad bload{X + (size_t)p0 * R * K, K, points * R};
+    gemm_main<T::BN>(acc, smem, K, aload, bload);
+    stage_tile<T::BN>(acc, smem);
+    for (int e = threadIdx.x; e < BM * T::PTS; e += THREADS) {
+        const int m = e % BM, p = e / BM;
+        const int mm = m_base + m;
+        if (p >= points || mm >= M) continue;
+        float z[R], y[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) z[r] = smem[(p * R + r) * S::LDZ + m];
+        z[0] += __ldg(bias + mm);
+        StaticJet<SID>::template forward<Act>(z, y);
+        float* out = Y + ((size_t)(p0 + p) * R) * M + mm;
+#pragma unroll
+        for (int r = 0; r < R; ++r) out[(size_t)r * M] = y[r];
+    }
+}
+
+// First hidden layer: Y = f(W X + b) for a narrow input (K <= 8); one thread
+// per (neuron, point). Memory-bound on the store of Y.
+template <int SID, class Act>
+__global__ void __launch_bounds__(THREADS) k_input_forward(int M, int K, long P, const float* __restrict__ W,
+                                                           const float* __restrict__ bias,
+                                                           const float* __restrict__ X, float* __restrict__ Y) {
+    constexpr int R = StaticJet<SID>::R;
+    const long total = (long)M * P;
+    for (long e = blockIdx.x * (long)blockDim.x + threadIdx.x; e < total; e += (long)blockDim.x * gridDim.x) {
+        const int m = int(e % M);
+        const long p = e / M;
+        float w[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) w[k] = k < K ? __ldg(W + m + (size_t)k * M) : 0.f;
+        const float* x = X + (size_t)p * R * K;
+        float z[R], y[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            float acc = 0.f;
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+                if (k < K) acc = fmaf(w[k], __ldg(x + r * K + k), acc);
+            z[r] = acc;
+        }
+        z[0] += __ldg(bias + m);
+        StaticJet<SID>::template forward<Act>(z, y);
+        float* out = Y + (size_t)p * R * M + m;
+#pragma unroll
+        for (int r = 0; r < R; ++r) out[(size_t)r * M] = y[r];
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Hidden layer backward: dZ_prev = adjoint(W^T dZ; Y_prev) with the jet
+// adjoint in the epilogue. M = width of the previous layer, K = this layer's.
+// With INPUT_GRAD the previous layer is the first hidden layer: its weight
+// gradient partial (M x (K0+1) with K0 input channels, bias last) is
+// accumulated per CTA and dZ_prev is not stored.
+
+template <int SID, class Act, bool INPUT_GRAD>
+__global__ void __launch_bounds__(THREADS, 2) k_backward(int M, int K, long P, const float* __restrict__ W,
+                                                      const float* __restrict__ dZ, const float* __restrict__ Yprev,
+                                                      float* __restrict__ dZprev, const float* __restrict__ X0,
+                                                      int K0, float* __restrict__ input_partials) {
+    constexpr int R = StaticJet<SID>::R;
+    using T = Tiling<R>;
+    using S = Smem<T::BN>;
+    extern __shared__ float4 smem4[];
+    float* smem = reinterpret_cast<float*>(smem4);
+    const int m_base = blockIdx.y * BM;
+    // INPUT_GRAD: up to 8 input channels + bias of this thread's neuron (every
+    // role of a thread has the same neuron because THREADS is a multiple of BM)
+    float gacc[9];
+#pragma unroll
+    for (int b = 0; b < 9; ++b) gacc[b] = 0.f;
+    // Grid-stride over point tiles so INPUT_GRAD partials stay per CTA.
+    for (long tile = blockIdx.x; tile * T::PTS < P; tile += gridDim.x) {
+        const long p0 = tile * T::PTS;
+        const long points = min((long)T::PTS, P - p0);
+        float acc[8][T::TN] = {};
+        // A = W^T: a(m, k) = W[k + m*K] (W is K x M column-major)
+        auto aload = [&](int m, int k) -> float {
+            int mm = m_base + m;
+            return (mm < M && k < K) ? __ldg(W + k + (size_t)mm * K) : 0.f;
+        };
+        ColumnLoad bload{dZ + (size_t)p0 * R * K, K, points * R};
+        gemm_main<T::BN>(acc, smem, K, aload, bload);
+        stage_tile<T::BN>(acc, smem);
+        for (int e = threadIdx.x; e < BM * T::PTS; e += THREADS) {
+            const int m = e % BM, p = e / BM;
+            const int mm = m_base + m;
+            if (p >= points || mm >= M) continue;
+            float g[R], y[R];
+            const float* yp = Yprev + ((size_t)(p0 + p) * R) * M + mm;
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                g[r] = smem[(p * R + r) * S::LDZ + m];
+                y[r] = yp[(size_t)r * M];
+            }
+            StaticJet<SID>::template adjoint<Act>(y, g);
+            if (INPUT_GRAD) {
+                const float* x = X0 + (size_t)(p0 + p) * R * K0;
+#pragma unroll
+                for (int r = 0; r < R; ++r) {
+#pragma unroll
+                    for (int k = 0; k < 8; ++k)
+                        if (k < K0) gacc[k] = fmaf(g[r], __ldg(x + r * K0 + k), gacc[k]);
+                }
+                gacc[8] += g[0];
+            } else {
+                float* out = dZprev + ((size_t)(p0 + p) * R) * M + mm;
+#pragma unroll
+                for (int r = 0; r < R; ++r) out[(size_t)r * M] = g[r];
+            }
+        }
+        __syncthreads();
+    }
+    if (INPUT_GRAD) {
+        // Fold this thread's roles into per-neuron sums in smem, then store the
+        // CTA partial: input_partials[cta][m][k], k = 0..K0 (bias last).
+        float* red = smem;  // [BM][9]
+        for (int i = threadIdx.x; i < BM * 9; i += THREADS) red[i] = 0.f;
+        __syncthreads();
+        const int m = threadIdx.x % BM;
+        for (int turn = 0; turn < THREADS / BM; ++turn) {
+            if (threadIdx.x / BM == turn)
+#pragma unroll
+                for (int k = 0; k < 9; ++k) red[m * 9 + k] += gacc[k];
+            __syncthreads();
+        }
+        // partial of CTA column x: full M x (K0+1) column-major; y-blocks write disjoint neuron slices
+        float* out = input_partials + (size_t)blockIdx.x * M * (K0 + 1);
+        for (int i = threadIdx.x; i < BM * (K0 + 1); i += THREADS) {
+            int ml = i % BM, k = i / BM;
+            if (m_base + ml < M) out[(m_base + ml) + (size_t)k * M] = red[ml * 9 + (k == K0 ? 8 : k)];
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Weight gradient of a hidden layer, split over columns: each CTA sums
+// dZ[:, c] A[:, c]^T over its column range into a 128 x 128 tile (plus the
+// bias column: sum of dZ over value-row columns) and stores a partial
+// partials[cta][m + n*M] (n = N is the bias). grid = (splits, ceil(N/128),
+// ceil(M/128)).
+
+__global__ void __launch_bounds__(THREADS, 2) k_weight_gradient(int M, int N, long columns, int R, long per_split,
+                                                             const float* __restrict__ dZ,
+                                                             const float* __restrict__ A,
+                                                             float* __restrict__ partials) {
+    constexpr int LD = BM + 4;
+    __shared__ __align__(16) float As[2][BK][LD];  // dZ slab: [k = column][m]
+    __shared__ __align__(16) float Bs[2][BK][LD];  // A slab:  [k = column][n]
+    const int t = threadIdx.x, tx = t & 15, ty = t >> 4;
+    const int n_base = blockIdx.y * BM, m_base = blockIdx.z * BM;
+    const long c_begin = (long)blockIdx.x * per_split;
+    const long c_end = min(columns, c_begin + per_split);
+    float acc[8][8] = {};
+    float bias_acc = 0.f;  // thread t < 128: neuron m_base + t
+    float4 ra[2], rb[2];
+    // slab loads: 16 columns x 128 rows = 512 float4; thread loads 2 of each
+    auto fetch = [&](long c0) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            int idx = t + j * THREADS;
+            int c = idx >> 5, r4 = idx & 31;  // column in slab, float4 index along rows
+            long col = c0 + c;
+            bool ok = col < c_end;
+            int m = m_base + r4 * 4, n = n_base + r4 * 4;
+            ra[j] = ok && m < M ? __ldg(reinterpret_cast<const float4*>(dZ + (size_t)col * M + m))
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+            rb[j] = ok && n < N ? __ldg(reinterpret_cast<const float4*>(A + (size_t)col * N + n))
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    };
+    auto store = [&](int buf) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            int idx = t + j * THREADS;
+            int c = idx >> 5, r4 = idx & 31;
+            *reinterpret_cast<float4*>(&As[buf][c][r4 * 4]) = ra[j];
+            *reinterpret_cast<float4*>(&Bs[buf][c][r4 * 4]) = rb[j];
+        }
+    };
+    if (c_begin < c_end) {
+        fetch(c_begin);
+        store(0);
+        __syncthreads();
+        int buf = 0;
+        for (long c0 = c_begin; c0 < c_end; c0 += BK) {
+            const bool more = c0 + BK < c_end;
+            if (more) fetch(c0 + BK);
+#pragma unroll
+            for (int k = 0; k < BK; ++k) {
+                const float4 a0 = *reinterpret_cast<const float4*>(&As[buf][k][ty * 8]);
+                const float4 a1 = *reinterpret_cast<const float4*>(&As[buf][k][ty * 8 + 4]);
+                const float4 b0 = *reinterpret_cast<const float4*>(&Bs[buf][k][tx * 8]);
+                const float4 b1 = *reinterpret_cast<const float4*>(&Bs[buf][k][tx * 8 + 4]);
+                const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+                const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+            }
+            if (blockIdx.y == 0 && t < BM) {
+                // value-row columns of this slab carry the bias gradient
+                long first = ((c0 + R - 1) / R) * R;
+                for (long c = first; c < c0 + BK && c < c_end; c += R) bias_acc += As[buf][c - c0][t];
+            }
+            if (more) {
+                __syncthreads();
+                store(buf ^ 1);
+                __syncthreads();
+                buf ^= 1;
+            }
+        }
+    }
+    float* out = partials + (size_t)blockIdx.x * M * (N + 1);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        int m = m_base + ty * 8 + i;
+        if (m >= M) continue;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            int n = n_base + tx * 8 + j;
+            if (n < N) out[m + (size_t)n * M] = acc[i][j];
+        }
+    }
+    if (blockIdx.y == 0 && t < BM && m_base + t < M) out[m_base + t + (size_t)N * M] = bias_acc;
+}
+
+// ---------------------------------------------------------------------------
+// Output layer (n_out <= 8 linear outputs): Z_out[o, p, r] = W_out Y + b.
+// One warp per (point, row) column group: lanes split the K inputs.
+
+__global__ void k_output_forward(int O, int K, long P, int R, const float* __restrict__ W,
+                                 const float* __restrict__ bias, const float* __restrict__ Y,
+                                 float* __restrict__ Z) {
+    const int lane = threadIdx.x & 31;
+    const long warps = ((long)gridDim.x * blockDim.x) >> 5;
+    const long columns = P * R;
+    for (long c = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5; c < columns; c += warps) {
+        const float* y = Y + (size_t)c * K;
+        float acc[8];
+#pragma unroll
+        for (int o = 0; o < 8; ++o) acc[o] = 0.f;
+        for (int k = lane; k < K; k += 32) {
+            const float v = __ldg(y + k);
+#pragma unroll
+            for (int o = 0; o < 8; ++o)
+                if (o < O) acc[o] = fmaf(__ldg(W + o + (size_t)k * O), v, acc[o]);
+        }
+#pragma unroll
+        for (int o = 0; o < 8; ++o) {
+            if (o >= O) break;
+            float v = acc[o];
+            for (int s = 16; s; s >>= 1) v += __shfl_xor_sync(0xffffffffu, v, s);
+            if (lane == 0) Z[(size_t)c * O + o] = v + ((c % R) == 0 ? __ldg(bias + o) : 0.f);
+        }
+    }
+}
+
+// Output layer backward: dY = W_out^T dZ_out, adjoint with Y -> dZ of the
+// last hidden layer; weight gradient of the output layer accumulated per CTA
+// (partials[cta][o + k*O], bias at k = K). One thread per (neuron, point).
+template <int SID, class Act>
+__global__ void __launch_bounds__(THREADS) k_output_backward(int O, int K, long P, const float* __restrict__ W,
+                                                             const float* __restrict__ dZout,
+                                                             const float* __restrict__ Y, float* __restrict__ dZ,
+                                                             float* __restrict__ partials) {
+    constexpr int R = StaticJet<SID>::R;
+    __shared__ float red[8][BM + 1];
+    float gw[8];
+#pragma unroll
+    for (int o = 0; o < 8; ++o) gw[o] = 0.f;
+    float gb[8];
+#pragma unroll
+    for (int o = 0; o < 8; ++o) gb[o] = 0.f;
+    // blocks own neuron slices of 128 (blockIdx.y) and stride over points
+    const int m = blockIdx.y * BM + (threadIdx.x % BM);
+    const int lane_p = threadIdx.x / BM;  // 0..1
+    const bool active = m < K;
+    float w[8];
+#pragma unroll
+    for (int o = 0; o < 8; ++o) w[o] = (o < O && active) ? __ldg(W + o + (size_t)m * O) : 0.f;
+    for (long p = (long)blockIdx.x * 2 + lane_p; p < P; p += (long)gridDim.x * 2) {
+        if (!active) continue;
+        const float* dzo = dZout + (size_t)p * R * O;
+        const float* yp = Y + (size_t)p * R * K + m;
+        float g[R], y[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            y[r] = yp[(size_t)r * K];
+            float acc = 0.f;
+#pragma unroll
+            for (int o = 0; o < 8; ++o)
+                if (o < O) {
+                    const float d = __ldg(dzo + r * O + o);
+                    acc = fmaf(w[o], d, acc);
+                    gw[o] = fmaf(d, y[r], gw[o]);
+                    if (r == 0) gb[o] += d;
+                }
+            g[r] = acc;
+        }
+        StaticJet<SID>::template adjoint<Act>(y, g);
+        float* out = dZ + (size_t)p * R * K + m;
+#pragma unroll
+        for (int r = 0; r < R; ++r) out[(size_t)r * K] = g[r];
+    }
+    // fold the two point-lanes of each neuron
+    for (int o = 0; o < 8; ++o) {
+        if (o >= O) break;
+        if (lane_p == 1) red[o][threadIdx.x % BM] = gw[o];
+        __syncthreads();
+        if (lane_p == 0) gw[o] += red[o][threadIdx.x % BM];
+        __syncthreads();
+    }
+    // partial of CTA column x: full O x (K+1) column-major; y-blocks write disjoint neuron slices
+    float* out = partials + (size_t)blockIdx.x * O * (K + 1);
+    if (lane_p == 0 && active)
+        for (int o = 0; o < O; ++o) out[o + (size_t)m * O] = gw[o];
+    // bias: every neuron thread saw the same output adjoints; use neuron 0's two point lanes
+    if (blockIdx.y == 0 && threadIdx.x == BM)
+        for (int o = 0; o < O; ++o) red[o][0] = gb[o];
+    __syncthreads();
+    if (blockIdx.y == 0 && threadIdx.x == 0)
+        for (int o = 0; o < O; ++o) out[o + (size_t)K * O] = gb[o] + red[o][0];
+}
+
+// Sum CTA partials (fixed order) into a layer gradient (accumulating).
+__global__ void k_sum_partials(const float* __restrict__ partials, int count, long size, float* __restrict__ out) {
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < size; i += (long)blockDim.x * gridDim.x) {
+        float acc = 0.f;
+        for (int c = 0; c < count; ++c) acc += partials[(size_t)c * size + i];
+        out[i] += acc;
+    }
+}
+
+}  // namespace fast
+}  // namespace cpde

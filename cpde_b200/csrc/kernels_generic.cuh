@@ -204,7 +204,7 @@ k_gemm(int M, int N, int K, const float* __restrict__ A, int lda, const float* _
     __shared__ float As[BK][BM + 4];
     __shared__ float Bs[BK][BN + 4];
     const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
-    const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
+    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;  // N tiles on x: no 65535 limit
     const long k_begin = (long)blockIdx.z * k_per_split;
     const long k_end = min((long)K, k_begin + k_per_split);
     float acc[4][4] = {};

@@ -202,9 +202,14 @@ def split_layer(flat, width, height):
     return flat[:width * height].reshape((height, width), order='F'), flat[width * height:]
 
 
+ACTIVATIONS = {0: 'sigmoid', 2: 'tanh'}
+
+
 def forward(schema, weights, layers, linear, x, activation='sigmoid'):
     """Jets of every layer. ``x`` has shape (R, n0, P). Returns the list of
-    pre-activations Z_l (l >= 1) and post-activation jets A_l (A_0 = x)."""
+    pre-activations Z_l (l >= 1) and post-activation jets A_l (A_0 = x).
+    Layer flags: 1 linear, 0 sigmoid, 2 tanh (tanh is an extension: the
+    reference knows only 0 and 1, cuda/cpde_server.cu:457)."""
     acts = [np.asarray(x, np.float64)]
     pre = [None]
     for l in range(1, len(layers)):
@@ -212,10 +217,10 @@ def forward(schema, weights, layers, linear, x, activation='sigmoid'):
         z = np.einsum('mk,rkp->rmp', w, acts[-1])
         z[0] += b[:, None]
         pre.append(z)
-        if linear[l]:
+        if linear[l] == 1:
             acts.append(z)
         else:
-            acts.append(jet_forward(schema, z, activation))
+            acts.append(jet_forward(schema, z, ACTIVATIONS.get(linear[l], activation)))
     return pre, acts
 
 
@@ -231,7 +236,8 @@ def backward(schema, weights, layers, linear, pre, acts, dout, activation='sigmo
         if l == 1:
             break
         dy = np.einsum('mk,rmp->rkp', w, dz)
-        dz = dy if linear[l - 1] else jet_adjoint(schema, pre[l - 1], dy, activation)
+        dz = dy if linear[l - 1] == 1 else jet_adjoint(schema, pre[l - 1], dy,
+                                                        ACTIVATIONS.get(linear[l - 1], activation))
     return grads
 
 

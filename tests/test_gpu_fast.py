@@ -1,0 +1,95 @@
+"""Fast-tier kernels (fused GEMM + register jets) against the oracle and the
+generic tier, for every schema with generated jet code. B200 only.
+
+Tolerances: per-row normwise relative error of outputs and per-layer normwise
+relative error of weight gradients vs the float64 oracle, 1e-5 for orders <= 3
+and 1e-4 for orders 4-6 (same rule as tests/golden_cases.py)."""
+import numpy as np
+import pytest
+
+import golden_cases as gc
+from cpde_b200 import codegen, native
+from cpde_b200.client import sum_graph
+from cpde_b200.expressions import quadrature_inputs
+from oracle import jets
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope='module')
+def engine():
+    with native.Engine(0) as e:
+        yield e
+
+
+def schema_table(rows):
+    return np.array([(sum(r), *r) for r in rows], np.int32)
+
+
+def setup(engine, rows, layers, linear, points, seed):
+    rng = np.random.default_rng(seed)
+    t = schema_table(rows)
+    V = t.shape[1] - 1
+    pts = rng.uniform(-1, 1, (points, V))
+    x = quadrature_inputs(pts, t)
+    x[2 * V + 1:] = rng.normal(size=x[2 * V + 1:].shape) * 0.1 if len(t) > 2 * V + 1 else x[2 * V + 1:]
+    weights = [(rng.normal(size=h * (w + 1)) * (1.0 / np.sqrt(w))).astype(np.float32)
+               for w, h in zip(layers[:-1], layers[1:])]
+    net = engine.network(layers, weights, linear)
+    data = engine.data(x, t)
+    return t, x, weights, net, data
+
+
+CASES = [(sid, name, rows) for sid, (name, rows) in enumerate(codegen.SCHEMAS)]
+
+
+@pytest.mark.parametrize('sid,name,rows', CASES, ids=[c[1] for c in CASES])
+@pytest.mark.parametrize('act', [0, 2], ids=['sigmoid', 'tanh'])
+def test_fast_tier_matches_oracle(engine, sid, name, rows, act):
+    V = len(rows[0])
+    layers = [V, 64, 32, 64, 2]
+    linear = [1, act, act, act, 1]
+    P = 203  # not a multiple of any tile's point count
+    t, x, weights, net, data = setup(engine, rows, layers, linear, P, sid + 10 * act)
+    out = engine.download(engine.evaluate(net, data, chunk=97))
+    schema = jets.Schema(t[:, 1:])
+    pre, acts = jets.forward(schema, weights, layers, linear, x)
+    tol = gc.tolerance(t)
+    assert gc.rowwise_error(out, acts[-1]).max() < tol
+    targets = (acts[-1] * 0.5).astype(np.float32)
+    tgt = engine.data(targets, t)
+    R = len(t)
+    mw = np.random.default_rng(1).uniform(0.5, 1.5, (R, 1, 2)).astype(np.float32)
+    cost = engine.matching(net, data, tgt, list(range(R)), list(range(R)), 1, mw, chunk=120)
+    value, grads = engine.graph_evaluate(net, [cost], sum_graph(1))
+    loss, dout = jets.matching(acts[-1], targets, mw.transpose(0, 2, 1))
+    expected = jets.backward(schema, weights, layers, linear, pre, acts, dout)
+    assert abs(value - loss) <= tol * abs(loss)
+    assert gc.layer_error(grads, expected) < tol
+    engine.set_tier(1)
+    try:
+        gen_value, gen_grads = engine.graph_evaluate(net, [cost], sum_graph(1))
+    finally:
+        engine.set_tier(0)
+    assert abs(value - gen_value) <= tol * abs(gen_value)
+    assert gc.layer_error(grads, gen_grads) < tol
+
+
+def test_fast_tier_wide_layers_and_single_output(engine):
+    """Config-style shapes: 2 -> 256 -> 128 -> 256 -> 1, order 4, many points."""
+    rows = codegen.SCHEMAS[4][1]
+    layers = [2, 256, 128, 256, 1]
+    linear = [1, 0, 0, 0, 1]
+    t, x, weights, net, data = setup(engine, rows, layers, linear, 1500, 3)
+    schema = jets.Schema(t[:, 1:])
+    pre, acts = jets.forward(schema, weights, layers, linear, x)
+    out = engine.download(engine.evaluate(net, data))
+    assert gc.rowwise_error(out, acts[-1]).max() < 1e-4
+    R = len(t)
+    tgt = engine.data(np.zeros_like(out), t)
+    cost = engine.matching(net, data, tgt, list(range(R)), list(range(R)), 1, np.ones((R, 1, 1), np.float32))
+    value, grads = engine.graph_evaluate(net, [cost], sum_graph(1))
+    loss, dout = jets.matching(acts[-1], np.zeros_like(out), 1.0)
+    expected = jets.backward(schema, weights, layers, linear, pre, acts, dout)
+    assert abs(value - loss) <= 1e-4 * loss
+    assert gc.layer_error(grads, expected) < 1e-4
