@@ -232,8 +232,12 @@ def run_b200(args):
     peaks, source = measured_peaks()
     launches = sum(v[0] for v in kernels.values()) // args.steps
     top = max(kernels.items(), key=lambda kv: kv[1][1])
-    # Algorithmic FLOPs per class: 'gemm' carries forward and input-gradient GEMMs.
-    class_flops = {'gemm': fwd + dgrad, 'gemm_wgrad': wgrad}
+    # Algorithmic FLOPs per kernel class and step (hidden 128 x 128 layers):
+    # 'forward' = layers 2..4, 'backward'/'backward_input' = input-gradient GEMMs
+    # of layers 4,3 / 2, 'weight_gradient' = layers 4..2 (bias column included).
+    hidden = 2 * 128 * 128 * args.points * R
+    class_flops = {'gemm': fwd + dgrad, 'gemm_wgrad': wgrad, 'forward': 3 * hidden, 'backward': 2 * hidden,
+                   'backward_input': hidden, 'weight_gradient': 3 * 2 * 128 * 129 * args.points * R}
     flops = class_flops.get(top[0])
     fp32_peak = 148 * 128 * 2 * (clock['sm_max_mhz'] if clock and clock['sm_max_mhz'] else 1965.0) / 1e6
     roofline = None
