@@ -1,3 +1,4 @@
 // Single translation unit of libcpde_b200.so: the engine and its C ABI.
 #include "engine.cu"
 #include "capi.cu"
+#include "noalloc.cu"

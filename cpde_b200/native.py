@@ -56,6 +56,7 @@ SIGNATURES = {
     'cpde_kernel_timing_report': (I32, [P, SINK, P]),
     'cpde_set_tier': (I32, [P, I32]),
     'cpde_jet_plan': (I32, [PI32, I32, I32, PI32, SZ, ctypes.POINTER(SZ)]),
+    'cpde_layer_gradient_static': (I32, [P, P, P, I32, I32, ctypes.c_int64, I32, P, P]),
 }
 
 
