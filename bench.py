@@ -171,6 +171,7 @@ def run_b200(args):
         dist.init_process_group('nccl', timeout=timedelta(seconds=120), device_id=torch.device('cuda', local))
     from cpde_b200 import native
     engine = native.Engine(local)
+    engine.set_tier(args.tier)
     t, x, targets, weights = workload(args.points)
     net = engine.network(LAYERS, weights)
     inp = engine.data(x, t)
@@ -236,7 +237,9 @@ def run_b200(args):
     # 'forward' = layers 2..4, 'backward'/'backward_input' = input-gradient GEMMs
     # of layers 4,3 / 2, 'weight_gradient' = layers 4..2 (bias column included).
     hidden = 2 * 128 * 128 * args.points * R
-    class_flops = {'gemm': fwd + dgrad, 'gemm_wgrad': wgrad, 'forward': 3 * hidden, 'backward': 2 * hidden,
+    class_flops = {'gemm': fwd + dgrad, 'gemm_wgrad': wgrad, 'forward': 3 * hidden, 'forward_tc': 3 * hidden,
+                   'backward': 2 * hidden, 'backward_tc': 2 * hidden, 'backward_input_tc': hidden,
+                   'weight_gradient_tc': 3 * 2 * 128 * 129 * args.points * R,
                    'backward_input': hidden, 'weight_gradient': 3 * 2 * 128 * 129 * args.points * R}
     flops = class_flops.get(top[0])
     fp32_peak = 148 * 128 * 2 * (clock['sm_max_mhz'] if clock and clock['sm_max_mhz'] else 1965.0) / 1e6
@@ -286,6 +289,7 @@ def main():
     p.add_argument('--reference-points', type=int, default=128)
     p.add_argument('--no-cpu-baseline', action='store_true')
     p.add_argument('--no-reference-cuda', action='store_true')
+    p.add_argument('--tier', type=int, default=0, help='0 automatic, 1 generic, 2 tensor cores')
     args = p.parse_args()
     if args.impl == 'reference':
         run_reference(args)

@@ -224,7 +224,7 @@ int cpde_epoch_result(cpde_engine* h, uint64_t net, double* objective, float* gr
         auto& e = E(h);
         auto& n = e.net(net);
         cpde::require(gradient == nullptr || count == size_t(n.params), "gradient size mismatch");
-        CPDE_CUDA(cudaStreamSynchronize(e.stream));
+        e.check_device_errors();
         if (objective) {
             cpde::CostStats s;
             CPDE_CUDA(cudaMemcpy(&s, n.cost_totals.ptr, sizeof(s), cudaMemcpyDeviceToHost));
@@ -254,7 +254,7 @@ int cpde_kernel_timing_report(cpde_engine* h, cpde_sink report, void* ctx) {
 
 int cpde_set_tier(cpde_engine* h, int32_t tier) {
     return guard(h, [&] {
-        cpde::require(tier == 0 || tier == 1, "tier must be 0 (automatic) or 1 (generic)");
+        cpde::require(tier >= 0 && tier <= 2, "tier must be 0 (automatic), 1 (generic) or 2 (tensor cores)");
         E(h).tier = tier;
     });
 }

@@ -107,6 +107,20 @@ Engine::Engine(int dev) : device(dev) {
     CPDE_CUDA(cudaSetDevice(device));
     CPDE_CUDA(cudaFree(nullptr));  // create the primary context
     CPDE_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+    tc_error.resize(1);
+    CPDE_CUDA(cudaMemsetAsync(tc_error.ptr, 0, sizeof(int), stream));
+    CPDE_CUDA(cudaStreamSynchronize(stream));
+}
+
+void Engine::check_device_errors() {
+    int code = 0;
+    CPDE_CUDA(cudaMemcpyAsync(&code, tc_error.ptr, sizeof(int), cudaMemcpyDeviceToHost, stream));
+    CPDE_CUDA(cudaStreamSynchronize(stream));
+    if (code) {
+        CPDE_CUDA(cudaMemsetAsync(tc_error.ptr, 0, sizeof(int), stream));
+        throw DeviceError(std::string("tensor-core kernel gave up waiting for ") +
+                          (code == tcg::kErrTma ? "a TMA tile" : "an MMA") + "; results of this pass are invalid");
+    }
 }
 
 Engine::~Engine() {
@@ -434,6 +448,35 @@ static void allow_smem(K kernel, size_t bytes) {
     CPDE_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes)));
 }
 
+static CUtensorMap tensor_map(const float* base, int inner, long rows, int box_rows) {
+    CUtensorMap map;
+    cuuint64_t dims[2] = {cuuint64_t(inner), cuuint64_t(rows)};
+    cuuint64_t strides[1] = {cuuint64_t(inner) * sizeof(float)};
+    cuuint32_t box[2] = {cuuint32_t(tcg::KS), cuuint32_t(box_rows)};
+    cuuint32_t element_strides[2] = {1, 1};
+    driver_check(driver_api().encode_tiled(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims,
+                                           strides, box, element_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE),
+                 "cuTensorMapEncodeTiled");
+    return map;
+}
+
+// Unswizzled box of 128 neurons x 32 columns (raw slabs of the weight-gradient kernel).
+static CUtensorMap raw_map(const float* base, int inner, long rows) {
+    CUtensorMap map;
+    cuuint64_t dims[2] = {cuuint64_t(inner), cuuint64_t(rows)};
+    cuuint64_t strides[1] = {cuuint64_t(inner) * sizeof(float)};
+    cuuint32_t box[2] = {cuuint32_t(tcg::BM), cuuint32_t(tcg::KS)};
+    cuuint32_t element_strides[2] = {1, 1};
+    driver_check(driver_api().encode_tiled(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims,
+                                           strides, box, element_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                           CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE),
+                 "cuTensorMapEncodeTiled");
+    return map;
+}
+
 bool Engine::fast_ok(NetRecord& n, Context& ctx) const {
     if (tier == 1 || ctx.static_id < 0) return false;
     const int L = n.layers;
@@ -448,6 +491,7 @@ struct FastForward {
     Engine& e;
     NetRecord& n;
     long P;
+    bool tensor;  // tcgen05 3xTF32 GEMMs where the shapes allow
     template <int SID, class Act>
     void layers() {
         using namespace fast;
@@ -468,6 +512,26 @@ struct FastForward {
                 CPDE_RUN(e, "input_forward",
                          (k_input_forward<SID, Act><<<grid_for(long(M) * P, THREADS, 148 * 32), THREADS, 0,
                                                       e.stream>>>(M, K, P, W, b, n.act[0].ptr, n.act[1].ptr)));
+            } else if (tensor && M % tcg::BM == 0 && K % tcg::KS == 0) {
+                using TT = tcg::Tiling<R>;
+                static bool tc_ready[64] = {};
+                if (!tc_ready[e.device & 63]) {
+                    allow_smem(tcg::k_forward_tc<SID, Act>, TT::SMEM);
+                    tc_ready[e.device & 63] = true;
+                }
+                n.w_hi.reserve(n.params);
+                n.w_lo.reserve(n.params);
+                float* hi = n.w_hi.ptr + n.offset[l - 1];
+                float* lo = n.w_lo.ptr + n.offset[l - 1];
+                CPDE_RUN(e, "split_weights", (tcg::k_split_tf32<<<grid_for(long(M) * K), 256, 0, e.stream>>>(
+                                                 W, hi, lo, M, K, 1)));
+                const CUtensorMap mh = tensor_map(hi, K, M, tcg::BM), ml = tensor_map(lo, K, M, tcg::BM);
+                const CUtensorMap mx = tensor_map(n.act[l - 1].ptr, K, P * R, TT::N);
+                const long tiles = (P + TT::PTS - 1) / TT::PTS;
+                dim3 grid(unsigned(std::min<long>(tiles, std::max(1, 296 / (M / tcg::BM)))), unsigned(M / tcg::BM));
+                CPDE_RUN(e, "forward_tc",
+                         (tcg::k_forward_tc<SID, Act><<<grid, tcg::THREADS, TT::SMEM, e.stream>>>(
+                             mh, ml, mx, M, K, P, b, n.act[l].ptr, e.tc_error.ptr)));
             } else {
                 dim3 grid(unsigned((P + T::PTS - 1) / T::PTS), unsigned((M + BM - 1) / BM));
                 CPDE_RUN(e, "forward",
@@ -493,6 +557,7 @@ struct FastBackward {
     NetRecord& n;
     long P;
     float* target;
+    bool use_tensor;
     template <int SID, class Act>
     void layers() {
         using namespace fast;
@@ -521,6 +586,19 @@ struct FastBackward {
                                             n.partial.ptr, bx, size, n.gradient_base(L - 1, target))));
         }
         float* cur = n.dz[1].ptr;
+        const bool tensor = use_tensor;
+        if (tensor) {
+            static bool tc_ready[64] = {};
+            if (!tc_ready[e.device & 63]) {
+                using TT = tcg::Tiling<R>;
+                allow_smem(tcg::k_backward_tc<SID, Act, false>, TT::SMEM);
+                allow_smem(tcg::k_backward_tc<SID, Act, true>, TT::SMEM);
+                allow_smem(tcg::k_weight_gradient_tc, tcg::kWgSmem);
+                tc_ready[e.device & 63] = true;
+            }
+            n.wb_hi.reserve(n.params);
+            n.wb_lo.reserve(n.params);
+        }
         for (int l = L - 1; l >= 2; --l) {
             const int M = n.neurons[l], N = n.neurons[l - 1];
             // weight gradient of layer l (M x N plus bias), split over columns
@@ -530,16 +608,53 @@ struct FastBackward {
             splits = (cols + per - 1) / per;
             n.partial.reserve(size_t(splits) * M * (N + 1));
             dim3 wg(unsigned(splits), (N + BM - 1) / BM, (M + BM - 1) / BM);
-            CPDE_RUN(e, "weight_gradient", (k_weight_gradient<<<wg, THREADS, 0, e.stream>>>(
-                                               M, N, cols, R, per, cur, n.act[l - 1].ptr, n.partial.ptr)));
+            if (tensor && M % tcg::BM == 0 && N % tcg::BM == 0) {
+                const CUtensorMap md = raw_map(cur, M, cols), ma = raw_map(n.act[l - 1].ptr, N, cols);
+                CPDE_RUN(e, "weight_gradient_tc",
+                         (tcg::k_weight_gradient_tc<<<wg, tcg::THREADS, tcg::kWgSmem, e.stream>>>(
+                             md, ma, M, N, cols, R, per, n.partial.ptr, e.tc_error.ptr)));
+            } else {
+                CPDE_RUN(e, "weight_gradient", (k_weight_gradient<<<wg, THREADS, 0, e.stream>>>(
+                                                   M, N, cols, R, per, cur, n.act[l - 1].ptr, n.partial.ptr)));
+            }
             long size = long(M) * (N + 1);
             CPDE_RUN(e, "sum_partials", (k_sum_partials<<<grid_for(size), 256, 0, e.stream>>>(
                                             n.partial.ptr, int(splits), size, n.gradient_base(l - 1, target))));
             // adjoint into layer l-1
             const float* W = n.weights(l - 1);
             const long tiles_p = (P + T::PTS - 1) / T::PTS;
-            if (l - 1 == 1) {
-                const int K0 = n.neurons[0];
+            const bool input = l - 1 == 1;
+            float* next = cur == n.dz[0].ptr ? n.dz[1].ptr : n.dz[0].ptr;
+            const int K0 = n.neurons[0];
+            if (tensor && N % tcg::BM == 0 && M % tcg::KS == 0) {
+                using TT = tcg::Tiling<R>;
+                float* hi = n.wb_hi.ptr + n.offset[l - 1];
+                float* lo = n.wb_lo.ptr + n.offset[l - 1];
+                CPDE_RUN(e, "split_weights", (tcg::k_split_tf32<<<grid_for(long(M) * N), 256, 0, e.stream>>>(
+                                                 W, hi, lo, N, M, 0)));
+                const CUtensorMap mh = tensor_map(hi, M, N, tcg::BM), ml = tensor_map(lo, M, N, tcg::BM);
+                const CUtensorMap mz = tensor_map(cur, M, cols, TT::N);
+                const long tt = (P + TT::PTS - 1) / TT::PTS;
+                const int bx = int(std::min<long>(tt, std::max(1, 296 / (N / tcg::BM))));
+                dim3 grid(bx, N / tcg::BM);
+                if (input) {
+                    n.input_partial.reserve(size_t(bx) * N * (K0 + 1));
+                    CPDE_RUN(e, "backward_input_tc",
+                             (tcg::k_backward_tc<SID, Act, true><<<grid, tcg::THREADS, TT::SMEM, e.stream>>>(
+                                 mh, ml, mz, N, M, P, n.act[1].ptr, nullptr, n.act[0].ptr, K0, n.input_partial.ptr,
+                                 e.tc_error.ptr)));
+                    long isize = long(N) * (K0 + 1);
+                    CPDE_RUN(e, "sum_partials", (k_sum_partials<<<grid_for(isize), 256, 0, e.stream>>>(
+                                                    n.input_partial.ptr, bx, isize, n.gradient_base(0, target))));
+                } else {
+                    CPDE_RUN(e, "backward_tc",
+                             (tcg::k_backward_tc<SID, Act, false><<<grid, tcg::THREADS, TT::SMEM, e.stream>>>(
+                                 mh, ml, mz, N, M, P, n.act[l - 1].ptr, next, nullptr, 0, nullptr, e.tc_error.ptr)));
+                    cur = next;
+                }
+                continue;
+            }
+            if (input) {
                 const int bx = int(std::min<long>(tiles_p, 148 * 2));
                 dim3 grid(bx, (N + BM - 1) / BM);
                 n.input_partial.reserve(size_t(bx) * N * (K0 + 1));
@@ -550,7 +665,6 @@ struct FastBackward {
                 CPDE_RUN(e, "sum_partials", (k_sum_partials<<<grid_for(isize), 256, 0, e.stream>>>(
                                                 n.input_partial.ptr, bx, isize, n.gradient_base(0, target))));
             } else {
-                float* next = cur == n.dz[0].ptr ? n.dz[1].ptr : n.dz[0].ptr;
                 const int bx = int(std::min<long>(tiles_p, 148 * 8));
                 dim3 grid(bx, (N + BM - 1) / BM);
                 CPDE_RUN(e, "backward",
@@ -568,12 +682,19 @@ struct FastBackward {
 };
 }  // namespace
 
+// Tensor cores (3xTF32, about 5e-6 normwise on weight gradients) are used by
+// default only where the tolerance is 1e-4 (highest order 4..6); orders <= 3
+// (tolerance 1e-5) keep exact FP32 FFMA unless tier 2 forces tensor cores.
+static bool use_tensor_cores(int tier, const Context& ctx) {
+    return tier == 2 || (tier == 0 && ctx.plan.max_order >= 4);
+}
+
 void Engine::fast_forward(NetRecord& n, Context& ctx, int points) {
-    with_schema(ctx.static_id, FastForward{*this, n, points});
+    with_schema(ctx.static_id, FastForward{*this, n, points, use_tensor_cores(tier, ctx)});
 }
 
 void Engine::fast_backward(NetRecord& n, Context& ctx, int points, float* target) {
-    with_schema(ctx.static_id, FastBackward{*this, n, points, target});
+    with_schema(ctx.static_id, FastBackward{*this, n, points, target, use_tensor_cores(tier, ctx)});
 }
 
 void Engine::run_cost(NetRecord& n, CostRecord& c, int cost_index, int points, int offset, bool collect,
@@ -686,7 +807,7 @@ uint64_t Engine::evaluate(uint64_t ni, uint64_t di, int chunk) {
                                                                         ctx->rows_dev.ptr, offset, valid, out->w,
                                                                         out->values.ptr));
     }
-    CPDE_CUDA(cudaStreamSynchronize(stream));
+    check_device_errors();
     uint64_t id = next_id++;
     data[id] = std::move(out);
     return id;
@@ -1004,6 +1125,7 @@ void Engine::inspect_gradients(NetRecord& n, float* target) {
 }
 
 void Engine::download(NetRecord& n, int count, int layers) {
+    check_device_errors();
     if (count)
         CPDE_CUDA(cudaMemcpyAsync(n.host_costs.ptr, n.cost_totals.ptr, count * sizeof(CostStats),
                                   cudaMemcpyDeviceToHost, stream));

@@ -16,6 +16,7 @@
 #include "common.hpp"
 #include "expression.hpp"
 #include "kernels_fast.cuh"
+#include "kernels_tc.cuh"
 #include "kernels_generic.cuh"
 #include "scalar.hpp"
 #include "schema.hpp"
@@ -100,6 +101,8 @@ struct NetRecord {
     std::vector<DeviceBuffer<float>> pre;  // pre[l]: Z_l of nonlinear layers
     DeviceBuffer<float> dz[2], dy, jet_scratch, partial, input_partial;
     DeviceBuffer<float> eval_gradient;  // gradient target of op 14 (keeps history intact)
+    DeviceBuffer<float> w_hi, w_lo;     // TF32 split of the weights, K-major for the forward (W)
+    DeviceBuffer<float> wb_hi, wb_lo;   // TF32 split of the weights as stored (K-major for W^T)
 
     // which chunk's forward is resident (cuda/cpde_server.cu:163)
     uint64_t loaded_id = 0, loaded_version = 0;
@@ -133,8 +136,10 @@ class Engine {
     ~Engine();
     int device;
     cudaStream_t stream = nullptr;
-    int tier = 0;
+    int tier = 0;  // 0 automatic, 1 generic kernels only, 2 tensor-core GEMMs where eligible
     std::string last_error;
+    DeviceBuffer<int> tc_error;  // nonzero after a tensor-core kernel gave up waiting
+    void check_device_errors();
 
     uint64_t next_id = 1;
     std::unordered_map<uint64_t, std::unique_ptr<DataRecord>> data;

@@ -166,6 +166,7 @@ struct DriverApi {
     decltype(&cuModuleGetFunction) get_function = nullptr;
     decltype(&cuLaunchKernel) launch = nullptr;
     decltype(&cuGetErrorString) error_string = nullptr;
+    decltype(&cuTensorMapEncodeTiled) encode_tiled = nullptr;
 };
 
 inline DriverApi& driver_api() {
@@ -182,6 +183,7 @@ inline DriverApi& driver_api() {
         get("cuModuleGetFunction", (void**)&d.get_function);
         get("cuLaunchKernel", (void**)&d.launch);
         get("cuGetErrorString", (void**)&d.error_string);
+        get("cuTensorMapEncodeTiled", (void**)&d.encode_tiled);
         return d;
     }();
     return api;

@@ -144,7 +144,8 @@ int cpde_engine_stream(cpde_engine* engine, void** stream);
  * default). The report is text: one "name launches total_ms" line per kernel. */
 int cpde_kernel_timing(cpde_engine* engine, int32_t enable);
 int cpde_kernel_timing_report(cpde_engine* engine, cpde_sink report, void* context);
-/* Selects the execution tier: 0 automatic, 1 generic kernels only. */
+/* Selects the execution tier: 0 automatic, 1 generic kernels only, 2 tensor-core
+ * (tcgen05 3xTF32) GEMMs wherever the layer shapes allow. */
 int cpde_set_tier(cpde_engine* engine, int32_t tier);
 
 /* Weight gradient of one layer without any device allocation. No counterpart

@@ -45,9 +45,11 @@ CASES = [(sid, name, rows) for sid, (name, rows) in enumerate(codegen.SCHEMAS)]
 
 @pytest.mark.parametrize('sid,name,rows', CASES, ids=[c[1] for c in CASES])
 @pytest.mark.parametrize('act', [0, 2], ids=['sigmoid', 'tanh'])
-def test_fast_tier_matches_oracle(engine, sid, name, rows, act):
+@pytest.mark.parametrize('tier', [0, 2], ids=['auto', 'tensor'])
+def test_fast_tier_matches_oracle(engine, sid, name, rows, act, tier):
     V = len(rows[0])
-    layers = [V, 64, 32, 64, 2]
+    engine.set_tier(tier)
+    layers = [V, 64, 32, 64, 2] if tier == 0 else [V, 128, 128, 128, 2]
     linear = [1, act, act, act, 1]
     P = 203  # not a multiple of any tile's point count
     t, x, weights, net, data = setup(engine, rows, layers, linear, P, sid + 10 * act)
@@ -71,6 +73,11 @@ def test_fast_tier_matches_oracle(engine, sid, name, rows, act):
         gen_value, gen_grads = engine.graph_evaluate(net, [cost], sum_graph(1))
     finally:
         engine.set_tier(0)
+    if tier == 2:
+        engine.set_tier(2)
+        tc_out = engine.download(engine.evaluate(net, data, chunk=97))
+        engine.set_tier(0)
+        assert gc.rowwise_error(tc_out, acts[-1]).max() < tol
     assert abs(value - gen_value) <= tol * abs(gen_value)
     assert gc.layer_error(grads, gen_grads) < tol
 
