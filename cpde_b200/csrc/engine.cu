@@ -358,7 +358,7 @@ static void launch_gemm(Engine& e, int M, int N, int K, const float* A, int lda,
 }
 
 void Engine::forward(NetRecord& n, Context& ctx, int points) {
-    if (fast_ok(n, ctx)) return fast_forward(n, ctx, points);
+    if (fast_ok(n, ctx)) return fast_forward(n, ctx, points, false);
     const int R = ctx.R();
     const int cols = points * R;
     for (int l = 1; l <= n.layers; ++l) {
@@ -382,7 +382,7 @@ void Engine::forward(NetRecord& n, Context& ctx, int points) {
 }
 
 void Engine::backward(NetRecord& n, Context& ctx, int points, float* target) {
-    if (fast_ok(n, ctx)) return fast_backward(n, ctx, points, target);
+    if (fast_ok(n, ctx)) return fast_backward(n, ctx, points, target, false);
     const int R = ctx.R();
     const long cols = long(points) * R;
     float* cur = n.dz[0].ptr;
@@ -492,6 +492,7 @@ struct FastForward {
     NetRecord& n;
     long P;
     bool tensor;  // tcgen05 3xTF32 GEMMs where the shapes allow
+    bool hidden_only;  // leave the output layer to a fused head
     template <int SID, class Act>
     void layers() {
         using namespace fast;
@@ -539,6 +540,7 @@ struct FastForward {
                                                                                   n.act[l].ptr)));
             }
         }
+        if (hidden_only) return;
         const int O = n.neurons[L], K = n.neurons[L - 1];
         const float* W = n.weights(L - 1);
         CPDE_RUN(e, "output_forward",
@@ -558,6 +560,7 @@ struct FastBackward {
     long P;
     float* target;
     bool use_tensor;
+    bool skip_output;  // a fused head already produced dZ of the last hidden layer
     template <int SID, class Act>
     void layers() {
         using namespace fast;
@@ -573,7 +576,7 @@ struct FastBackward {
         const int L = n.layers;
         const long cols = P * R;
         // output layer: adjoint into the last hidden layer, output weight gradient
-        {
+        if (!skip_output) {
             const int O = n.neurons[L], K = n.neurons[L - 1];
             const int bx = int(std::min<long>(148 * 4, (P + 1) / 2));
             dim3 grid(bx, (K + BM - 1) / BM);
@@ -682,6 +685,47 @@ struct FastBackward {
 };
 }  // namespace
 
+struct FastHead {
+    Engine& e;
+    NetRecord& n;
+    CostRecord& c;
+    long P;
+    int offset;
+    bool collect;
+    const double* multiplier;
+    CostReduce red;
+    float* target;
+    template <int SID, class Act, int O, int KPT>
+    void go() {
+        const int L = n.layers, K = n.neurons[L - 1];
+        const int grid = int(std::min<long>(P, 148L * 8));
+        n.partial.reserve(size_t(grid) * O * (K + 1));
+        auto& t = e.dat(c.target_id);
+        CPDE_RUN(e, "head_matching",
+                 (fast::k_head_matching<SID, Act, O, KPT><<<grid, fast::BM, 0, e.stream>>>(
+                     K, P, offset, n.weights(L - 1), n.act[L - 1].ptr, n.dz[1].ptr, t.values.ptr, t.w,
+                     c.target_rows.ptr, c.weights.ptr, c.weight_samples, multiplier, collect, red, n.partial.ptr)));
+        const long size = long(O) * (K + 1);
+        CPDE_RUN(e, "sum_partials", (fast::k_sum_partials<<<grid_for(size), 256, 0, e.stream>>>(
+                                        n.partial.ptr, grid, size, n.gradient_base(L - 1, target))));
+    }
+    template <int SID, class Act, int O>
+    void by_width() {
+        if (n.neurons[n.layers - 1] == 128) go<SID, Act, O, 1>();
+        else go<SID, Act, O, 2>();
+    }
+    template <int SID, class Act>
+    void by_outputs() {
+        if (n.neurons.back() == 1) by_width<SID, Act, 1>();
+        else by_width<SID, Act, 2>();
+    }
+    template <int SID>
+    void run() {
+        if (n.linear[1] == kTanhAct) by_outputs<SID, Tanh>();
+        else by_outputs<SID, Sigmoid>();
+    }
+};
+
 // Tensor cores (3xTF32, about 5e-6 normwise on weight gradients) are used by
 // default only where the tolerance is 1e-4 (highest order 4..6); orders <= 3
 // (tolerance 1e-5) keep exact FP32 FFMA unless tier 2 forces tensor cores.
@@ -689,12 +733,19 @@ static bool use_tensor_cores(int tier, const Context& ctx) {
     return tier == 2 || (tier == 0 && ctx.plan.max_order >= 4);
 }
 
-void Engine::fast_forward(NetRecord& n, Context& ctx, int points) {
-    with_schema(ctx.static_id, FastForward{*this, n, points, use_tensor_cores(tier, ctx)});
+void Engine::fast_forward(NetRecord& n, Context& ctx, int points, bool hidden_only) {
+    with_schema(ctx.static_id, FastForward{*this, n, points, use_tensor_cores(tier, ctx), hidden_only});
 }
 
-void Engine::fast_backward(NetRecord& n, Context& ctx, int points, float* target) {
-    with_schema(ctx.static_id, FastBackward{*this, n, points, target, use_tensor_cores(tier, ctx)});
+void Engine::fast_backward(NetRecord& n, Context& ctx, int points, float* target, bool skip_output) {
+    with_schema(ctx.static_id, FastBackward{*this, n, points, target, use_tensor_cores(tier, ctx), skip_output});
+}
+
+// The fused head serves matching costs with 1 or 2 outputs and a last hidden
+// layer of 128 or 256 neurons.
+bool Engine::fused_head_ok(NetRecord& n, CostRecord& c, Context& ctx) const {
+    const int K = n.neurons[n.layers - 1], O = n.neurons.back();
+    return c.kind == 0 && fast_ok(n, ctx) && (O == 1 || O == 2) && (K == 128 || K == 256);
 }
 
 void Engine::run_cost(NetRecord& n, CostRecord& c, int cost_index, int points, int offset, bool collect,
@@ -750,6 +801,7 @@ void Engine::pass(NetRecord& n, CostRecord& c, int cost_index, bool bwd, bool co
     Context& ctx = *c.context;
     require(n.capacity >= long(c.width) * long(c.rows.size()) && n.dz[0].ptr && n.cost_totals.ptr,
             "internal error: network storage was not prepared for this cost");
+    const bool fused = bwd && fused_head_ok(n, c, ctx);
     for (int offset = begin; offset < end; offset += c.width) {
         int valid = std::min(c.width, input.w - offset);
         if (reuse_forward) {
@@ -758,7 +810,16 @@ void Engine::pass(NetRecord& n, CostRecord& c, int cost_index, bool bwd, bool co
                     "forward context is no longer current");
         } else {
             activate(n, c.input_id, ctx, c.width, offset, valid);
-            if (c.has_components) forward(n, ctx, valid);
+            if (c.has_components) {
+                if (fused) fast_forward(n, ctx, valid, true);
+                else forward(n, ctx, valid);
+            }
+        }
+        if (fused) {
+            CostReduce red{n.cost_partials.ptr, n.cost_ticket.ptr, n.cost_totals.ptr + cost_index};
+            with_schema(ctx.static_id, FastHead{*this, n, c, valid, offset, collect, multiplier, red, target});
+            fast_backward(n, ctx, valid, target, true);
+            continue;
         }
         run_cost(n, c, cost_index, valid, offset, collect, bwd, multiplier);
         if (bwd) backward(n, ctx, valid, target);

@@ -190,8 +190,9 @@ class Engine {
     void forward(NetRecord& n, Context& ctx, int points);
     void backward(NetRecord& n, Context& ctx, int points, float* target);
     bool fast_ok(NetRecord& n, Context& ctx) const;
-    void fast_forward(NetRecord& n, Context& ctx, int points);
-    void fast_backward(NetRecord& n, Context& ctx, int points, float* target);
+    bool fused_head_ok(NetRecord& n, CostRecord& c, Context& ctx) const;
+    void fast_forward(NetRecord& n, Context& ctx, int points, bool hidden_only);
+    void fast_backward(NetRecord& n, Context& ctx, int points, float* target, bool skip_output);
     void run_cost(NetRecord& n, CostRecord& c, int cost_index, int points, int offset, bool collect, bool gradient,
                   const double* multiplier);
     void pass(NetRecord& n, CostRecord& c, int cost_index, bool backward, bool collect, const double* multiplier,

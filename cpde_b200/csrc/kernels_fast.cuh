@@ -489,6 +489,125 @@ __global__ void __launch_bounds__(THREADS) k_output_backward(int O, int K, long 
         for (int o = 0; o < O; ++o) out[o + (size_t)K * O] = gb[o] + red[o][0];
 }
 
+// Fused output head for a matching cost: Z_out = W_out Y + b for O linear
+// outputs, the squared-error loss and its adjoints (the arithmetic and order of
+// k_cost_matching, cuda/cost_kernels.cuh:6-35), the output layer's weight
+// gradient, dY = W_out^T dZ_out and the jet adjoint into the last hidden layer,
+// all from one read of that layer's jets. One thread owns neurons
+// t + 128 j (j < KPT, K = 128 KPT); a CTA walks points, reducing the output
+// dot products across its 4 warps through shared memory.
+// partials[cta][o + m O] (bias at m = K) are summed by k_sum_partials.
+template <int SID, class Act, int O, int KPT>
+__global__ void __launch_bounds__(BM) k_head_matching(int K, long P, int offset, const float* __restrict__ W,
+                                                      const float* __restrict__ Y, float* __restrict__ dZ,
+                                                      const float* __restrict__ target, int target_samples,
+                                                      const int* __restrict__ target_rows,
+                                                      const float* __restrict__ weights, int weight_samples,
+                                                      const double* __restrict__ multiplier, int collect,
+                                                      CostReduce red, float* __restrict__ partials) {
+    constexpr int R = StaticJet<SID>::R;
+    __shared__ float sums[4][O * R];
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    float w[KPT][O], gw[KPT][O];
+#pragma unroll
+    for (int j = 0; j < KPT; ++j)
+#pragma unroll
+        for (int o = 0; o < O; ++o) {
+            w[j][o] = __ldg(W + o + (size_t)(t + BM * j) * O);
+            gw[j][o] = 0.f;
+        }
+    float bias[O], gb[O];
+#pragma unroll
+    for (int o = 0; o < O; ++o) {
+        bias[o] = __ldg(W + (size_t)K * O + o);
+        gb[o] = 0.f;
+    }
+    const double scale = multiplier ? *multiplier : 1.0;
+    CostStats local = cost_empty();
+    for (long p = blockIdx.x; p < P; p += gridDim.x) {
+        float y[KPT][R];
+#pragma unroll
+        for (int j = 0; j < KPT; ++j)
+#pragma unroll
+            for (int r = 0; r < R; ++r) y[j][r] = __ldg(Y + ((size_t)p * R + r) * K + t + BM * j);
+#pragma unroll
+        for (int o = 0; o < O; ++o)
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                float v = 0.f;
+#pragma unroll
+                for (int j = 0; j < KPT; ++j) v = fmaf(w[j][o], y[j][r], v);
+#pragma unroll
+                for (int sft = 16; sft; sft >>= 1) v += __shfl_xor_sync(0xffffffffu, v, sft);
+                if (lane == 0) sums[warp][o * R + r] = v;
+            }
+        __syncthreads();
+        float g[O][R];
+        float value = 0.f;
+        const int wp = weight_samples == 1 ? 0 : offset + int(p);
+#pragma unroll
+        for (int d = 0; d < R; ++d)
+#pragma unroll
+            for (int o = 0; o < O; ++o) {
+                const float z = sums[0][o * R + d] + sums[1][o * R + d] + sums[2][o * R + d] +
+                                sums[3][o * R + d] + (d == 0 ? bias[o] : 0.f);
+                const float wt = __ldg(weights + ((size_t)d * weight_samples + wp) * O + o);
+                float grad = 0.f;
+                if (wt != 0.f) {
+                    const float res =
+                        z - __ldg(target + ((size_t)__ldg(target_rows + d) * target_samples + offset + p) * O + o);
+                    value += wt * res * res;
+                    grad = 2.0f * wt * res;
+                }
+                g[o][d] = grad;
+            }
+        __syncthreads();  // sums is rewritten by the next point
+        if (t == 0) {
+            if (!isfinite(value)) mark_bad(local, offset + int(p), -1);
+            if (collect) local.value += double(value);
+#pragma unroll
+            for (int d = 0; d < R; ++d)
+#pragma unroll
+                for (int o = 0; o < O; ++o)
+                    if (!isfinite(g[o][d])) mark_bad(local, offset + int(p), d * O + o);
+        }
+        if (multiplier)
+#pragma unroll
+            for (int o = 0; o < O; ++o)
+#pragma unroll
+                for (int d = 0; d < R; ++d) g[o][d] = scale == 0 ? 0.f : float(g[o][d] * scale);
+#pragma unroll
+        for (int o = 0; o < O; ++o) gb[o] += g[o][0];
+#pragma unroll
+        for (int j = 0; j < KPT; ++j) {
+            float dy[R];
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                float acc = 0.f;
+#pragma unroll
+                for (int o = 0; o < O; ++o) {
+                    acc = fmaf(w[j][o], g[o][r], acc);
+                    gw[j][o] = fmaf(g[o][r], y[j][r], gw[j][o]);
+                }
+                dy[r] = acc;
+            }
+            StaticJet<SID>::template adjoint<Act>(y[j], dy);
+            float* out = dZ + (size_t)p * R * K + t + BM * j;
+#pragma unroll
+            for (int r = 0; r < R; ++r) out[(size_t)r * K] = dy[r];
+        }
+    }
+    float* out = partials + (size_t)blockIdx.x * O * (K + 1);
+#pragma unroll
+    for (int j = 0; j < KPT; ++j)
+#pragma unroll
+        for (int o = 0; o < O; ++o) out[o + (size_t)(t + BM * j) * O] = gw[j][o];
+    if (t == 0)
+#pragma unroll
+        for (int o = 0; o < O; ++o) out[o + (size_t)K * O] = gb[o];
+    cost_finish(local, red);
+}
+
 // Sum CTA partials (fixed order) into a layer gradient (accumulating).
 __global__ void k_sum_partials(const float* __restrict__ partials, int count, long size, float* __restrict__ out) {
     for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < size; i += (long)blockDim.x * gridDim.x) {

@@ -256,7 +256,9 @@ __global__ void __launch_bounds__(THREADS) k_backward_tc(const __grid_constant__
     }
     if (INPUT_GRAD && m < M) {
         float* out = partials + (size_t)blockIdx.x * M * (K0 + 1);
-        for (int k = 0; k < K0; ++k) out[m + (size_t)k * M] = gacc[k];
+#pragma unroll
+        for (int k = 0; k < 8; ++k)  // constant bound keeps gacc in registers
+            if (k < K0) out[m + (size_t)k * M] = gacc[k];
         out[m + (size_t)K0 * M] = gacc[8];
     }
     teardown<T::TMEM>(tmem);
