@@ -138,6 +138,82 @@ def reference_cuda(device, points=POINTS, iterations=3, batches=3):
                     f'op 90, median of {batches} batches x {iterations} epochs, device time')
 
 
+PUBLISHED_RTX3090_MS = [0.41, 0.68, 1.10, 1.72, 2.40, 3.59, 5.65]  # docs/benchmarks/fourier-rtx3090.md:23-29
+
+
+def published_inputs(order):
+    """The reference's published benchmark workload, regenerated from its
+    description (scripts/benchmark_fourier_performance.py:20-38): 27 x 27 grid
+    on [-1, 1]^2, all mixed derivatives through `order`, a 10 x 10 Fourier
+    target with coefficients from seed 2026, rows weighted by the inverse
+    variance of their targets, and the front end's seed-3407 initialisation
+    (uniform +-2/sqrt(fan_in) weights, +-0.1 biases; cpde/api.py:277-280)."""
+    from cpde_b200.expressions import all_mixed, quadrature_inputs
+    t = all_mixed(order, 'xy')
+    g = np.linspace(-1, 1, 27)
+    gx, gy = np.meshgrid(g, g, indexing='ij')
+    pts = np.column_stack((gx.ravel(), gy.ravel())).astype(np.float32).astype(np.float64)
+    x, y = pts.T
+    coef = np.random.default_rng(2026).uniform(-1, 1, (4, 10, 10))
+    target = np.zeros((len(t), len(pts)))
+    for row, (_, dx, dy) in enumerate(t):
+        for n in range(1, 11):
+            for k in range(1, 11):
+                a, b, c, d = coef[:, n - 1, k - 1] * n ** int(dx) * k ** int(dy) / (n * k)
+                sx, cx = np.sin(n * x + dx * np.pi / 2), np.cos(n * x + dx * np.pi / 2)
+                sy, cy = np.sin(k * y + dy * np.pi / 2), np.cos(k * y + dy * np.pi / 2)
+                target[row] += a * sx * sy + b * sx * cy + c * cx * sy + d * cx * cy
+    weights = (1 / target.std(axis=1) ** 2).astype(np.float32)
+    rng = np.random.default_rng(3407)
+    init = [np.concatenate((rng.uniform(-2 / np.sqrt(w), 2 / np.sqrt(w), h * w),
+                            rng.uniform(-.1, .1, h))).astype(np.float32)
+            for w, h in zip(LAYERS[:-1], LAYERS[1:])]
+    return t, quadrature_inputs(pts, t), target[:, None, :].astype(np.float32), weights, init
+
+
+def published_workload(device, engine=None, iterations=50, batches=5):
+    """ms/epoch (op-90 epochs: forward, loss, weight gradients) of this engine
+    and of the reference CUDA server on the same GPU, orders 0..6."""
+    from cpde_b200 import native
+    from cpde_b200.client import Data, Network, Session
+    exe = ROOT / 'oracle' / '_ref' / 'cpde_ref_cuda_server'
+    rows = []
+    own = engine or native.Engine(device)
+    ref = Session(exe, device=device) if exe.exists() else None
+    try:
+        for order in range(7):
+            t, x, target, weights, init = published_inputs(order)
+            R = len(t)
+            net = own.network(LAYERS, init)
+            data = own.data(x, t)
+            tgt = own.data(target, t)
+            cost = own.matching(net, data, tgt, list(range(R)), list(range(R)), 1, weights[:, None, None])
+            _, dev, loss, _ = own.benchmark(net, cost, 10, iterations, batches, len(LAYERS) - 1)
+            entry = dict(order=order, rows=R, ms=float(np.median(dev)), loss=loss,
+                         rtx3090_reference_ms=PUBLISHED_RTX3090_MS[order])
+            for kind, h in ((2, cost), (0, tgt), (0, data), (1, net)):
+                own.release(kind, h)
+            if ref is not None:
+                rnet = Network(ref, LAYERS, weights=init)
+                rd, rt = Data(ref, x, t), Data(ref, target, t)
+                rc = rnet.matching(rd, rt, weights[None, :])
+                _, rdev, rloss, _ = rnet.benchmark(rc, 10, iterations, batches)
+                entry.update(reference_cuda_ms=float(np.median(rdev)), reference_loss=rloss,
+                             speedup_vs_reference_cuda=float(np.median(rdev)) / entry['ms'])
+                rc.close(); rt.close(); rd.close(); rnet.close()
+            rows.append(entry)
+    finally:
+        if ref is not None:
+            ref.close()
+        if engine is None:
+            own.close()
+    return dict(workload='27x27 grid on [-1,1]^2, 2->128^4->1 sigmoid, all mixed derivatives through the order, '
+                         'Fourier matching (scripts/benchmark_fourier_performance.py), op-90 epochs, '
+                         f'median of {batches} batches x {iterations}, device time; reference = the reference '
+                         'CUDA server built for sm_100a on the same GPU',
+                orders=rows)
+
+
 def run_reference(args):
     rank = int(os.environ.get('RANK', '0'))
     if rank != 0:
@@ -268,6 +344,7 @@ def run_b200(args):
         if world == 1 and not args.no_cpu_baseline:
             line['cpu_baseline'] = cpu_baseline()
         if world == 1 and not args.no_reference_cuda:
+            line['published_workload'] = published_workload(local, engine)
             engine.close()
             ref = reference_cuda(local, args.points)
             if ref is not None:

@@ -39,6 +39,7 @@ def build(force=False, verbose_ptxas=False):
     sources.append(PACKAGE.parent / 'include' / 'cpde_b200.h')
     if force or _stale(LIBRARY, sources):
         cmd = [nvcc, *ARCH, '-lineinfo', '-O3', '-std=c++17', '-Xcompiler', '-fPIC', '-shared',
+               f'--split-compile={os.cpu_count() or 1}',
                '--expt-relaxed-constexpr', '-o', LIBRARY, CSRC / 'library.cu', '-lnvrtc']
         if verbose_ptxas:
             cmd.insert(1, '-Xptxas=-v')

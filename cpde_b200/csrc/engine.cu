@@ -529,7 +529,7 @@ struct FastForward {
                 const CUtensorMap mh = tensor_map(hi, K, M, tcg::BM), ml = tensor_map(lo, K, M, tcg::BM);
                 const CUtensorMap mx = tensor_map(n.act[l - 1].ptr, K, P * R, TT::N);
                 const long tiles = (P + TT::PTS - 1) / TT::PTS;
-                dim3 grid(unsigned(std::min<long>(tiles, std::max(1, 296 / (M / tcg::BM)))), unsigned(M / tcg::BM));
+                dim3 grid(unsigned(std::min<long>(tiles, std::max(1, 444 / (M / tcg::BM)))), unsigned(M / tcg::BM));
                 CPDE_RUN(e, "forward_tc",
                          (tcg::k_forward_tc<SID, Act><<<grid, tcg::THREADS, TT::SMEM, e.stream>>>(
                              mh, ml, mx, M, K, P, b, n.act[l].ptr, e.tc_error.ptr)));
@@ -638,7 +638,7 @@ struct FastBackward {
                 const CUtensorMap mh = tensor_map(hi, M, N, tcg::BM), ml = tensor_map(lo, M, N, tcg::BM);
                 const CUtensorMap mz = tensor_map(cur, M, cols, TT::N);
                 const long tt = (P + TT::PTS - 1) / TT::PTS;
-                const int bx = int(std::min<long>(tt, std::max(1, 296 / (N / tcg::BM))));
+                const int bx = int(std::min<long>(tt, std::max(1, 444 / (N / tcg::BM))));
                 dim3 grid(bx, N / tcg::BM);
                 if (input) {
                     n.input_partial.reserve(size_t(bx) * N * (K0 + 1));
@@ -712,7 +712,7 @@ struct FastHead {
     template <int SID, class Act, int O>
     void by_width() {
         if (n.neurons[n.layers - 1] == 128) go<SID, Act, O, 1>();
-        else go<SID, Act, O, 2>();
+        else go<SID, Act, 1, 2>();  // fused_head_ok admits 256-wide last layers for one output only
     }
     template <int SID, class Act>
     void by_outputs() {
@@ -741,11 +741,11 @@ void Engine::fast_backward(NetRecord& n, Context& ctx, int points, float* target
     with_schema(ctx.static_id, FastBackward{*this, n, points, target, use_tensor_cores(tier, ctx), skip_output});
 }
 
-// The fused head serves matching costs with 1 or 2 outputs and a last hidden
-// layer of 128 or 256 neurons.
+// The fused head serves matching costs with 1 or 2 outputs after a 128-wide
+// last hidden layer, or 1 output after a 256-wide one.
 bool Engine::fused_head_ok(NetRecord& n, CostRecord& c, Context& ctx) const {
     const int K = n.neurons[n.layers - 1], O = n.neurons.back();
-    return c.kind == 0 && fast_ok(n, ctx) && (O == 1 || O == 2) && (K == 128 || K == 256);
+    return c.kind == 0 && fast_ok(n, ctx) && ((O <= 2 && K == 128) || (O == 1 && K == 256));
 }
 
 void Engine::run_cost(NetRecord& n, CostRecord& c, int cost_index, int points, int offset, bool collect,

@@ -25,16 +25,21 @@ constexpr int BM = 128;                       // neurons per tile = TMEM lanes
 constexpr int KS = 32;                        // K per slab: 32 fp32 = one 128-byte row
 constexpr long long kWaitCycles = 2000000000LL;  // about one second
 
+// Tile = 128 neurons x PTS whole points (N <= kTileColumns MMA columns). The
+// B regions are sized to N, so smaller tiles let more CTAs share an SM and
+// overlap each other's load / split / MMA / epilogue phases.
+constexpr int kTileColumns = 128;
+
 template <int R>
 struct Tiling {
-    static constexpr int PTS = (256 / R) > 0 ? (256 / R) : 1;
+    static constexpr int PTS = (kTileColumns / R) > 0 ? (kTileColumns / R) : 1;
     static constexpr int COLS = PTS * R;
     static constexpr int N = ((COLS + 7) / 8) * 8;
     static constexpr int TMEM = N <= 32 ? 32 : N <= 64 ? 64 : N <= 128 ? 128 : 256;
-    static constexpr int A_BYTES = BM * KS * 4;  // 16 KB
-    static constexpr int B_BYTES = N * KS * 4;   // <= 32 KB
+    static constexpr int A_BYTES = BM * KS * 4;                      // 16 KB
+    static constexpr int B_BYTES = ((N * KS * 4 + 1023) / 1024) * 1024;  // 1024-aligned
     // smem: a_hi, a_lo, b, b_lo, then barriers; +1024 for alignment
-    static constexpr int SMEM = 2 * A_BYTES + 2 * 32768 + 64 + 1024;
+    static constexpr int SMEM = 2 * A_BYTES + 2 * B_BYTES + 64 + 1024;
 };
 
 enum : int { kErrTma = 1, kErrMma = 2 };
@@ -115,14 +120,14 @@ struct Shared {
     uint32_t* tmem_slot;
 };
 
-__device__ __forceinline__ Shared carve(uint8_t* raw, int a_bytes) {
+__device__ __forceinline__ Shared carve(uint8_t* raw, int a_bytes, int b_bytes) {
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
     Shared s;
     s.a_hi = reinterpret_cast<float*>(base);
     s.a_lo = reinterpret_cast<float*>(base + a_bytes);
     s.b = reinterpret_cast<float*>(base + 2 * a_bytes);
-    s.b_lo = reinterpret_cast<float*>(base + 2 * a_bytes + 32768);
-    s.tma_bar = reinterpret_cast<uint64_t*>(base + 2 * a_bytes + 65536);
+    s.b_lo = reinterpret_cast<float*>(base + 2 * a_bytes + b_bytes);
+    s.tma_bar = reinterpret_cast<uint64_t*>(base + 2 * a_bytes + 2 * b_bytes);
     s.mma_bar = s.tma_bar + 1;
     s.tmem_slot = reinterpret_cast<uint32_t*>(s.tma_bar + 2);
     return s;
@@ -166,7 +171,7 @@ __global__ void __launch_bounds__(THREADS) k_forward_tc(const __grid_constant__ 
     constexpr int R = StaticJet<SID>::R;
     using T = Tiling<R>;
     extern __shared__ uint8_t smem_raw[];
-    Shared s = carve(smem_raw, T::A_BYTES);
+    Shared s = carve(smem_raw, T::A_BYTES, T::B_BYTES);
     uint32_t tmem;
     setup<T::TMEM>(s, tmem);
     const int m_base = blockIdx.y * BM;
@@ -212,7 +217,7 @@ __global__ void __launch_bounds__(THREADS) k_backward_tc(const __grid_constant__
     constexpr int R = StaticJet<SID>::R;
     using T = Tiling<R>;
     extern __shared__ uint8_t smem_raw[];
-    Shared s = carve(smem_raw, T::A_BYTES);
+    Shared s = carve(smem_raw, T::A_BYTES, T::B_BYTES);
     uint32_t tmem;
     setup<T::TMEM>(s, tmem);
     const int m_base = blockIdx.y * BM;
