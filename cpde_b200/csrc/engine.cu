@@ -306,7 +306,7 @@ void Engine::ensure_arena(NetRecord& n, long columns, bool backward) {
 
 void Engine::ensure_reductions(NetRecord& n, int count) {
     if (!n.cost_partials.ptr) {
-        n.cost_partials.resize(1024);
+        n.cost_partials.resize(kMaxReduceBlocks);
         n.cost_ticket.resize(1);
         CPDE_CUDA(cudaMemsetAsync(n.cost_ticket.ptr, 0, sizeof(unsigned), stream));
         n.grad_partials.resize(size_t(n.layers) * 256);
@@ -578,14 +578,14 @@ struct FastBackward {
         // output layer: adjoint into the last hidden layer, output weight gradient
         if (!skip_output) {
             const int O = n.neurons[L], K = n.neurons[L - 1];
-            const int bx = int(std::min<long>(148 * 4, (P + 1) / 2));
+            const int bx = int(std::min<long>(148 * 4, std::max(1L, (P + 15) / 16)));
             dim3 grid(bx, (K + BM - 1) / BM);
             n.partial.reserve(size_t(bx) * O * (K + 1));
             CPDE_RUN(e, "output_backward",
                      (k_output_backward<SID, Act><<<grid, THREADS, 0, e.stream>>>(
                          O, K, P, n.weights(L - 1), n.dz[0].ptr, n.act[L - 1].ptr, n.dz[1].ptr, n.partial.ptr)));
             long size = long(O) * (K + 1);
-            CPDE_RUN(e, "sum_partials", (k_sum_partials<<<grid_for(size), 256, 0, e.stream>>>(
+            CPDE_RUN(e, "sum_partials", (k_sum_partials<<<fast::sum_grid(size), 256, 0, e.stream>>>(
                                             n.partial.ptr, bx, size, n.gradient_base(L - 1, target))));
         }
         float* cur = n.dz[1].ptr;
@@ -605,13 +605,17 @@ struct FastBackward {
         for (int l = L - 1; l >= 2; --l) {
             const int M = n.neurons[l], N = n.neurons[l - 1];
             // weight gradient of layer l (M x N plus bias), split over columns
+            // enough column splits to fill two CTAs per SM, but at least 64
+            // columns (FFMA) or 128 columns (tensor cores) per split
             const int tiles = ((N + BM - 1) / BM) * ((M + BM - 1) / BM);
-            long splits = std::max(1L, std::min<long>((2L * 148 + tiles - 1) / tiles, (cols + 1023) / 1024));
-            long per = ((cols + splits - 1) / splits + BK - 1) / BK * BK;
+            const bool tc_wgrad = tensor && M % tcg::BM == 0 && N % tcg::BM == 0;
+            const long min_cols = tc_wgrad ? 128 : 64, align = tc_wgrad ? tcg::KS : BK;
+            long splits = std::max(1L, std::min<long>((2L * 148 + tiles - 1) / tiles, (cols + min_cols - 1) / min_cols));
+            long per = ((cols + splits - 1) / splits + align - 1) / align * align;
             splits = (cols + per - 1) / per;
             n.partial.reserve(size_t(splits) * M * (N + 1));
             dim3 wg(unsigned(splits), (N + BM - 1) / BM, (M + BM - 1) / BM);
-            if (tensor && M % tcg::BM == 0 && N % tcg::BM == 0) {
+            if (tc_wgrad) {
                 const CUtensorMap md = raw_map(cur, M, cols), ma = raw_map(n.act[l - 1].ptr, N, cols);
                 CPDE_RUN(e, "weight_gradient_tc",
                          (tcg::k_weight_gradient_tc<<<wg, tcg::THREADS, tcg::kWgSmem, e.stream>>>(
@@ -621,7 +625,7 @@ struct FastBackward {
                                                    M, N, cols, R, per, cur, n.act[l - 1].ptr, n.partial.ptr)));
             }
             long size = long(M) * (N + 1);
-            CPDE_RUN(e, "sum_partials", (k_sum_partials<<<grid_for(size), 256, 0, e.stream>>>(
+            CPDE_RUN(e, "sum_partials", (k_sum_partials<<<fast::sum_grid(size), 256, 0, e.stream>>>(
                                             n.partial.ptr, int(splits), size, n.gradient_base(l - 1, target))));
             // adjoint into layer l-1
             const float* W = n.weights(l - 1);
@@ -647,7 +651,7 @@ struct FastBackward {
                                  mh, ml, mz, N, M, P, n.act[1].ptr, nullptr, n.act[0].ptr, K0, n.input_partial.ptr,
                                  e.tc_error.ptr)));
                     long isize = long(N) * (K0 + 1);
-                    CPDE_RUN(e, "sum_partials", (k_sum_partials<<<grid_for(isize), 256, 0, e.stream>>>(
+                    CPDE_RUN(e, "sum_partials", (k_sum_partials<<<fast::sum_grid(isize), 256, 0, e.stream>>>(
                                                     n.input_partial.ptr, bx, isize, n.gradient_base(0, target))));
                 } else {
                     CPDE_RUN(e, "backward_tc",
@@ -665,7 +669,7 @@ struct FastBackward {
                          (k_backward<SID, Act, true><<<grid, THREADS, smem, e.stream>>>(
                              N, M, P, W, cur, n.act[1].ptr, nullptr, n.act[0].ptr, K0, n.input_partial.ptr)));
                 long isize = long(N) * (K0 + 1);
-                CPDE_RUN(e, "sum_partials", (k_sum_partials<<<grid_for(isize), 256, 0, e.stream>>>(
+                CPDE_RUN(e, "sum_partials", (k_sum_partials<<<fast::sum_grid(isize), 256, 0, e.stream>>>(
                                                 n.input_partial.ptr, bx, isize, n.gradient_base(0, target))));
             } else {
                 const int bx = int(std::min<long>(tiles_p, 148 * 8));
@@ -698,7 +702,7 @@ struct FastHead {
     template <int SID, class Act, int O, int KPT>
     void go() {
         const int L = n.layers, K = n.neurons[L - 1];
-        const int grid = int(std::min<long>(P, 148L * 8));
+        const int grid = int(std::min<long>(148L * 8, std::max(1L, (P + 3) / 4)));
         n.partial.reserve(size_t(grid) * O * (K + 1));
         auto& t = e.dat(c.target_id);
         CPDE_RUN(e, "head_matching",
@@ -706,7 +710,7 @@ struct FastHead {
                      K, P, offset, n.weights(L - 1), n.act[L - 1].ptr, n.dz[1].ptr, t.values.ptr, t.w,
                      c.target_rows.ptr, c.weights.ptr, c.weight_samples, multiplier, collect, red, n.partial.ptr)));
         const long size = long(O) * (K + 1);
-        CPDE_RUN(e, "sum_partials", (fast::k_sum_partials<<<grid_for(size), 256, 0, e.stream>>>(
+        CPDE_RUN(e, "sum_partials", (fast::k_sum_partials<<<fast::sum_grid(size), 256, 0, e.stream>>>(
                                         n.partial.ptr, grid, size, n.gradient_base(L - 1, target))));
     }
     template <int SID, class Act, int O>
@@ -725,6 +729,70 @@ struct FastHead {
         else by_outputs<SID, Sigmoid>();
     }
 };
+
+namespace {
+struct PointEpoch {
+    Engine& e;
+    NetRecord& n;
+    CostRecord& c;
+    long P;
+    int offset;
+    bool collect;
+    const double* multiplier;
+    CostReduce red;
+    float* target;
+    template <int SID, class Act, int O, int K>
+    void go() {
+        constexpr int R = StaticJet<SID>::R;
+        using T = small::Tiling<R>;
+        const size_t smem = small::SmemSize<R, O>::FLOATS * sizeof(float);
+        static bool ready[64] = {};
+        if (!ready[e.device & 63]) {
+            allow_smem(small::k_point_epoch<SID, Act, O, K>, smem);
+            ready[e.device & 63] = true;
+        }
+        // at most one CTA per SM, each over a contiguous run of point tiles
+        const long tiles = (P + T::PTS - 1) / T::PTS;
+        const int per = int((tiles + 147) / 148);
+        const int grid = int((tiles + per - 1) / per);
+        small::EpochNet net{};
+        net.layers = n.layers;
+        for (int l = 0; l <= n.layers; ++l) net.width[l] = n.neurons[l];
+        for (int l = 0; l < n.layers; ++l) {
+            net.W[l] = n.weights(l);
+            net.act[l] = n.act[l].ptr;
+            net.offset[l] = n.offset[l];
+        }
+        net.dz[0] = n.dz[0].ptr;
+        net.dz[1] = n.dz[1].ptr;
+        net.params = n.params;
+        n.partial.reserve(size_t(grid) * n.params);
+        net.partials = n.partial.ptr;
+        auto& t = e.dat(c.target_id);
+        small::EpochHead head{t.values.ptr, t.w,    c.target_rows.ptr, c.weights.ptr, c.weight_samples,
+                              multiplier,   collect, offset,           red};
+        CPDE_RUN(e, "point_epoch", (small::k_point_epoch<SID, Act, O, K><<<grid, small::THREADS, smem, e.stream>>>(
+                                       net, P, per, head)));
+        CPDE_RUN(e, "sum_partials", (fast::k_sum_partials<<<fast::sum_grid(n.params), 256, 0, e.stream>>>(
+                                        n.partial.ptr, grid, n.params, n.gradient_base(0, target))));
+    }
+    template <int SID, class Act, int O>
+    void by_width() {
+        if (n.neurons[n.layers - 1] == 128) go<SID, Act, O, 128>();
+        else go<SID, Act, 1, 256>();  // fused_head_ok admits 256-wide last layers for one output only
+    }
+    template <int SID, class Act>
+    void by_outputs() {
+        if (n.neurons.back() == 1) by_width<SID, Act, 1>();
+        else by_width<SID, Act, 2>();
+    }
+    template <int SID>
+    void run() {
+        if (n.linear[1] == kTanhAct) by_outputs<SID, Tanh>();
+        else by_outputs<SID, Sigmoid>();
+    }
+};
+}  // namespace
 
 // Tensor cores (3xTF32, about 5e-6 normwise on weight gradients) are used by
 // default only where the tolerance is 1e-4 (highest order 4..6); orders <= 3
@@ -746,6 +814,27 @@ void Engine::fast_backward(NetRecord& n, Context& ctx, int points, float* target
 bool Engine::fused_head_ok(NetRecord& n, CostRecord& c, Context& ctx) const {
     const int K = n.neurons[n.layers - 1], O = n.neurons.back();
     return c.kind == 0 && fast_ok(n, ctx) && ((O <= 2 && K == 128) || (O == 1 && K == 256));
+}
+
+// The point-tile epoch (kernels_small.cuh) takes chunks whose forward is not
+// reused, when the fused head applies, the gradient banks of all layers are
+// one contiguous range, and the chunk is small enough (tier 0) or tier 3 asks.
+bool Engine::point_epoch_ok(NetRecord& n, Context& ctx, long points, float* target) const {
+    if (tier != 0 && tier != 3) return false;
+    if (n.layers > small::kMaxLayers) return false;
+    if (!target)
+        for (int l = 1; l < n.layers; ++l)
+            if (n.active[l] != n.active[0]) return false;
+    // tensor-core layers overtake it sooner than FFMA layers (measured on the
+    // 2->128^4->1 published workload: orders 4-6 favour tensor cores from ~8K columns)
+    const long limit = use_tensor_cores(tier, ctx) ? point_epoch_columns / 4 : point_epoch_columns;
+    return tier == 3 || points * ctx.R() <= limit;
+}
+
+void Engine::point_epoch(NetRecord& n, CostRecord& c, Context& ctx, long points, int offset, bool collect,
+                         const double* multiplier, int cost_index, float* target) {
+    CostReduce red{n.cost_partials.ptr, n.cost_ticket.ptr, n.cost_totals.ptr + cost_index};
+    with_schema(ctx.static_id, PointEpoch{*this, n, c, points, offset, collect, multiplier, red, target});
 }
 
 void Engine::run_cost(NetRecord& n, CostRecord& c, int cost_index, int points, int offset, bool collect,
@@ -804,12 +893,17 @@ void Engine::pass(NetRecord& n, CostRecord& c, int cost_index, bool bwd, bool co
     const bool fused = bwd && fused_head_ok(n, c, ctx);
     for (int offset = begin; offset < end; offset += c.width) {
         int valid = std::min(c.width, input.w - offset);
+        const bool tile_epoch = fused && !reuse_forward && c.has_components && point_epoch_ok(n, ctx, valid, target);
         if (reuse_forward) {
             require(n.loaded_id == c.input_id && n.loaded_version == input.version && n.loaded_width == c.width &&
                         n.loaded_offset == offset && n.loaded_valid == valid && n.loaded_rows == c.rows,
                     "forward context is no longer current");
         } else {
             activate(n, c.input_id, ctx, c.width, offset, valid);
+            if (tile_epoch) {
+                point_epoch(n, c, ctx, valid, offset, collect, multiplier, cost_index, target);
+                continue;
+            }
             if (c.has_components) {
                 if (fused) fast_forward(n, ctx, valid, true);
                 else forward(n, ctx, valid);

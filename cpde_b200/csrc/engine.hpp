@@ -16,6 +16,7 @@
 #include "common.hpp"
 #include "expression.hpp"
 #include "kernels_fast.cuh"
+#include "kernels_small.cuh"
 #include "kernels_tc.cuh"
 #include "kernels_generic.cuh"
 #include "scalar.hpp"
@@ -136,7 +137,10 @@ class Engine {
     ~Engine();
     int device;
     cudaStream_t stream = nullptr;
-    int tier = 0;  // 0 automatic, 1 generic kernels only, 2 tensor-core GEMMs where eligible
+    // 0 automatic, 1 generic kernels only, 2 tensor-core GEMMs where eligible,
+    // 3 the point-tile epoch wherever it is eligible
+    int tier = 0;
+    long point_epoch_columns = 16384;  // automatic tier: point-tile epochs up to this many columns per chunk
     std::string last_error;
     DeviceBuffer<int> tc_error;  // nonzero after a tensor-core kernel gave up waiting
     void check_device_errors();
@@ -191,6 +195,9 @@ class Engine {
     void backward(NetRecord& n, Context& ctx, int points, float* target);
     bool fast_ok(NetRecord& n, Context& ctx) const;
     bool fused_head_ok(NetRecord& n, CostRecord& c, Context& ctx) const;
+    bool point_epoch_ok(NetRecord& n, Context& ctx, long points, float* target) const;
+    void point_epoch(NetRecord& n, CostRecord& c, Context& ctx, long points, int offset, bool collect,
+                     const double* multiplier, int cost_index, float* target);
     void fast_forward(NetRecord& n, Context& ctx, int points, bool hidden_only);
     void fast_backward(NetRecord& n, Context& ctx, int points, float* target, bool skip_output);
     void run_cost(NetRecord& n, CostRecord& c, int cost_index, int points, int offset, bool collect, bool gradient,

@@ -608,14 +608,32 @@ __global__ void __launch_bounds__(BM) k_head_matching(int K, long P, int offset,
     cost_finish(local, red);
 }
 
-// Sum CTA partials (fixed order) into a layer gradient (accumulating).
-__global__ void k_sum_partials(const float* __restrict__ partials, int count, long size, float* __restrict__ out) {
-    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < size; i += (long)blockDim.x * gridDim.x) {
+// Sum CTA partials (fixed order) into a layer gradient (accumulating). A block
+// of 256 threads takes 32 consecutive elements; its 8 warps sum interleaved
+// subsets of the partials, which are then folded in warp order.
+__global__ void __launch_bounds__(256) k_sum_partials(const float* __restrict__ partials, int count, long size,
+                                                      float* __restrict__ out) {
+    __shared__ float part[8][33];
+    const int x = threadIdx.x & 31, y = threadIdx.x >> 5;
+    for (long base = (long)blockIdx.x * 32; base < size; base += (long)gridDim.x * 32) {
+        const long i = base + x;
         float acc = 0.f;
-        for (int c = 0; c < count; ++c) acc += partials[(size_t)c * size + i];
-        out[i] += acc;
+        if (i < size)
+            for (int c = y; c < count; c += 8) acc += partials[(size_t)c * size + i];
+        part[y][x] = acc;
+        __syncthreads();
+        if (y == 0 && i < size) {
+            float t = part[0][x];
+#pragma unroll
+            for (int k = 1; k < 8; ++k) t += part[k][x];
+            out[i] += t;
+        }
+        __syncthreads();
     }
 }
+
+// Blocks for k_sum_partials (256 threads each) over `size` elements.
+inline int sum_grid(long size) { return int(std::min<long>((size + 31) / 32, 148L * 16)); }
 
 }  // namespace fast
 }  // namespace cpde

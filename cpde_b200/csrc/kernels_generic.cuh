@@ -14,6 +14,7 @@
 namespace cpde {
 
 constexpr int kReduceThreads = 256;
+constexpr int kMaxReduceBlocks = 4096;  // capacity of the per-block partial arrays
 
 struct CostStats {
     double value;
@@ -114,9 +115,11 @@ __device__ void finish_blocks(T mine, T* partials, unsigned* ticket, T* total, C
     __syncthreads();
     if (!last) return;
     __threadfence();
+    // the last block folds the partials with all its threads (fixed order)
+    T acc = empty();
+    for (unsigned b = threadIdx.x; b < gridDim.x; b += blockDim.x) acc = combine(acc, load_cg(partials + b));
+    acc = block_reduce(acc, empty);
     if (threadIdx.x == 0) {
-        T acc = empty();
-        for (unsigned b = 0; b < gridDim.x; ++b) acc = combine(acc, load_cg(partials + b));
         *total = combine(*total, acc);
         *ticket = 0;
     }

@@ -69,7 +69,7 @@ extern "C" int cpde_layer_gradient_static(cpde_engine* h, const float* dz, const
         dim3 grid(unsigned(splits), (inputs + BM - 1) / BM, (outputs + BM - 1) / BM);
         k_weight_gradient<<<grid, THREADS, 0, s>>>(outputs, inputs, columns, rows, per, dz, activations, partials);
         CPDE_LAUNCHED();
-        k_sum_partials<<<int(std::min<long>((size + 255) / 256, 148 * 16)), 256, 0, s>>>(partials, int(splits),
+        k_sum_partials<<<sum_grid(size), 256, 0, s>>>(partials, int(splits),
                                                                                           size, gradient);
         CPDE_LAUNCHED();
     });

@@ -100,3 +100,57 @@ def test_fast_tier_wide_layers_and_single_output(engine):
     expected = jets.backward(schema, weights, layers, linear, pre, acts, dout)
     assert abs(value - loss) <= 1e-4 * loss
     assert gc.layer_error(grads, expected) < 1e-4
+
+
+POINT_SHAPES = {'o1': [128, 64, 128, 1], 'o2': [128, 128, 2], 'wide': [96, 256, 1]}
+
+
+@pytest.mark.parametrize('sid,name,rows', CASES, ids=[c[1] for c in CASES])
+@pytest.mark.parametrize('act', [0, 2], ids=['sigmoid', 'tanh'])
+@pytest.mark.parametrize('shape', sorted(POINT_SHAPES))
+def test_point_epoch_matches_oracle(engine, sid, name, rows, act, shape):
+    """Tier 3: the single-launch point-tile epoch (matching costs), over
+    several chunks with a ragged tail, against the float64 oracle."""
+    V = len(rows[0])
+    layers = [V] + POINT_SHAPES[shape]
+    linear = [1] + [act] * (len(layers) - 2) + [1]
+    P = 157
+    t, x, weights, net, data = setup(engine, rows, layers, linear, P, 100 + sid + 10 * act)
+    schema = jets.Schema(t[:, 1:])
+    pre, acts = jets.forward(schema, weights, layers, linear, x)
+    targets = (acts[-1] * 0.5).astype(np.float32)
+    tgt = engine.data(targets, t)
+    R, O = len(t), layers[-1]
+    mw = np.random.default_rng(2).uniform(0.5, 1.5, (R, 1, O)).astype(np.float32)
+    cost = engine.matching(net, data, tgt, list(range(R)), list(range(R)), 1, mw, chunk=64)
+    engine.set_tier(3)
+    try:
+        value, grads = engine.graph_evaluate(net, [cost], sum_graph(1))
+    finally:
+        engine.set_tier(0)
+    loss, dout = jets.matching(acts[-1], targets, mw.transpose(0, 2, 1))
+    expected = jets.backward(schema, weights, layers, linear, pre, acts, dout)
+    tol = gc.tolerance(t)
+    assert abs(value - loss) <= tol * abs(loss)
+    assert gc.layer_error(grads, expected) < tol
+
+
+def test_point_epoch_is_the_launched_kernel(engine):
+    """Tier 3 runs the point-tile epoch and its partial sum, nothing per layer."""
+    rows = codegen.SCHEMAS[3][1]
+    layers = [2, 128, 128, 128, 1]
+    t, x, weights, net, data = setup(engine, rows, layers, [1, 0, 0, 0, 1], 300, 7)
+    R = len(t)
+    tgt = engine.data(np.zeros((R, 1, 300), np.float32), t)
+    cost = engine.matching(net, data, tgt, list(range(R)), list(range(R)), 1, np.ones((R, 1, 1), np.float32))
+    engine.set_tier(3)
+    try:
+        engine.timing(True)
+        engine.timing_report()
+        engine.epoch(net, [cost])
+        report = engine.timing_report()
+    finally:
+        engine.timing(False)
+        engine.set_tier(0)
+    assert report['point_epoch'][0] == 1
+    assert not any(k in report for k in ('forward', 'backward', 'weight_gradient', 'head_matching'))
