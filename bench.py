@@ -245,10 +245,12 @@ def run_b200(args):
         import torch.distributed as dist
         from datetime import timedelta
         dist.init_process_group('nccl', timeout=timedelta(seconds=120), device_id=torch.device('cuda', local))
-    from cpde_b200 import native
-    engine = native.Engine(local)
+    from cpde_b200 import native, sharding
+    # N > 1: one point-sharded group; every rank submits the whole N x points
+    # workload and keeps its own contiguous shard of it
+    engine = sharding.engine(local) if dist is not None else native.Engine(local)
     engine.set_tier(args.tier)
-    t, x, targets, weights = workload(args.points)
+    t, x, targets, weights = workload(args.points * world)
     net = engine.network(LAYERS, weights)
     inp = engine.data(x, t)
     tgt = engine.data(targets, t)
@@ -336,7 +338,9 @@ def run_b200(args):
                                 parallelism=f'dp{world}'),
                     e2e=dict(value=world * args.points * R / (e2e_ms / 1000), unit=UNIT,
                              h2d_bytes_per_step=int(pinned_x.numel() * 4 + pinned_t.numel() * 4),
-                             d2h_bytes_per_step=int(params * 4 + 8), timer='host wall clock'),
+                             d2h_bytes_per_step=int(world * (params * 4 + 8)), timer='host wall clock',
+                             note='all ranks together copy the whole input once per step (each its shard) '
+                                  'and each rank reads the all-reduced objective and gradient'),
                     gpu_launches=int(launches), roofline=roofline, clocks=clock,
                     kernels={k: dict(launches=v[0] // args.steps, ms_per_step=v[1] / args.steps)
                              for k, v in sorted(kernels.items())},

@@ -15,6 +15,10 @@ namespace {
 template <class F>
 int guard(cpde_engine* h, F&& f) {
     if (!h) return CPDE_REJECTED;
+    if (!h->engine) {
+        h->error = "the engine was not created";
+        return CPDE_REJECTED;
+    }
     try {
         if (h->engine) CPDE_CUDA(cudaSetDevice(h->engine->device));
         f();
@@ -53,12 +57,47 @@ int cpde_engine_create(int32_t device, cpde_engine** out) {
     return CPDE_OK;
 }
 
-int cpde_engine_create_sharded(int32_t, int32_t, int32_t, const void*, cpde_engine** out) {
-    if (out) *out = nullptr;
-    return CPDE_REJECTED;
+int cpde_engine_create_sharded(int32_t device, int32_t rank, int32_t world, const void* unique_id,
+                               cpde_engine** out) {
+    if (!out) return CPDE_REJECTED;
+    *out = nullptr;
+    auto* h = new cpde_engine;
+    *out = h;
+    try {
+        cpde::require(world >= 1 && rank >= 0 && rank < world && unique_id, "invalid shard rank or group size");
+        h->engine = new cpde::Engine(device);
+        h->engine->join(rank, world, unique_id);
+    } catch (const cpde::DeviceError& e) {
+        h->error = e.what();
+        delete h->engine;
+        h->engine = nullptr;
+        return CPDE_DEVICE_ERROR;
+    } catch (const std::exception& e) {
+        h->error = e.what();
+        delete h->engine;
+        h->engine = nullptr;
+        return CPDE_REJECTED;
+    }
+    return CPDE_OK;
 }
 
-int cpde_sharding_id(void*, size_t) { return CPDE_REJECTED; }
+int cpde_sharding_id(void* unique_id, size_t capacity) {
+    if (!unique_id || capacity < sizeof(ncclUniqueId)) return CPDE_REJECTED;
+    auto& nccl = cpde::Nccl::get();
+    if (!nccl.available()) return CPDE_REJECTED;
+    ncclUniqueId id;
+    if (nccl.get_unique_id(&id) != ncclSuccess) return CPDE_DEVICE_ERROR;
+    std::memcpy(unique_id, &id, sizeof(id));
+    return CPDE_OK;
+}
+
+int cpde_shard_range(int64_t total, int32_t rank, int32_t world, int64_t* lo, int64_t* count) {
+    if (total < 0 || world < 1 || rank < 0 || rank >= world || !lo || !count) return CPDE_REJECTED;
+    const cpde::Shard s = cpde::shard_range(total, rank, world);
+    *lo = s.lo;
+    *count = s.count;
+    return CPDE_OK;
+}
 
 void cpde_engine_destroy(cpde_engine* h) {
     if (!h) return;
@@ -90,16 +129,15 @@ int cpde_data_shape(cpde_engine* h, uint64_t id, int32_t* d, int32_t* c, int32_t
         auto& r = E(h).dat(id);
         *d = r.d;
         *c = r.h;
-        *s = r.w;
+        *s = r.total;
     });
 }
 
 int cpde_data_download(cpde_engine* h, uint64_t id, float* values, size_t count) {
     return guard(h, [&] {
         auto& r = E(h).dat(id);
-        cpde::require(count == r.values.count, "download size mismatch");
-        CPDE_CUDA(cudaStreamSynchronize(E(h).stream));
-        CPDE_CUDA(cudaMemcpy(values, r.values.ptr, count * sizeof(float), cudaMemcpyDeviceToHost));
+        cpde::require(count == size_t(r.d) * r.h * r.total, "download size mismatch");
+        E(h).gather(r, values);
     });
 }
 

@@ -112,6 +112,24 @@ Engine::Engine(int dev) : device(dev) {
     CPDE_CUDA(cudaStreamSynchronize(stream));
 }
 
+// Cost totals <-> the buffers of the group reduction (sample indices made global).
+__global__ void k_pack_costs(const CostStats* totals, const int* offsets, int count, double* values,
+                             long long* keys) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < count; i += blockDim.x * gridDim.x) {
+        const CostStats s = totals[i];
+        values[i] = s.value;
+        keys[i] = bad_entry_key(s.bad_sample == INT_MAX ? INT_MAX : s.bad_sample + offsets[i], s.bad_component);
+    }
+}
+__global__ void k_unpack_costs(CostStats* totals, int count, const double* values, const long long* keys) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < count; i += blockDim.x * gridDim.x) {
+        CostStats s;
+        s.value = values[i];
+        bad_entry_unkey(keys[i], s.bad_sample, s.bad_component);
+        totals[i] = s;
+    }
+}
+
 void Engine::check_device_errors() {
     int code = 0;
     CPDE_CUDA(cudaMemcpyAsync(&code, tc_error.ptr, sizeof(int), cudaMemcpyDeviceToHost, stream));
@@ -123,9 +141,23 @@ void Engine::check_device_errors() {
     }
 }
 
+// Joins a sharded group: one NCCL communicator per engine, on its device.
+void Engine::join(int r, int n, const void* unique_id) {
+    require(n >= 1 && r >= 0 && r < n && unique_id, "invalid shard rank or group size");
+    auto& nccl = Nccl::get();
+    if (!nccl.available()) throw DeviceError(nccl.load_error());
+    ncclUniqueId id;
+    std::memcpy(&id, unique_id, sizeof(id));
+    CPDE_CUDA(cudaSetDevice(device));
+    nccl.check(nccl.comm_init_rank(&comm, n, id, r), "ncclCommInitRank");
+    rank = r;
+    world = n;
+}
+
 Engine::~Engine() {
     cudaSetDevice(device);
     if (stream) cudaStreamSynchronize(stream);
+    if (comm) Nccl::get().comm_destroy(comm);
     costs.clear();
     nets.clear();
     data.clear();
@@ -154,12 +186,16 @@ uint64_t Engine::create_data(int d, int h, int w, int v, const int* table, size_
     require(v > 0 && v <= 26, "invalid variable count");
     require(table_count == size_t(d) * (v + 1) && count == size_t(d) * h * w, "data shape mismatch");
     auto rec = std::unique_ptr<DataRecord>(new DataRecord);
+    const Shard part = shard(w);
     rec->d = d;
     rec->h = h;
-    rec->w = w;
+    rec->w = int(part.count);
+    rec->total = w;
+    rec->lo = int(part.lo);
     rec->v = v;
     rec->table.assign(table, table + table_count);
-    rec->values.upload(values, count, stream);
+    rec->values.resize(size_t(d) * h * part.count);
+    upload_shard(*rec, values);
     CPDE_CUDA(cudaStreamSynchronize(stream));
     uint64_t id = next_id++;
     data[id] = std::move(rec);
@@ -168,10 +204,96 @@ uint64_t Engine::create_data(int d, int h, int w, int v, const int* table, size_
 
 void Engine::replace_data(uint64_t id, const float* values, size_t count) {
     auto& d = dat(id);
-    require(count == d.values.count, "replacement data shape mismatch");
-    CPDE_CUDA(cudaMemcpyAsync(d.values.ptr, values, count * sizeof(float), cudaMemcpyHostToDevice, stream));
+    require(count == size_t(d.d) * d.h * d.total, "replacement data shape mismatch");
+    upload_shard(d, values);
     CPDE_CUDA(cudaStreamSynchronize(stream));
     ++d.version;
+}
+
+// Copies this rank's samples of a host (row, sample, channel) array: one
+// strided copy, a row of the shard per source row.
+void Engine::upload_shard(DataRecord& d, const float* values) {
+    if (d.w == 0) return;
+    const size_t row = size_t(d.w) * d.h * sizeof(float);
+    if (world == 1) {
+        CPDE_CUDA(cudaMemcpyAsync(d.values.ptr, values, row * d.d, cudaMemcpyHostToDevice, stream));
+        return;
+    }
+    CPDE_CUDA(cudaMemcpy2DAsync(d.values.ptr, row, values + size_t(d.lo) * d.h, size_t(d.total) * d.h * sizeof(float),
+                                row, d.d, cudaMemcpyHostToDevice, stream));
+}
+
+// Download of a sharded array: every rank pads its shard to the largest one
+// (rank 0's), one all-gather, then each rank's rows land at their samples.
+void Engine::gather(DataRecord& d, float* host) {
+    CPDE_CUDA(cudaStreamSynchronize(stream));
+    if (world == 1) {
+        CPDE_CUDA(cudaMemcpy(host, d.values.ptr, d.values.count * sizeof(float), cudaMemcpyDeviceToHost));
+        return;
+    }
+    auto& nccl = Nccl::get();
+    const long widest = shard_range(d.total, 0, world).count;
+    const size_t slot = size_t(d.d) * widest * d.h;
+    gather_send.reserve(std::max<size_t>(slot, 1));
+    gather_recv.reserve(std::max<size_t>(slot * world, 1));
+    if (d.w)
+        CPDE_CUDA(cudaMemcpy2DAsync(gather_send.ptr, size_t(widest) * d.h * sizeof(float), d.values.ptr,
+                                    size_t(d.w) * d.h * sizeof(float), size_t(d.w) * d.h * sizeof(float), d.d,
+                                    cudaMemcpyDeviceToDevice, stream));
+    nccl.check(nccl.all_gather(gather_send.ptr, gather_recv.ptr, slot, ncclFloat, comm, stream), "ncclAllGather");
+    for (int q = 0; q < world; ++q) {
+        const Shard s = shard_range(d.total, q, world);
+        if (s.count)
+            CPDE_CUDA(cudaMemcpy2DAsync(host + size_t(s.lo) * d.h, size_t(d.total) * d.h * sizeof(float),
+                                        gather_recv.ptr + slot * q, size_t(widest) * d.h * sizeof(float),
+                                        size_t(s.count) * d.h * sizeof(float), d.d, cudaMemcpyDeviceToHost, stream));
+    }
+    CPDE_CUDA(cudaStreamSynchronize(stream));
+}
+
+// Sums the cost totals over the group: values in double, and the first bad
+// (global sample, component) by an integer minimum of its key.
+void Engine::reduce_costs(NetRecord& n, const std::vector<uint64_t>& ids) {
+    if (world == 1 || ids.empty()) return;
+    auto& nccl = Nccl::get();
+    const int count = int(ids.size());
+    std::vector<int> offsets(count);
+    for (int i = 0; i < count; ++i) {
+        auto& c = cost(ids[i]);
+        offsets[i] = c.input_id ? dat(c.input_id).lo : 0;
+    }
+    shard_offsets.upload(offsets, stream);
+    shard_values.reserve(count);
+    shard_keys.reserve(count);
+    CPDE_RUN(*this, "pack_costs", k_pack_costs<<<grid_for(count), 256, 0, stream>>>(
+                                      n.cost_totals.ptr, shard_offsets.ptr, count, shard_values.ptr, shard_keys.ptr));
+    nccl.check(nccl.group_start(), "ncclGroupStart");
+    nccl.check(nccl.all_reduce(shard_values.ptr, shard_values.ptr, count, ncclDouble, ncclSum, comm, stream),
+               "ncclAllReduce");
+    nccl.check(nccl.all_reduce(shard_keys.ptr, shard_keys.ptr, count, ncclInt64, ncclMin, comm, stream),
+               "ncclAllReduce");
+    nccl.check(nccl.group_end(), "ncclGroupEnd");
+    CPDE_RUN(*this, "unpack_costs", k_unpack_costs<<<grid_for(count), 256, 0, stream>>>(
+                                        n.cost_totals.ptr, count, shard_values.ptr, shard_keys.ptr));
+}
+
+// Sums the weight gradients over the group: one all-reduce over the flat
+// gradient when every layer's active bank is the same buffer.
+void Engine::reduce_gradient(NetRecord& n, float* target) {
+    if (world == 1) return;
+    auto& nccl = Nccl::get();
+    bool uniform = true;
+    for (int l = 1; l < n.layers; ++l) uniform = uniform && n.active[l] == n.active[0];
+    if (target || uniform) {
+        float* g = n.gradient_base(0, target);
+        nccl.check(nccl.all_reduce(g, g, size_t(n.params), ncclFloat, ncclSum, comm, stream), "ncclAllReduce");
+        return;
+    }
+    nccl.check(nccl.group_start(), "ncclGroupStart");
+    for (int l = 0; l < n.layers; ++l)
+        nccl.check(nccl.all_reduce(n.gradient(l), n.gradient(l), size_t(n.count[l]), ncclFloat, ncclSum, comm, stream),
+                   "ncclAllReduce");
+    nccl.check(nccl.group_end(), "ncclGroupEnd");
 }
 
 // ---------------------------------------------------------------------------
@@ -940,8 +1062,8 @@ uint64_t Engine::evaluate(uint64_t ni, uint64_t di, int chunk) {
     auto& n = net(ni);
     auto& input = dat(di);
     require(input.h == n.neurons.front(), "input channel mismatch");
-    int width = chunk ? std::min(chunk, input.w) : input.w;
-    require(width > 0, "invalid chunk size");
+    require((chunk ? std::min(chunk, input.total) : input.total) > 0, "invalid chunk size");
+    int width = std::max(1, chunk ? std::min(chunk, input.w) : input.w);
     auto rows = all_rows(input);
     auto ctx = make_context(input, rows, nonlinear_net(n));
     ensure_arena(n, long(width) * ctx->R(), false);
@@ -949,6 +1071,8 @@ uint64_t Engine::evaluate(uint64_t ni, uint64_t di, int chunk) {
     out->d = input.d;
     out->h = n.neurons.back();
     out->w = input.w;
+    out->total = input.total;
+    out->lo = input.lo;
     out->v = input.v;
     out->table = input.table;
     out->values.resize(size_t(out->d) * out->h * out->w);
@@ -971,6 +1095,24 @@ uint64_t Engine::evaluate(uint64_t ni, uint64_t di, int chunk) {
 // ---------------------------------------------------------------------------
 // costs (cuda/cpde_server.cu:477-482, 489-533)
 
+// Chunk width in samples of this rank's shard (at least 1, so an empty shard
+// runs no chunks); the reference's "invalid chunk size" check applies to the
+// whole data.
+static int chunk_width(const DataRecord& d, int chunk) {
+    require((chunk ? std::min(chunk, d.total) : d.total) > 0, "invalid chunk size");
+    return std::max(1, chunk ? std::min(chunk, d.w) : d.w);
+}
+
+// [rows][samples][inner] host array -> the rows restricted to one shard's samples.
+template <class T>
+static std::vector<T> shard_rows(const std::vector<T>& a, size_t rows, long samples, long inner, Shard part) {
+    std::vector<T> out(rows * size_t(part.count) * inner);
+    for (size_t r = 0; r < rows; ++r)
+        std::copy(a.begin() + (r * samples + part.lo) * inner, a.begin() + (r * samples + part.lo + part.count) * inner,
+                  out.begin() + r * part.count * inner);
+    return out;
+}
+
 uint64_t Engine::cost_matching(uint64_t ni, uint64_t in, uint64_t tgt, int chunk, std::vector<int> rows,
                                std::vector<int> tr, int ws, std::vector<float> w) {
     auto c = std::unique_ptr<CostRecord>(new CostRecord);
@@ -982,16 +1124,19 @@ uint64_t Engine::cost_matching(uint64_t ni, uint64_t in, uint64_t tgt, int chunk
     auto& n = net(ni);
     auto& d = dat(in);
     require(d.h == n.neurons.front(), "input channel mismatch");
-    c->width = chunk ? std::min(chunk, d.w) : d.w;
-    require(c->width > 0, "invalid chunk size");
+    c->width = chunk_width(d, chunk);
     c->context = make_context(d, rows, nonlinear_net(n));
     auto& t = dat(tgt);
-    require(t.h == n.neurons.back() && t.w == d.w, "target shape mismatch");
-    c->weight_samples = ws;
-    require(tr.size() == rows.size() && (ws == 1 || ws == d.w) && w.size() == rows.size() * size_t(ws) * t.h,
+    require(t.h == n.neurons.back() && t.total == d.total, "target shape mismatch");
+    require(tr.size() == rows.size() && (ws == 1 || ws == d.total) && w.size() == rows.size() * size_t(ws) * t.h,
             "matching weight shape mismatch");
     for (int r : tr) require(r >= 0 && r < t.d, "target derivative mismatch");
     for (float x : w) require(std::isfinite(x) && x >= 0, "invalid matching weight");
+    if (ws > 1 && world > 1) {
+        w = shard_rows(w, rows.size(), ws, t.h, shard(ws));
+        ws = d.w;
+    }
+    c->weight_samples = ws;
     c->target_rows.upload(tr, stream);
     c->weights.upload(w, stream);
     CPDE_CUDA(cudaStreamSynchronize(stream));
@@ -1011,12 +1156,11 @@ uint64_t Engine::cost_polynomial(uint64_t ni, uint64_t in, int chunk, std::vecto
     auto& n = net(ni);
     auto& d = dat(in);
     require(d.h == n.neurons.front(), "input channel mismatch");
-    c->width = chunk ? std::min(chunk, d.w) : d.w;
-    require(c->width > 0, "invalid chunk size");
+    c->width = chunk_width(d, chunk);
     c->context = make_context(d, rows, nonlinear_net(n));
     c->equations = equations;
-    require(equations > 0 && raw.size() % 3 == 0 && co.size() == raw.size() / 3 * size_t(d.w) &&
-                rhs.size() == size_t(equations) * d.w && w.size() == rhs.size(),
+    require(equations > 0 && raw.size() % 3 == 0 && co.size() == raw.size() / 3 * size_t(d.total) &&
+                rhs.size() == size_t(equations) * d.total && w.size() == rhs.size(),
             "equation data shape mismatch");
     const long limit = long(rows.size()) * n.neurons.back();
     std::vector<PolyTerm> terms;
@@ -1030,6 +1174,12 @@ uint64_t Engine::cost_polynomial(uint64_t ni, uint64_t in, int chunk, std::vecto
     for (float x : co) require(std::isfinite(x), "invalid coefficient");
     for (float x : rhs) require(std::isfinite(x), "invalid right-hand side");
     c->term_count = int(terms.size());
+    if (world > 1) {
+        const Shard part = shard(d.total);
+        co = shard_rows(co, terms.size(), d.total, 1, part);
+        rhs = shard_rows(rhs, size_t(equations), d.total, 1, part);
+        w = shard_rows(w, size_t(equations), d.total, 1, part);
+    }
     c->terms.upload(terms, stream);
     c->coefficients.upload(co, stream);
     c->rhs.upload(rhs, stream);
@@ -1057,7 +1207,7 @@ uint64_t Engine::cost_integral(uint64_t ni, uint64_t in, int chunk, int samples,
             "invalid expression IR size");
     if (samples) {
         auto& d = dat(in);
-        require(d.h == n.neurons.front() && d.w == samples, "integral input shape mismatch");
+        require(d.h == n.neurons.front() && d.total == samples, "integral input shape mismatch");
         std::vector<int> requested;
         for (size_t i = 0; i < constants.size(); ++i)
             if (raw[3 * i] == 1) {
@@ -1080,7 +1230,7 @@ uint64_t Engine::cost_integral(uint64_t ni, uint64_t in, int chunk, int samples,
             if (needed) c->rows.push_back(row);
         }
         c->context = make_context(d, c->rows, nonlinear_net(n));
-        c->width = chunk ? std::min(chunk, d.w) : d.w;
+        c->width = chunk_width(d, chunk);
     } else {
         require(!in, "empty integral must not have input data");
         c->width = 0;
@@ -1118,6 +1268,12 @@ uint64_t Engine::cost_integral(uint64_t ni, uint64_t in, int chunk, int samples,
     if (found == programs.end())
         found = programs.emplace(source, std::make_shared<ExpressionProgram>(std::move(ir))).first;
     c->program = found->second;
+    if (samples && world > 1) {
+        const Shard part = shard(samples);
+        numeric = shard_rows(numeric, size_t(fields), samples, 1, part);
+        weights = shard_rows(weights, 1, samples, 1, part);
+        c->samples = int(part.count);
+    }
     c->fields.upload(numeric, stream);
     c->quadrature_weights.upload(weights, stream);
     CPDE_CUDA(cudaStreamSynchronize(stream));
@@ -1499,6 +1655,7 @@ void Engine::graph_pass(NetRecord& n, const std::vector<uint64_t>& ids, GraphRec
         last_offset = ((dat(c.input_id).w - 1) / c.width) * c.width;
         pass(n, c, reuse, false, true, nullptr, 0, INT_MAX, false, true, target);
     }
+    reduce_costs(n, ids);  // leaf integrals over all ranks before the graph runs
     run_graph(g, n, int(ids.size()), bwd);
     if (bwd) {
         if (reuse >= 0)
@@ -1508,6 +1665,7 @@ void Engine::graph_pass(NetRecord& n, const std::vector<uint64_t>& ids, GraphRec
             if (!g.schedule[i].known)
                 pass(n, cost(ids[i]), int(i), true, false, g.multipliers.ptr + i, 0,
                      int(i) == reuse ? last_offset : INT_MAX, false, true, target);
+        reduce_gradient(n, target);
     }
     CPDE_CUDA(cudaMemcpyAsync(g.host.ptr, g.summary.ptr, sizeof(GraphRecord::Summary), cudaMemcpyDeviceToHost,
                               stream));
@@ -1530,6 +1688,7 @@ void Engine::evaluate_costs(NetRecord& n, const std::vector<uint64_t>& ids, std:
     begin_costs(n, int(ids.size()));
     for (size_t i = 0; i < ids.size(); ++i)
         pass(n, cost(ids[i]), int(i), false, true, nullptr, 0, INT_MAX, false, false, nullptr);
+    reduce_costs(n, ids);
     download(n, int(ids.size()), 0);
     validate_costs(n, ids.size(), values, false);
 }
@@ -1629,6 +1788,8 @@ void Engine::train(Payload& b, bool graph_mode, const EventSink& emit, const vol
                 CPDE_CUDA(cudaMemsetAsync(n.gradient(l), 0, n.count[l] * 4, stream));
             for (size_t i = 0; i < ids.size(); ++i)
                 pass(n, cost(ids[i]), int(i), true, collect, nullptr, 0, INT_MAX, false, true, nullptr);
+            reduce_gradient(n, nullptr);
+            reduce_costs(n, ids);
         }
         inspect_gradients(n, nullptr);
         download(n, int(ids.size()), n.layers);
@@ -1667,8 +1828,8 @@ void Engine::train(Payload& b, bool graph_mode, const EventSink& emit, const vol
                     auto& c = cost(id);
                     uint64_t output = evaluate(ni, c.input_id, c.width);
                     auto& d = dat(output);
-                    std::vector<float> a(d.values.count);
-                    CPDE_CUDA(cudaMemcpy(a.data(), d.values.ptr, a.size() * 4, cudaMemcpyDeviceToHost));
+                    std::vector<float> a(size_t(d.d) * d.h * d.total);
+                    gather(d, a.data());
                     Payload r;
                     r.put<uint64_t>(id);
                     r.put_array(a);
@@ -1736,6 +1897,8 @@ void Engine::epoch(uint64_t ni, const std::vector<uint64_t>& ids) {
     for (int l = 0; l < n.layers; ++l) CPDE_CUDA(cudaMemsetAsync(n.gradient(l), 0, n.count[l] * 4, stream));
     for (size_t i = 0; i < ids.size(); ++i)
         pass(n, cost(ids[i]), int(i), true, true, nullptr, 0, INT_MAX, false, true, nullptr);
+    reduce_gradient(n, nullptr);
+    reduce_costs(n, ids);
 }
 
 Payload Engine::benchmark(uint64_t ni, uint64_t ci, int warm, int iterations, int batches) {

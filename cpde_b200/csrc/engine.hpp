@@ -13,6 +13,7 @@
 #include <unordered_map>
 #include <vector>
 
+#include "collectives.hpp"
 #include "common.hpp"
 #include "expression.hpp"
 #include "kernels_fast.cuh"
@@ -28,7 +29,8 @@ namespace cpde {
 enum Activation { kSigmoid = 0, kLinear = 1, kTanhAct = 2 };
 
 struct DataRecord {
-    int d = 0, h = 0, w = 0, v = 0;  // derivative rows, channels, samples, variables
+    int d = 0, h = 0, w = 0, v = 0;  // derivative rows, channels, samples (this rank's shard), variables
+    int total = 0, lo = 0;            // samples over all ranks; first sample of this rank's shard
     std::vector<int> table;           // d x (v+1) row-major: order, counts...
     DeviceBuffer<float> values;       // (row, sample, channel)
     uint64_t version = 0;
@@ -143,6 +145,22 @@ class Engine {
     long point_epoch_columns = 16384;  // automatic tier: point-tile epochs up to this many columns per chunk
     std::string last_error;
     DeviceBuffer<int> tc_error;  // nonzero after a tensor-core kernel gave up waiting
+
+    // Point sharding: rank `rank` of `world` engines, one per device, each
+    // holding a contiguous shard of every Data object; gradients and cost
+    // totals are summed over the group with NCCL on this engine's stream.
+    int rank = 0, world = 1;
+    ncclComm_t comm = nullptr;
+    void join(int rank, int world, const void* unique_id);
+    Shard shard(long total) const { return shard_range(total, rank, world); }
+    void reduce_costs(NetRecord& n, const std::vector<uint64_t>& ids);
+    void reduce_gradient(NetRecord& n, float* target);
+    void gather(DataRecord& d, float* host);  // the whole (row, sample, channel) array on every rank
+    void upload_shard(DataRecord& d, const float* values);
+    DeviceBuffer<double> shard_values;
+    DeviceBuffer<long long> shard_keys;
+    DeviceBuffer<int> shard_offsets;
+    DeviceBuffer<float> gather_send, gather_recv;
     void check_device_errors();
 
     uint64_t next_id = 1;

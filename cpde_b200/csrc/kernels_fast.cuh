@@ -141,6 +141,76 @@ struct ColumnLoad {
 };
 
 // ---------------------------------------------------------------------------
+// Narrow first layer (K <= 8 inputs): one loop nest per input width, so no FMA
+// or load is predicated off for the unused inputs (a predicated 8-wide loop
+// issues 2.5x the instructions at K = 2).
+
+// z[r] = sum_k W[m + k M] x[r K + k]
+template <int R, int K>
+__device__ __forceinline__ void input_rows_k(const float* __restrict__ W, int M, int m, const float* x,
+                                             float (&z)[R]) {
+    float w[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) w[k] = __ldg(W + m + (size_t)k * M);
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        float acc = 0.f;
+#pragma unroll
+        for (int k = 0; k < K; ++k) acc = fmaf(w[k], __ldg(x + r * K + k), acc);
+        z[r] = acc;
+    }
+}
+template <int R>
+__device__ __forceinline__ void input_rows(const float* __restrict__ W, int M, int m, int K, const float* x,
+                                           float (&z)[R]) {
+    switch (K) {
+        case 1: input_rows_k<R, 1>(W, M, m, x, z); break;
+        case 2: input_rows_k<R, 2>(W, M, m, x, z); break;
+        case 3: input_rows_k<R, 3>(W, M, m, x, z); break;
+        case 4: input_rows_k<R, 4>(W, M, m, x, z); break;
+        default: {
+            float w[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) w[k] = k < K ? __ldg(W + m + (size_t)k * M) : 0.f;
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                float acc = 0.f;
+#pragma unroll
+                for (int k = 0; k < 8; ++k)
+                    if (k < K) acc = fmaf(w[k], __ldg(x + r * K + k), acc);
+                z[r] = acc;
+            }
+        }
+    }
+}
+
+// gacc[k] += sum_r g[r] x[r K + k] (k < K), gacc[8] += g[0] (bias)
+template <int R, int K>
+__device__ __forceinline__ void input_gradient_k(const float (&g)[R], const float* x, float (&gacc)[9]) {
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int k = 0; k < K; ++k) gacc[k] = fmaf(g[r], __ldg(x + r * K + k), gacc[k]);
+    gacc[8] += g[0];
+}
+template <int R>
+__device__ __forceinline__ void input_gradient(const float (&g)[R], const float* x, int K, float (&gacc)[9]) {
+    switch (K) {
+        case 1: input_gradient_k<R, 1>(g, x, gacc); break;
+        case 2: input_gradient_k<R, 2>(g, x, gacc); break;
+        case 3: input_gradient_k<R, 3>(g, x, gacc); break;
+        case 4: input_gradient_k<R, 4>(g, x, gacc); break;
+        default:
+#pragma unroll
+            for (int r = 0; r < R; ++r)
+#pragma unroll
+                for (int k = 0; k < 8; ++k)
+                    if (k < K) gacc[k] = fmaf(g[r], __ldg(x + r * K + k), gacc[k]);
+            gacc[8] += g[0];
+    }
+}
+
+// ---------------------------------------------------------------------------
 // Hidden layer forward: Y = f(W X + b) with the jet combine in the epilogue.
 // grid = (ceil(P / PTS), ceil(M / 128)). Requires K % 4 == 0.
 
@@ -190,19 +260,8 @@ __global__ void __launch_bounds__(THREADS) k_input_forward(int M, int K, long P,
     for (long e = blockIdx.x * (long)blockDim.x + threadIdx.x; e < total; e += (long)blockDim.x * gridDim.x) {
         const int m = int(e % M);
         const long p = e / M;
-        float w[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) w[k] = k < K ? __ldg(W + m + (size_t)k * M) : 0.f;
-        const float* x = X + (size_t)p * R * K;
         float z[R], y[R];
-#pragma unroll
-        for (int r = 0; r < R; ++r) {
-            float acc = 0.f;
-#pragma unroll
-            for (int k = 0; k < 8; ++k)
-                if (k < K) acc = fmaf(w[k], __ldg(x + r * K + k), acc);
-            z[r] = acc;
-        }
+        input_rows<R>(W, M, m, K, X + (size_t)p * R * K, z);
         z[0] += __ldg(bias + m);
         StaticJet<SID>::template forward<Act>(z, y);
         float* out = Y + (size_t)p * R * M + m;
@@ -260,14 +319,7 @@ __global__ void __launch_bounds__(THREADS, 2) k_backward(int M, int K, long P, c
             }
             StaticJet<SID>::template adjoint<Act>(y, g);
             if (INPUT_GRAD) {
-                const float* x = X0 + (size_t)(p0 + p) * R * K0;
-#pragma unroll
-                for (int r = 0; r < R; ++r) {
-#pragma unroll
-                    for (int k = 0; k < 8; ++k)
-                        if (k < K0) gacc[k] = fmaf(g[r], __ldg(x + r * K0 + k), gacc[k]);
-                }
-                gacc[8] += g[0];
+                input_gradient<R>(g, X0 + (size_t)(p0 + p) * R * K0, K0, gacc);
             } else {
                 float* out = dZprev + ((size_t)(p0 + p) * R) * M + mm;
 #pragma unroll

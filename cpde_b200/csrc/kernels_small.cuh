@@ -354,13 +354,7 @@ __device__ __forceinline__ void hidden_backward(int M, int K, const float* W, co
                 }
                 StaticJet<SID>::template adjoint<Act>(y, g);
                 if (INPUT_GRAD) {
-                    const float* x = X0 + (size_t)(p0 + p) * R * K0;
-#pragma unroll
-                    for (int r = 0; r < R; ++r)
-#pragma unroll
-                        for (int k = 0; k < 8; ++k)
-                            if (k < K0) gacc[k] = fmaf(g[r], __ldcg(x + r * K0 + k), gacc[k]);
-                    gacc[8] += g[0];
+                    fast::input_gradient<R>(g, X0 + (size_t)(p0 + p) * R * K0, K0, gacc);  // inputs: staged before launch
                 } else {
                     float* out = dZprev + ((size_t)(p0 + p) * R) * M + mm;
 #pragma unroll
@@ -413,19 +407,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_point_epoch(EpochNet net, long P
         for (long e = threadIdx.x; e < (long)M * (q1 - q0); e += THREADS) {
             const int m = int(e % M);
             const long p = q0 + e / M;
-            float w[8];
-#pragma unroll
-            for (int k = 0; k < 8; ++k) w[k] = k < K0 ? __ldg(W + m + (size_t)k * M) : 0.f;
-            const float* x = X + (size_t)p * R * K0;
             float z[R], y[R];
-#pragma unroll
-            for (int r = 0; r < R; ++r) {
-                float acc = 0.f;
-#pragma unroll
-                for (int k = 0; k < 8; ++k)
-                    if (k < K0) acc = fmaf(w[k], __ldcg(x + r * K0 + k), acc);
-                z[r] = acc;
-            }
+            fast::input_rows<R>(W, M, m, K0, X + (size_t)p * R * K0, z);  // inputs: staged before launch
             z[0] += __ldg(W + (size_t)M * K0 + m);
             StaticJet<SID>::template forward<Act>(z, y);
             float* out = Y + (size_t)p * R * M + m;

@@ -243,13 +243,7 @@ __global__ void __launch_bounds__(THREADS) k_backward_tc(const __grid_constant__
                 for (int r = 0; r < R; ++r) y[r] = yp[(size_t)r * M];
                 StaticJet<SID>::template adjoint<Act>(y, g);
                 if (INPUT_GRAD) {
-                    const float* x = X0 + (size_t)(p0 + p) * R * K0;
-#pragma unroll
-                    for (int r = 0; r < R; ++r)
-#pragma unroll
-                        for (int k = 0; k < 8; ++k)
-                            if (k < K0) gacc[k] = fmaf(g[r], __ldg(x + r * K0 + k), gacc[k]);
-                    gacc[8] += g[0];
+                    fast::input_gradient<R>(g, X0 + (size_t)(p0 + p) * R * K0, K0, gacc);
                 } else {
                     float* out = dZprev + ((size_t)(p0 + p) * R) * M + m;
 #pragma unroll

@@ -30,6 +30,8 @@ SIGNATURES = {
     'cpde_engine_create': (I32, [I32, ctypes.POINTER(P)]),
     'cpde_engine_create_sharded': (I32, [I32, I32, I32, P, ctypes.POINTER(P)]),
     'cpde_sharding_id': (I32, [P, SZ]),
+    'cpde_shard_range': (I32, [ctypes.c_int64, I32, I32, ctypes.POINTER(ctypes.c_int64),
+                               ctypes.POINTER(ctypes.c_int64)]),
     'cpde_engine_destroy': (None, [P]),
     'cpde_last_error': (ctypes.c_char_p, [P]),
     'cpde_hello': (I32, [P, SINK, P]),
@@ -121,13 +123,39 @@ def jet_plan(counts):
     return out
 
 
-class Engine:
-    """One engine on one CUDA device, driven through the C ABI."""
+def sharding_id():
+    """A fresh 128-byte NCCL group id (rank 0 creates it, every rank joins with it)."""
+    lib = load()
+    buf = ctypes.create_string_buffer(128)
+    status = lib.cpde_sharding_id(buf, 128)
+    if status != OK:
+        raise EngineError(status, 'NCCL is unavailable for sharded engines')
+    return buf.raw
 
-    def __init__(self, device=0):
+
+def shard_range(total, rank, world):
+    """(first sample, sample count) of rank's shard of ``total`` samples."""
+    lo, count = ctypes.c_int64(), ctypes.c_int64()
+    if load().cpde_shard_range(total, rank, world, ctypes.byref(lo), ctypes.byref(count)) != OK:
+        raise ValueError('invalid shard request')
+    return lo.value, count.value
+
+
+class Engine:
+    """One engine on one CUDA device, driven through the C ABI. With
+    ``world > 1`` it is rank ``rank`` of a point-sharded group joined through
+    ``unique_id`` (from :func:`sharding_id` on rank 0): every rank receives the
+    same requests, keeps its own shard of each Data object and sums gradients
+    and cost totals over the group once per epoch."""
+
+    def __init__(self, device=0, rank=0, world=1, unique_id=None):
         self.lib = load()
         handle = ctypes.c_void_p()
-        status = self.lib.cpde_engine_create(device, ctypes.byref(handle))
+        if world > 1:
+            uid = ctypes.create_string_buffer(bytes(unique_id), 128)
+            status = self.lib.cpde_engine_create_sharded(device, rank, world, uid, ctypes.byref(handle))
+        else:
+            status = self.lib.cpde_engine_create(device, ctypes.byref(handle))
         self.handle = handle
         if status != OK:
             message = self.lib.cpde_last_error(handle).decode() if handle else 'engine creation failed'

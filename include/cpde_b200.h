@@ -57,6 +57,10 @@ int cpde_engine_create(int32_t device, cpde_engine** engine);
 int cpde_engine_create_sharded(int32_t device, int32_t rank, int32_t world, const void* unique_id,
                                cpde_engine** engine);
 int cpde_sharding_id(void* unique_id, size_t capacity);
+/* The contiguous sample range [lo, lo + count) that rank `rank` of `world`
+ * holds of a Data object with `total` samples (remainder spread over the first
+ * ranks). Host only; no device or engine needed. New. */
+int cpde_shard_range(int64_t total, int32_t rank, int32_t world, int64_t* lo, int64_t* count);
 
 void cpde_engine_destroy(cpde_engine* engine);
 const char* cpde_last_error(const cpde_engine* engine);
