@@ -635,6 +635,19 @@ struct FastForward {
                 CPDE_RUN(e, "input_forward",
                          (k_input_forward<SID, Act><<<grid_for(long(M) * P, THREADS, 148 * 32), THREADS, 0,
                                                       e.stream>>>(M, K, P, W, b, n.act[0].ptr, n.act[1].ptr)));
+            } else if (tensor && M % tcg::BM == 0 && K % tcg::KS == 0 && K <= ws::kMaxK) {
+                // warp-specialised: weights resident in tensor memory, slab ring in shared memory
+                using WT = ws::Tiling<R>;
+                static bool ws_ready[64] = {};
+                if (!ws_ready[e.device & 63]) {
+                    allow_smem(ws::k_forward_ws<SID, Act>, WT::SMEM);
+                    ws_ready[e.device & 63] = true;
+                }
+                const CUtensorMap mx = tensor_map(n.act[l - 1].ptr, K, P * R, WT::N);
+                const long tiles = (P + WT::PTS - 1) / WT::PTS;
+                dim3 grid(unsigned(std::min<long>(tiles, std::max(1, 148 / (M / tcg::BM)))), unsigned(M / tcg::BM));
+                CPDE_RUN(e, "forward_ws", (ws::k_forward_ws<SID, Act><<<grid, ws::THREADS, WT::SMEM, e.stream>>>(
+                                              mx, M, K, P, W, n.act[l].ptr, e.tc_error.ptr)));
             } else if (tensor && M % tcg::BM == 0 && K % tcg::KS == 0) {
                 using TT = tcg::Tiling<R>;
                 static bool tc_ready[64] = {};

@@ -19,6 +19,7 @@
 #include "kernels_fast.cuh"
 #include "kernels_small.cuh"
 #include "kernels_tc.cuh"
+#include "kernels_ws.cuh"
 #include "kernels_generic.cuh"
 #include "scalar.hpp"
 #include "schema.hpp"

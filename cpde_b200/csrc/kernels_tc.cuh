@@ -14,6 +14,7 @@
 // memory is released and the CTA returns. The host checks the code.
 #pragma once
 #include "generated/jets_static.cuh"
+#include "kernels_fast.cuh"
 #include "kernels_generic.cuh"
 #include "tc.cuh"
 

@@ -50,6 +50,24 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, long l
     return true;
 }
 
+// As mbar_wait, but also gives up as soon as *abort becomes nonzero (another
+// role of the CTA timed out); a timeout here raises *abort itself.
+__device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parity, long long limit,
+                                                   volatile int* abort) {
+    const long long start = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (*abort) return false;
+        if (clock64() - start > limit) {
+            *abort = 1;
+            return false;
+        }
+    }
+    return true;
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 // --- TMA ---------------------------------------------------------------------
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
     asm volatile(
@@ -109,6 +127,16 @@ __device__ __forceinline__ void tmem_ld1(uint32_t taddr, float& v) {
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// 32 lanes x 8 consecutive 32-bit columns from registers; thread i writes lane base+i.
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const float (&v)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr),
+                 "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+                 "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+                 "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7]))
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 // Reads columns [col, col + COUNT) of this thread's lane into v (COUNT <= 64).
 template <int COUNT>
 __device__ __forceinline__ void tmem_read(uint32_t taddr, float (&v)[COUNT]) {
@@ -164,6 +192,17 @@ __device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint6
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}" ::"r"(d_tmem),
         "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(mask)
+        : "memory");
+}
+// Same with A read from tensor memory (K-major: lane = row, one column per K element).
+__device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    uint32_t mask = 0;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, {%5, %5, %5, %5}, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(mask)
         : "memory");
 }
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
