@@ -599,6 +599,22 @@ static CUtensorMap raw_map(const float* base, int inner, long rows) {
     return map;
 }
 
+// Box of 32 neurons x 32 columns in the 128-byte swizzle with 32-byte atoms
+// (MN-major TF32 operands of the weight-gradient kernel).
+static CUtensorMap mn32_map(const float* base, int inner, long rows) {
+    CUtensorMap map;
+    cuuint64_t dims[2] = {cuuint64_t(inner), cuuint64_t(rows)};
+    cuuint64_t strides[1] = {cuuint64_t(inner) * sizeof(float)};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t element_strides[2] = {1, 1};
+    driver_check(driver_api().encode_tiled(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims,
+                                           strides, box, element_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                           CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE),
+                 "cuTensorMapEncodeTiled");
+    return map;
+}
+
 bool Engine::fast_ok(NetRecord& n, Context& ctx) const {
     if (tier == 1 || ctx.static_id < 0) return false;
     const int L = n.layers;
@@ -750,7 +766,23 @@ struct FastBackward {
             splits = (cols + per - 1) / per;
             n.partial.reserve(size_t(splits) * M * (N + 1));
             dim3 wg(unsigned(splits), (N + BM - 1) / BM, (M + BM - 1) / BM);
-            if (tc_wgrad) {
+            if (tc_wgrad && M == tcg::BM) {
+                // warp-specialised: dZ through registers into tensor memory, Y_prev MN-major from TMA
+                static bool wg_ready[64] = {};
+                if (!wg_ready[e.device & 63]) {
+                    allow_smem(ws::k_wgrad_ws, ws::kWgSmem);
+                    wg_ready[e.device & 63] = true;
+                }
+                const int ny = N / tcg::BM;
+                long ws_splits = std::max(1L, std::min<long>(148 / ny, (cols + 127) / 128));
+                const long ws_per = ((cols + ws_splits - 1) / ws_splits + 31) / 32 * 32;
+                splits = (cols + ws_per - 1) / ws_per;
+                n.partial.reserve(size_t(splits) * M * (N + 1));
+                const CUtensorMap md = mn32_map(cur, M, cols), ma = mn32_map(n.act[l - 1].ptr, N, cols);
+                CPDE_RUN(e, "weight_gradient_ws",
+                         (ws::k_wgrad_ws<<<dim3(unsigned(splits), unsigned(ny)), ws::kWgThreads, ws::kWgSmem,
+                                           e.stream>>>(md, ma, N, cols, R, ws_per, n.partial.ptr, e.tc_error.ptr)));
+            } else if (tc_wgrad) {
                 const CUtensorMap md = raw_map(cur, M, cols), ma = raw_map(n.act[l - 1].ptr, N, cols);
                 CPDE_RUN(e, "weight_gradient_tc",
                          (tcg::k_weight_gradient_tc<<<wg, tcg::THREADS, tcg::kWgSmem, e.stream>>>(
@@ -768,6 +800,36 @@ struct FastBackward {
             const bool input = l - 1 == 1;
             float* next = cur == n.dz[0].ptr ? n.dz[1].ptr : n.dz[0].ptr;
             const int K0 = n.neurons[0];
+            if (tensor && N % tcg::BM == 0 && M % tcg::KS == 0 && M <= ws::kMaxK) {
+                // warp-specialised: W^T resident in tensor memory, dZ slab ring in shared memory
+                using WT = ws::Tiling<R>;
+                static bool bw_ready[64] = {};
+                if (!bw_ready[e.device & 63]) {
+                    allow_smem(ws::k_backward_ws<SID, Act, false>, WT::SMEM);
+                    allow_smem(ws::k_backward_ws<SID, Act, true>, WT::SMEM);
+                    bw_ready[e.device & 63] = true;
+                }
+                const CUtensorMap mz = tensor_map(cur, M, cols, WT::N);
+                const long tt = (P + WT::PTS - 1) / WT::PTS;
+                const int bx = int(std::min<long>(tt, std::max(1, 148 / (N / tcg::BM))));
+                dim3 grid(bx, N / tcg::BM);
+                if (input) {
+                    n.input_partial.reserve(size_t(2 * bx) * N * (K0 + 1));
+                    CPDE_RUN(e, "backward_input_ws",
+                             (ws::k_backward_ws<SID, Act, true><<<grid, ws::THREADS, WT::SMEM, e.stream>>>(
+                                 mz, M, N, P, W, n.act[1].ptr, nullptr, n.act[0].ptr, K0, n.input_partial.ptr,
+                                 e.tc_error.ptr)));
+                    long isize = long(N) * (K0 + 1);
+                    CPDE_RUN(e, "sum_partials", (k_sum_partials<<<fast::sum_grid(isize), 256, 0, e.stream>>>(
+                                                    n.input_partial.ptr, 2 * bx, isize, n.gradient_base(0, target))));
+                } else {
+                    CPDE_RUN(e, "backward_ws",
+                             (ws::k_backward_ws<SID, Act, false><<<grid, ws::THREADS, WT::SMEM, e.stream>>>(
+                                 mz, M, N, P, W, n.act[l - 1].ptr, next, nullptr, 0, nullptr, e.tc_error.ptr)));
+                    cur = next;
+                }
+                continue;
+            }
             if (tensor && N % tcg::BM == 0 && M % tcg::KS == 0) {
                 using TT = tcg::Tiling<R>;
                 float* hi = n.wb_hi.ptr + n.offset[l - 1];

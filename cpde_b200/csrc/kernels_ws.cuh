@@ -49,6 +49,40 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
     return __all_sync(0xffffffffu, ok);
 }
 
+// TF32 hi (in place) and lo of float4 elements [0, count) of h4 strided over
+// 128 threads, eight loads in flight per thread; elements for which
+// keep(i) is false become zero in both.
+template <class Keep>
+__device__ __forceinline__ void split_range(float4* h4, float4* l4, int count, int tid, Keep keep) {
+    constexpr int U = 8;
+    for (int base = 0; base < count; base += 128 * U) {
+        float4 v[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int i = base + tid + 128 * u;
+            v[u] = i < count ? h4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int i = base + tid + 128 * u;
+            if (i >= count) break;
+            float4 h = make_float4(0.f, 0.f, 0.f, 0.f), l = h;
+            if (keep(i)) {
+                h.x = tc::tf32_round(v[u].x);
+                h.y = tc::tf32_round(v[u].y);
+                h.z = tc::tf32_round(v[u].z);
+                h.w = tc::tf32_round(v[u].w);
+                l.x = tc::tf32_round(v[u].x - h.x);
+                l.y = tc::tf32_round(v[u].y - h.y);
+                l.z = tc::tf32_round(v[u].z - h.z);
+                l.w = tc::tf32_round(v[u].w - h.w);
+            }
+            h4[i] = h;
+            l4[i] = l;
+        }
+    }
+}
+
 struct Ring {
     float *hi, *lo;  // [STAGES][SLAB / 4]
     uint64_t *full, *split, *empty, *acc_full, *acc_empty, *a_ready, *drain;
@@ -129,21 +163,8 @@ __device__ __forceinline__ void split_all(const Ring& r, long tiles, int N, int 
         for (int s = 0; s < slabs; ++s, ++it) {
             const int st = it % STAGES;
             if (!warp_wait(r.full + st, (it / STAGES) & 1, r.abort)) return;
-            float4* h4 = reinterpret_cast<float4*>(r.hi + st * (SLAB / 4));
-            float4* l4 = reinterpret_cast<float4*>(r.lo + st * (SLAB / 4));
-            for (int i = tid; i < N * 8; i += 128) {
-                float4 v = h4[i], h, l;
-                h.x = tc::tf32_round(v.x);
-                h.y = tc::tf32_round(v.y);
-                h.z = tc::tf32_round(v.z);
-                h.w = tc::tf32_round(v.w);
-                l.x = tc::tf32_round(v.x - h.x);
-                l.y = tc::tf32_round(v.y - h.y);
-                l.z = tc::tf32_round(v.z - h.z);
-                l.w = tc::tf32_round(v.w - h.w);
-                h4[i] = h;
-                l4[i] = l;
-            }
+            split_range(reinterpret_cast<float4*>(r.hi + st * (SLAB / 4)),
+                        reinterpret_cast<float4*>(r.lo + st * (SLAB / 4)), N * 8, tid, [](int) { return true; });
             tc::fence_proxy_async();
             __syncwarp();
             if ((threadIdx.x & 31) == 0) tc::mbar_arrive(r.split + st);
@@ -186,18 +207,19 @@ __device__ __forceinline__ void issue_mmas(const Ring& r, uint32_t tmem, long ti
     tc::mbar_wait(r.drain, 0, tcg::kWaitCycles);
 }
 
-// Epilogue warps 6-9: this CTA's 128 weight rows (column-major W with leading
-// dimension M) split into TF32 hi and lo, into tensor memory columns [0, K)
-// and [128, 128 + K) of the thread's lane.
+// Epilogue warps 6-9: the A operand's row `m` (K values) split into TF32 hi
+// and lo, into tensor memory columns [0, K) and [128, 128 + K) of the thread's
+// lane. The forward's A is W (column-major, leading dimension M: row m holds
+// W[m + k M]); the backward's is W^T (row n holds W[k + n K], contiguous).
 __device__ __forceinline__ void load_weights(const Ring& r, uint32_t tmem, const float* __restrict__ W, int M,
-                                             int K, int m) {
+                                             int K, int m, bool transposed = false) {
     const int quarter = (threadIdx.x >> 5) & 3;
     const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
     for (int c0 = 0; c0 < K; c0 += 8) {
         float h[8], l[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            const float v = __ldg(W + m + (size_t)(c0 + j) * M);
+            const float v = transposed ? __ldg(W + (size_t)m * K + c0 + j) : __ldg(W + m + (size_t)(c0 + j) * M);
             h[j] = tc::tf32_round(v);
             l[j] = tc::tf32_round(v - h[j]);
         }
@@ -269,6 +291,254 @@ __global__ void __launch_bounds__(THREADS, 1) k_forward_ws(const __grid_constant
         }
     }
     teardown(r, tmem, error);
+}
+
+// Hidden layer backward: dZ_prev = adjoint(W^T dZ; Y_prev), the jet adjoint
+// in the epilogue. The GEMM is the forward's with A = W^T (rows = the N
+// previous-layer neurons of this CTA's slice, K = Ml neurons of this layer)
+// and B = the dZ slabs. With INPUT_GRAD the previous layer is the first hidden
+// one: dZ_prev is not stored and the first layer's gradient is accumulated
+// per thread into input_partials[2 blockIdx.x + group][n + k N] (bias at
+// k = K0), one partial per epilogue group.
+// grid = (CTAs over column tiles, N / 128); Ml a multiple of 32, at most 128.
+template <int SID, class Act, bool INPUT_GRAD>
+__global__ void __launch_bounds__(THREADS, 1) k_backward_ws(const __grid_constant__ CUtensorMap map_dz, int Ml, int N,
+                                                            long P, const float* __restrict__ W,
+                                                            const float* __restrict__ Yprev,
+                                                            float* __restrict__ dZprev, const float* __restrict__ X0,
+                                                            int K0, float* __restrict__ input_partials, int* error) {
+    constexpr int R = StaticJet<SID>::R;
+    using T = Tiling<R>;
+    extern __shared__ uint8_t smem_raw[];
+    Ring r = carve_ring<T::SLAB>(smem_raw);
+    ring_init(r);
+    const uint32_t tmem = *r.tmem_slot;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long tiles = (P + T::PTS - 1) / T::PTS;
+    const int slabs = Ml / 32;
+    if (warp == kProducerWarp) {
+        if (lane == 0) produce<T::SLAB>(r, &map_dz, tiles, T::COLS, T::N, slabs);
+    } else if (warp == kMmaWarp) {
+        if (lane == 0) issue_mmas<T::N, T::SLAB>(r, tmem, tiles, slabs);
+    } else if (warp < kEpilogueWarp) {
+        split_all<T::SLAB>(r, tiles, T::N, slabs);
+    } else {
+        const int quarter = warp & 3, group = (warp - kEpilogueWarp) >> 2;
+        const int n = blockIdx.y * 128 + quarter * 32 + lane;
+        if (group == 0) load_weights(r, tmem, W, N, Ml, n, true);
+        const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
+        float gacc[9];
+#pragma unroll
+        for (int k = 0; k < 9; ++k) gacc[k] = 0.f;
+        uint32_t local = 0;
+        for (long tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
+            const int a = local & 1;
+            if (!warp_wait(r.acc_full + a, (local >> 1) & 1, r.abort)) break;
+            tc::tc_fence_after();
+            const long p0 = tile * T::PTS;
+            for (int p = group; p < T::PTS; p += kEpilogueGroups) {
+                if (p0 + p >= P) break;
+                float g[R], y[R];
+                tc::tmem_read<R>(lane_base + kAccColumn + a * 128 + p * R, g);
+                const float* yp = Yprev + ((size_t)(p0 + p) * R) * N + n;
+#pragma unroll
+                for (int q = 0; q < R; ++q) y[q] = __ldg(yp + (size_t)q * N);
+                StaticJet<SID>::template adjoint<Act>(y, g);
+                if (INPUT_GRAD) {
+                    fast::input_gradient<R>(g, X0 + (size_t)(p0 + p) * R * K0, K0, gacc);
+                } else {
+                    float* out = dZprev + ((size_t)(p0 + p) * R) * N + n;
+#pragma unroll
+                    for (int q = 0; q < R; ++q) out[(size_t)q * N] = g[q];
+                }
+            }
+            tc::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(r.acc_empty + a);
+        }
+        if (INPUT_GRAD) {
+            float* out = input_partials + (size_t)(2 * blockIdx.x + group) * N * (K0 + 1);
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+                if (k < K0) out[n + (size_t)k * N] = gacc[k];
+            out[n + (size_t)K0 * N] = gacc[8];
+        }
+    }
+    teardown(r, tmem, error);
+}
+
+// ---------------------------------------------------------------------------
+// Weight gradient of a hidden layer of 128 neurons: G (128 x a 128-neuron
+// slice of the previous layer, plus the bias column) = sum over this CTA's
+// column range of dZ[:, c] Y_prev[:, c]^T. Per 32-column stage, TMA brings 4
+// boxes of 32 neurons x 32 columns of each operand (128-byte swizzle with
+// 32-byte atoms, the layout of MN-major TF32 operands). The split warps move
+// dZ through registers into tensor memory as the K-major A operand (thread =
+// neuron: its 32 columns, TF32 hi and lo, plus its bias sum over value-row
+// columns) while the epilogue warps split Y_prev in place into hi and lo as
+// the MN-major B operand, so shared memory carries each operand once per MMA
+// term instead of also serving the A side. The 128 x 128 accumulator stays in
+// tensor memory for the whole range. grid = (column splits, N / 128);
+// per_split a multiple of 32.
+
+constexpr int kWgStages = 4;
+constexpr int kWgBox = 32 * 32 * 4;       // 32 neurons x 32 columns
+constexpr int kWgOperand = 4 * kWgBox;    // 128 neurons
+constexpr int kWgStage = 3 * kWgOperand;  // dZ raw, Y hi, Y lo
+constexpr int kWgSmem = kWgStages * kWgStage + 1024 + 256;
+constexpr int kWgThreads = 320;  // producer, MMA, 4 split warps, 4 epilogue warps
+constexpr uint32_t kWgAccColumns = 128, kWgTmemColumns = 512;
+
+// element (mn, k) of such an operand, in floats from its start
+__device__ __forceinline__ int mn32_index(int mn, int k) {
+    return (mn >> 5) * (kWgBox / 4) + k * 32 + ((((mn & 31) >> 3) ^ (k & 3)) << 3) + (mn & 7);
+}
+
+__global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_constant__ CUtensorMap map_dz,
+                                                            const __grid_constant__ CUtensorMap map_y, int N,
+                                                            long columns, int R, long per_split,
+                                                            float* __restrict__ partials, int* error) {
+    constexpr int M = 128;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(base + kWgStages * kWgStage);
+    uint64_t *full = bars, *split = bars + kWgStages, *empty = bars + 2 * kWgStages, *drain = bars + 3 * kWgStages;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kWgStages; ++s) {
+            tc::mbar_init(full + s, 1);
+            tc::mbar_init(split + s, 8);
+            tc::mbar_init(empty + s, 1);
+        }
+        tc::mbar_init(drain, 1);
+        *abort = 0;
+        tc::fence_barrier_init();
+    }
+    if (warp == kMmaWarp) {
+        tc::tmem_alloc(tmem_slot, kWgTmemColumns);
+        tc::tmem_relinquish();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const int n_base = blockIdx.y * 128;
+    const long c_begin = (long)blockIdx.x * per_split, c_end = min(columns, c_begin + per_split);
+    const int chunks = c_begin < c_end ? int((c_end - c_begin + 31) / 32) : 0;
+    // stage st: [dZ raw][Y hi][Y lo]; tensor memory: G [0, 128), stage st's dZ hi/lo at 128 + 64 st (+32)
+    auto stage_ptr = [&](int st, int part) { return reinterpret_cast<float*>(base + st * kWgStage + part * kWgOperand); };
+    auto dz_column = [](int st) { return kWgAccColumns + 64u * uint32_t(st); };
+    float* out = partials + (size_t)blockIdx.x * M * (N + 1);
+    if (warp == kProducerWarp) {
+        if (lane == 0) {
+            int it = 0;
+            for (; it < chunks && !*abort; ++it) {
+                const int st = it % kWgStages;
+                if (!tc::mbar_wait_or_abort(empty + st, ((it / kWgStages) & 1) ^ 1, tcg::kWaitCycles, abort)) break;
+                tc::mbar_expect_tx(full + st, 2 * kWgOperand);
+                const int c0 = int(c_begin + 32L * it);
+                for (int j = 0; j < 4; ++j) {
+                    tc::tma_load_2d(stage_ptr(st, 0) + j * (kWgBox / 4), &map_dz, full + st, 32 * j, c0);
+                    tc::tma_load_2d(stage_ptr(st, 1) + j * (kWgBox / 4), &map_y, full + st, n_base + 32 * j, c0);
+                }
+            }
+            for (int k = it > kWgStages ? it - kWgStages : 0; k < it; ++k)
+                tc::mbar_wait(full + k % kWgStages, (k / kWgStages) & 1, tcg::kWaitCycles);
+        }
+    } else if (warp == kMmaWarp) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = tc::idesc_tf32(M, 128) | (1u << 16);  // B (Y) MN-major, A (dZ) from TMEM
+            for (int it = 0; it < chunks; ++it) {
+                const int st = it % kWgStages;
+                if (!tc::mbar_wait_or_abort(split + st, (it / kWgStages) & 1, tcg::kWaitCycles, abort)) break;
+                tc::tc_fence_after();
+                const uint32_t yh = tc::smem_u32(stage_ptr(st, 1)), yl = tc::smem_u32(stage_ptr(st, 2));
+                const uint32_t ah = tmem + dz_column(st), al = ah + 32;
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                    const uint32_t off = kk * 1024;  // 8 columns of Y
+                    tc::mma_tf32_ts(tmem, al + kk * 8, tc::desc_mn32_sw128(yh + off, kWgBox), idesc, (it | kk) != 0);
+                    tc::mma_tf32_ts(tmem, ah + kk * 8, tc::desc_mn32_sw128(yl + off, kWgBox), idesc, 1);
+                    tc::mma_tf32_ts(tmem, ah + kk * 8, tc::desc_mn32_sw128(yh + off, kWgBox), idesc, 1);
+                }
+                tc::mma_commit(empty + st);
+            }
+            tc::mma_commit(drain);
+            tc::mbar_wait(drain, 0, tcg::kWaitCycles);
+        }
+    } else if (warp < kEpilogueWarp) {
+        // split warps: thread = neuron m (its TMEM lane); the stage's dZ row of
+        // that neuron into tensor memory (hi, lo) and its bias over value-row columns
+        const int quarter = warp & 3, m = quarter * 32 + lane;
+        const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
+        float bias = 0.f;
+        for (int it = 0; it < chunks; ++it) {
+            const int st = it % kWgStages;
+            if (!warp_wait(full + st, (it / kWgStages) & 1, abort)) break;
+            tc::tc_fence_after();
+            const long c0 = c_begin + 32L * it;
+            const int valid = int(min(32L, c_end - c0));
+            const int first = int((R - c0 % R) % R);  // first value-row column of the stage
+            const float* z = stage_ptr(st, 0);
+            for (int c = first; c < valid; c += R) bias += z[mn32_index(m, c)];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                float h[8], l[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const int c = 8 * q + j;
+                    const float v = c < valid ? z[mn32_index(m, c)] : 0.f;
+                    h[j] = tc::tf32_round(v);
+                    l[j] = tc::tf32_round(v - h[j]);
+                }
+                tc::tmem_st8(lane_base + dz_column(st) + 8 * q, h);
+                tc::tmem_st8(lane_base + dz_column(st) + 32 + 8 * q, l);
+            }
+            tc::tmem_wait_st();
+            tc::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(split + st);
+        }
+        if (blockIdx.y == 0) out[(size_t)N * M + m] = bias;
+    } else {
+        // epilogue warps: split Y_prev of every stage in place, then write the
+        // accumulator (lane m, column n) into the partial
+        const int quarter = warp & 3, m = quarter * 32 + lane, tid = threadIdx.x - kEpilogueWarp * 32;
+        for (int it = 0; it < chunks; ++it) {
+            const int st = it % kWgStages;
+            if (!warp_wait(full + st, (it / kWgStages) & 1, abort)) break;
+            const int valid = int(min(32L, c_end - (c_begin + 32L * it)));
+            split_range(reinterpret_cast<float4*>(stage_ptr(st, 1)), reinterpret_cast<float4*>(stage_ptr(st, 2)),
+                        kWgOperand / 16, tid, [valid](int i) { return ((i >> 3) & 31) < valid; });
+            tc::fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(split + st);
+        }
+        if (warp_wait(drain, 0, abort)) {
+            tc::tc_fence_after();
+            const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
+            for (int c0 = 0; c0 < 128; c0 += 16) {
+                float v[16];
+                if (chunks) {
+                    tc::tmem_read<16>(lane_base + c0, v);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) v[j] = 0.f;
+                }
+#pragma unroll
+                for (int j = 0; j < 16; ++j) out[m + (size_t)(n_base + c0 + j) * M] = v[j];
+            }
+        }
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == kMmaWarp) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, kWgTmemColumns);
+    }
+    if (threadIdx.x == 0 && *abort) atomicExch(error, tcg::kErrMma);
 }
 
 }  // namespace ws

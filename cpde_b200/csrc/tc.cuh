@@ -180,6 +180,21 @@ __device__ __forceinline__ uint64_t desc_k_sw128(uint32_t smem_addr) {
     return d;
 }
 
+// MN-major TF32 operand in the 128-byte swizzle with 32-byte atoms (layout
+// type 1): rows of 128 bytes hold 32 consecutive M (or N) elements of one K
+// index, the 32-byte chunk index of a row xor (row % 4); 4-row groups 512
+// bytes apart along K (stride byte offset), 32-element MN blocks `mn_stride`
+// bytes apart (leading byte offset).
+__device__ __forceinline__ uint64_t desc_mn32_sw128(uint32_t smem_addr, uint32_t mn_stride) {
+    uint64_t d = 0;
+    d |= uint64_t((smem_addr >> 4) & 0x3FFFu);
+    d |= uint64_t((mn_stride >> 4) & 0x3FFFu) << 16;
+    d |= uint64_t(512u >> 4) << 32;
+    d |= uint64_t(1u) << 46;
+    d |= uint64_t(1u) << 61;
+    return d;
+}
+
 __host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {
     return (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
 }
