@@ -774,14 +774,12 @@ struct FastBackward {
                     wg_ready[e.device & 63] = true;
                 }
                 const int ny = N / tcg::BM;
-                long ws_splits = std::max(1L, std::min<long>(148 / ny, (cols + 127) / 128));
-                const long ws_per = ((cols + ws_splits - 1) / ws_splits + 31) / 32 * 32;
-                splits = (cols + ws_per - 1) / ws_per;
+                splits = std::max(1L, std::min<long>(148 / ny, (cols + 31) / 32));
                 n.partial.reserve(size_t(splits) * M * (N + 1));
                 const CUtensorMap md = mn32_map(cur, M, cols), ma = mn32_map(n.act[l - 1].ptr, N, cols);
                 CPDE_RUN(e, "weight_gradient_ws",
                          (ws::k_wgrad_ws<<<dim3(unsigned(splits), unsigned(ny)), ws::kWgThreads, ws::kWgSmem,
-                                           e.stream>>>(md, ma, N, cols, R, ws_per, n.partial.ptr, e.tc_error.ptr)));
+                                           e.stream>>>(md, ma, N, cols, R, n.partial.ptr, e.tc_error.ptr)));
             } else if (tc_wgrad) {
                 const CUtensorMap md = raw_map(cur, M, cols), ma = raw_map(n.act[l - 1].ptr, N, cols);
                 CPDE_RUN(e, "weight_gradient_tc",

@@ -370,7 +370,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_backward_ws(const __grid_constan
 // ---------------------------------------------------------------------------
 // Weight gradient of a hidden layer of 128 neurons: G (128 x a 128-neuron
 // slice of the previous layer, plus the bias column) = sum over this CTA's
-// column range of dZ[:, c] Y_prev[:, c]^T. Per 32-column stage, TMA brings 4
+// columns of dZ[:, c] Y_prev[:, c]^T. Per 32-column stage, TMA brings 4
 // boxes of 32 neurons x 32 columns of each operand (128-byte swizzle with
 // 32-byte atoms, the layout of MN-major TF32 operands). The split warps move
 // dZ through registers into tensor memory as the K-major A operand (thread =
@@ -378,8 +378,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_backward_ws(const __grid_constan
 // columns) while the epilogue warps split Y_prev in place into hi and lo as
 // the MN-major B operand, so shared memory carries each operand once per MMA
 // term instead of also serving the A side. The 128 x 128 accumulator stays in
-// tensor memory for the whole range. grid = (column splits, N / 128);
-// per_split a multiple of 32.
+// tensor memory for the whole kernel. grid = (CTAs, N / 128).
 
 constexpr int kWgStages = 4;
 constexpr int kWgBox = 32 * 32 * 4;       // 32 neurons x 32 columns
@@ -396,8 +395,8 @@ __device__ __forceinline__ int mn32_index(int mn, int k) {
 
 __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_constant__ CUtensorMap map_dz,
                                                             const __grid_constant__ CUtensorMap map_y, int N,
-                                                            long columns, int R, long per_split,
-                                                            float* __restrict__ partials, int* error) {
+                                                            long columns, int R, float* __restrict__ partials,
+                                                            int* error) {
     constexpr int M = 128;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -425,8 +424,11 @@ __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_constan
     tc::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     const int n_base = blockIdx.y * 128;
-    const long c_begin = (long)blockIdx.x * per_split, c_end = min(columns, c_begin + per_split);
-    const int chunks = c_begin < c_end ? int((c_end - c_begin + 31) / 32) : 0;
+    // 32-column chunks dealt round-robin over the CTAs, so the whole grid
+    // streams through one region of both operands at a time
+    const long total_chunks = (columns + 31) / 32;
+    const int chunks = blockIdx.x < total_chunks ? int((total_chunks - 1 - blockIdx.x) / gridDim.x + 1) : 0;
+    auto chunk_start = [&](int it) { return 32L * ((long)blockIdx.x + (long)it * gridDim.x); };
     // stage st: [dZ raw][Y hi][Y lo]; tensor memory: G [0, 128), stage st's dZ hi/lo at 128 + 64 st (+32)
     auto stage_ptr = [&](int st, int part) { return reinterpret_cast<float*>(base + st * kWgStage + part * kWgOperand); };
     auto dz_column = [](int st) { return kWgAccColumns + 64u * uint32_t(st); };
@@ -438,7 +440,7 @@ __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_constan
                 const int st = it % kWgStages;
                 if (!tc::mbar_wait_or_abort(empty + st, ((it / kWgStages) & 1) ^ 1, tcg::kWaitCycles, abort)) break;
                 tc::mbar_expect_tx(full + st, 2 * kWgOperand);
-                const int c0 = int(c_begin + 32L * it);
+                const int c0 = int(chunk_start(it));
                 for (int j = 0; j < 4; ++j) {
                     tc::tma_load_2d(stage_ptr(st, 0) + j * (kWgBox / 4), &map_dz, full + st, 32 * j, c0);
                     tc::tma_load_2d(stage_ptr(st, 1) + j * (kWgBox / 4), &map_y, full + st, n_base + 32 * j, c0);
@@ -478,8 +480,8 @@ __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_constan
             const int st = it % kWgStages;
             if (!warp_wait(full + st, (it / kWgStages) & 1, abort)) break;
             tc::tc_fence_after();
-            const long c0 = c_begin + 32L * it;
-            const int valid = int(min(32L, c_end - c0));
+            const long c0 = chunk_start(it);
+            const int valid = int(min(32L, columns - c0));
             const int first = int((R - c0 % R) % R);  // first value-row column of the stage
             const float* z = stage_ptr(st, 0);
             for (int c = first; c < valid; c += R) bias += z[mn32_index(m, c)];
@@ -509,7 +511,7 @@ __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_constan
         for (int it = 0; it < chunks; ++it) {
             const int st = it % kWgStages;
             if (!warp_wait(full + st, (it / kWgStages) & 1, abort)) break;
-            const int valid = int(min(32L, c_end - (c_begin + 32L * it)));
+            const int valid = int(min(32L, columns - chunk_start(it)));
             split_range(reinterpret_cast<float4*>(stage_ptr(st, 1)), reinterpret_cast<float4*>(stage_ptr(st, 2)),
                         kWgOperand / 16, tid, [valid](int i) { return ((i >> 3) & 31) < valid; });
             tc::fence_proxy_async();
