@@ -541,13 +541,35 @@ __global__ void __launch_bounds__(THREADS) k_output_backward(int O, int K, long 
         for (int o = 0; o < O; ++o) out[o + (size_t)K * O] = gb[o] + red[o][0];
 }
 
+// Sum over the 32 lanes of a warp of each of 32 per-lane values, transposed:
+// afterwards lane i holds the warp sum of v[i] in v[0] (31 shuffles in all,
+// recursive halving: the lanes of each pair keep the half their index bit
+// selects and add the partner's copy of it).
+__device__ __forceinline__ float warp_transpose_sum(float (&v)[32]) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+        const bool upper = lane & off;
+#pragma unroll
+        for (int j = 0; j < off; ++j) {
+            const float send = upper ? v[j] : v[j + off];
+            const float keep = upper ? v[j + off] : v[j];
+            v[j] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+        }
+    }
+    return v[0];
+}
+
 // Fused output head for a matching cost: Z_out = W_out Y + b for O linear
 // outputs, the squared-error loss and its adjoints (the arithmetic and order of
 // k_cost_matching, cuda/cost_kernels.cuh:6-35), the output layer's weight
 // gradient, dY = W_out^T dZ_out and the jet adjoint into the last hidden layer,
 // all from one read of that layer's jets. One thread owns neurons
-// t + 128 j (j < KPT, K = 128 KPT); a CTA walks points, reducing the output
-// dot products across its 4 warps through shared memory.
+// t + 128 j (j < KPT, K = 128 KPT); a CTA walks points. Per point the O x R
+// output dot products are reduced within each warp by transposed butterflies
+// and across the 4 warps in shared memory; thread v < O R then owns output
+// component v (row v % R, output v / R): its residual, loss term and gradient,
+// which every thread reads back for the adjoint.
 // partials[cta][o + m O] (bias at m = K) are summed by k_sum_partials.
 template <int SID, class Act, int O, int KPT>
 __global__ void __launch_bounds__(BM) k_head_matching(int K, long P, int offset, const float* __restrict__ W,
@@ -558,7 +580,12 @@ __global__ void __launch_bounds__(BM) k_head_matching(int K, long P, int offset,
                                                       const double* __restrict__ multiplier, int collect,
                                                       CostReduce red, float* __restrict__ partials) {
     constexpr int R = StaticJet<SID>::R;
-    __shared__ float sums[4][O * R];
+    constexpr int V = O * R;              // output components of a point, at most BM
+    constexpr int GROUPS = (V + 31) / 32;
+    static_assert(V <= BM, "one thread per output component");
+    __shared__ float sums[4][GROUPS * 32];
+    __shared__ float grads[V];
+    __shared__ float values[4];
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
     float w[KPT][O], gw[KPT][O];
 #pragma unroll
@@ -568,12 +595,13 @@ __global__ void __launch_bounds__(BM) k_head_matching(int K, long P, int offset,
             w[j][o] = __ldg(W + o + (size_t)(t + BM * j) * O);
             gw[j][o] = 0.f;
         }
-    float bias[O], gb[O];
+    // thread t < V: output component (row d, output o); its bias and target row
+    const int d_own = t % R, o_own = t / R;
+    const float bias_own = t < V ? __ldg(W + (size_t)K * O + o_own) : 0.f;
+    const int trow = t < V ? __ldg(target_rows + d_own) : 0;
+    float gb[O];
 #pragma unroll
-    for (int o = 0; o < O; ++o) {
-        bias[o] = __ldg(W + (size_t)K * O + o);
-        gb[o] = 0.f;
-    }
+    for (int o = 0; o < O; ++o) gb[o] = 0.f;
     const double scale = multiplier ? *multiplier : 1.0;
     CostStats local = cost_empty();
     for (long p = blockIdx.x; p < P; p += gridDim.x) {
@@ -583,53 +611,51 @@ __global__ void __launch_bounds__(BM) k_head_matching(int K, long P, int offset,
 #pragma unroll
             for (int r = 0; r < R; ++r) y[j][r] = __ldg(Y + ((size_t)p * R + r) * K + t + BM * j);
 #pragma unroll
+        for (int g = 0; g < GROUPS; ++g) {
+            float v[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                const int c = g * 32 + i, o = c / R, r = c % R;
+                float a = 0.f;
+                if (c < V)
+#pragma unroll
+                    for (int j = 0; j < KPT; ++j) a = fmaf(w[j][o], y[j][r], a);
+                v[i] = a;
+            }
+            sums[warp][g * 32 + lane] = warp_transpose_sum(v);
+        }
+        __syncthreads();
+        float value = 0.f;
+        if (t < V) {
+            const float z = sums[0][t] + sums[1][t] + sums[2][t] + sums[3][t] + (d_own == 0 ? bias_own : 0.f);
+            const int wp = weight_samples == 1 ? 0 : offset + int(p);
+            const float wt = __ldg(weights + ((size_t)d_own * weight_samples + wp) * O + o_own);
+            float grad = 0.f;
+            if (wt != 0.f) {
+                const float res = z - __ldg(target + ((size_t)trow * target_samples + offset + p) * O + o_own);
+                value = wt * res * res;
+                grad = 2.0f * wt * res;
+            }
+            if (!isfinite(grad)) mark_bad(local, offset + int(p), d_own * O + o_own);
+            if (multiplier) grad = scale == 0 ? 0.f : float(grad * scale);
+            grads[t] = grad;
+        }
+#pragma unroll
+        for (int sft = 16; sft; sft >>= 1) value += __shfl_xor_sync(0xffffffffu, value, sft);
+        if (lane == 0) values[warp] = value;
+        __syncthreads();
+        if (t == 0) {
+            const float total = values[0] + values[1] + values[2] + values[3];
+            if (!isfinite(total)) mark_bad(local, offset + int(p), -1);
+            if (collect) local.value += double(total);
+        }
+        float gr[O][R];
+#pragma unroll
         for (int o = 0; o < O; ++o)
 #pragma unroll
-            for (int r = 0; r < R; ++r) {
-                float v = 0.f;
+            for (int r = 0; r < R; ++r) gr[o][r] = grads[o * R + r];
 #pragma unroll
-                for (int j = 0; j < KPT; ++j) v = fmaf(w[j][o], y[j][r], v);
-#pragma unroll
-                for (int sft = 16; sft; sft >>= 1) v += __shfl_xor_sync(0xffffffffu, v, sft);
-                if (lane == 0) sums[warp][o * R + r] = v;
-            }
-        __syncthreads();
-        float g[O][R];
-        float value = 0.f;
-        const int wp = weight_samples == 1 ? 0 : offset + int(p);
-#pragma unroll
-        for (int d = 0; d < R; ++d)
-#pragma unroll
-            for (int o = 0; o < O; ++o) {
-                const float z = sums[0][o * R + d] + sums[1][o * R + d] + sums[2][o * R + d] +
-                                sums[3][o * R + d] + (d == 0 ? bias[o] : 0.f);
-                const float wt = __ldg(weights + ((size_t)d * weight_samples + wp) * O + o);
-                float grad = 0.f;
-                if (wt != 0.f) {
-                    const float res =
-                        z - __ldg(target + ((size_t)__ldg(target_rows + d) * target_samples + offset + p) * O + o);
-                    value += wt * res * res;
-                    grad = 2.0f * wt * res;
-                }
-                g[o][d] = grad;
-            }
-        __syncthreads();  // sums is rewritten by the next point
-        if (t == 0) {
-            if (!isfinite(value)) mark_bad(local, offset + int(p), -1);
-            if (collect) local.value += double(value);
-#pragma unroll
-            for (int d = 0; d < R; ++d)
-#pragma unroll
-                for (int o = 0; o < O; ++o)
-                    if (!isfinite(g[o][d])) mark_bad(local, offset + int(p), d * O + o);
-        }
-        if (multiplier)
-#pragma unroll
-            for (int o = 0; o < O; ++o)
-#pragma unroll
-                for (int d = 0; d < R; ++d) g[o][d] = scale == 0 ? 0.f : float(g[o][d] * scale);
-#pragma unroll
-        for (int o = 0; o < O; ++o) gb[o] += g[o][0];
+        for (int o = 0; o < O; ++o) gb[o] += gr[o][0];
 #pragma unroll
         for (int j = 0; j < KPT; ++j) {
             float dy[R];
@@ -638,8 +664,8 @@ __global__ void __launch_bounds__(BM) k_head_matching(int K, long P, int offset,
                 float acc = 0.f;
 #pragma unroll
                 for (int o = 0; o < O; ++o) {
-                    acc = fmaf(w[j][o], g[o][r], acc);
-                    gw[j][o] = fmaf(g[o][r], y[j][r], gw[j][o]);
+                    acc = fmaf(w[j][o], gr[o][r], acc);
+                    gw[j][o] = fmaf(gr[o][r], y[j][r], gw[j][o]);
                 }
                 dy[r] = acc;
             }
