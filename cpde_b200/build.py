@@ -2,9 +2,12 @@
 
     python -m cpde_b200.build
 
-nvcc cross-compiles without a GPU. The library is one translation unit
-(csrc/library.cu); the server is a host program linked against it with an
-$ORIGIN-relative rpath so the pair can be moved together.
+nvcc cross-compiles without a GPU. The library is four translation units
+compiled in parallel (csrc/library.cu: engine core, C ABI, allocation-free
+entry; fast_forward.cu, fast_backward.cu, fast_head.cu: the fast-tier
+dispatch and the kernels it instantiates); the server is a host program
+linked against it with an $ORIGIN-relative rpath so the pair can be moved
+together.
 """
 import os
 import subprocess
@@ -15,7 +18,9 @@ PACKAGE = Path(__file__).resolve().parent
 CSRC = PACKAGE / 'csrc'
 LIBRARY = PACKAGE / 'libcpde_b200.so'
 SERVER = PACKAGE / 'bin' / 'cpde_server'
+BUILD = PACKAGE / '_build'
 ARCH = ['-gencode', 'arch=compute_100a,code=sm_100a']
+UNITS = ['library', 'fast_forward', 'fast_backward', 'fast_head']
 
 
 def _run(cmd):
@@ -38,12 +43,24 @@ def build(force=False, verbose_ptxas=False):
     sources += sorted((CSRC / 'generated').glob('*.cuh'))
     sources.append(PACKAGE.parent / 'include' / 'cpde_b200.h')
     if force or _stale(LIBRARY, sources):
-        cmd = [nvcc, *ARCH, '-lineinfo', '-O3', '-std=c++17', '-Xcompiler', '-fPIC', '-shared',
-               f'--split-compile={os.cpu_count() or 1}',
-               '--expt-relaxed-constexpr', '-o', LIBRARY, CSRC / 'library.cu', '-lnvrtc']
-        if verbose_ptxas:
-            cmd.insert(1, '-Xptxas=-v')
-        _run(cmd)
+        # One object per translation unit, compiled in parallel; each unit is
+        # compiled whole (no --split-compile, whose partitioning changed the
+        # code of unrelated kernels from one build to the next).
+        BUILD.mkdir(exist_ok=True)
+        procs, objects = [], []
+        for unit in UNITS:
+            obj = BUILD / (unit + '.o')
+            cmd = [nvcc, *ARCH, '-lineinfo', '-O3', '-std=c++17', '-Xcompiler', '-fPIC', '-c',
+                   '--expt-relaxed-constexpr', '-o', obj, CSRC / (unit + '.cu')]
+            if verbose_ptxas:
+                cmd.insert(1, '-Xptxas=-v')
+            print(' '.join(map(str, cmd)), flush=True)
+            procs.append(subprocess.Popen([str(c) for c in cmd]))
+            objects.append(obj)
+        failed = [unit for unit, proc in zip(UNITS, procs) if proc.wait() != 0]
+        if failed:
+            raise RuntimeError(f'nvcc failed on {", ".join(failed)}')
+        _run([nvcc, *ARCH, '-shared', '-o', LIBRARY, *objects, '-lnvrtc'])
     SERVER.parent.mkdir(exist_ok=True)
     server_sources = [CSRC / 'server_main.cpp', CSRC / 'wire.hpp', CSRC / 'common.hpp', LIBRARY]
     if force or _stale(SERVER, server_sources):

@@ -9,73 +9,9 @@
 #include <cmath>
 #include <numeric>
 
-#include "engine.hpp"
+#include "engine_internal.hpp"
 
 namespace cpde {
-
-// ---------------------------------------------------------------------------
-// kernel timing
-
-struct KernelTimer {
-    struct Mark {
-        const char* name;
-        cudaEvent_t start, stop;
-    };
-    std::vector<Mark> marks;
-    std::vector<cudaEvent_t> pool;
-    cudaEvent_t get() {
-        if (!pool.empty()) {
-            auto e = pool.back();
-            pool.pop_back();
-            return e;
-        }
-        cudaEvent_t e;
-        CPDE_CUDA(cudaEventCreate(&e));
-        return e;
-    }
-    struct Totals {
-        long launches = 0;
-        double ms = 0;
-    };
-    std::map<std::string, Totals> totals;
-    void collect() {
-        for (auto& m : marks) {
-            CPDE_CUDA(cudaEventSynchronize(m.stop));
-            float ms = 0;
-            CPDE_CUDA(cudaEventElapsedTime(&ms, m.start, m.stop));
-            auto& t = totals[m.name];
-            t.launches += 1;
-            t.ms += ms;
-            pool.push_back(m.start);
-            pool.push_back(m.stop);
-        }
-        marks.clear();
-    }
-    ~KernelTimer() {
-        for (auto& m : marks) {
-            cudaEventDestroy(m.start);
-            cudaEventDestroy(m.stop);
-        }
-        for (auto e : pool) cudaEventDestroy(e);
-    }
-};
-
-#define CPDE_RUN(engine, name, ...)                                           \
-    do {                                                                      \
-        KernelTimer* t_ = (engine).timer.get();                               \
-        cudaEvent_t a_ = nullptr, b_ = nullptr;                               \
-        if (t_) {                                                             \
-            a_ = t_->get();                                                   \
-            b_ = t_->get();                                                   \
-            CPDE_CUDA(cudaEventRecord(a_, (engine).stream));                  \
-        }                                                                     \
-        __VA_ARGS__;                                                          \
-        CPDE_LAUNCHED();                                                      \
-        if (t_) {                                                             \
-            CPDE_CUDA(cudaEventRecord(b_, (engine).stream));                  \
-            t_->marks.push_back({name, a_, b_});                              \
-        }                                                                     \
-    } while (0)
 
 void Engine::timing(bool enable) {
     if (enable && !timer) timer.reset(new KernelTimer);
@@ -92,10 +28,6 @@ std::string Engine::timing_report() {
     return out;
 }
 
-static int grid_for(long count, int threads = 256, int cap = 148 * 16) {
-    long g = (count + threads - 1) / threads;
-    return int(std::max(1L, std::min<long>(g, cap)));
-}
 
 // ---------------------------------------------------------------------------
 // construction and lookup
@@ -546,75 +478,6 @@ void Engine::backward(NetRecord& n, Context& ctx, int points, float* target) {
 }
 
 
-// ---------------------------------------------------------------------------
-// fast tier dispatch
-
-static_assert(kStaticSchemas == 10, "update CPDE_STATIC_CASES after changing the generated schemas");
-#define CPDE_STATIC_CASES(X) X(0) X(1) X(2) X(3) X(4) X(5) X(6) X(7) X(8) X(9)
-
-template <class F>
-static void with_schema(int sid, F&& f) {
-    switch (sid) {
-#define CPDE_CASE(i) \
-    case i:          \
-        f.template run<i>(); \
-        return;
-        CPDE_STATIC_CASES(CPDE_CASE)
-#undef CPDE_CASE
-    }
-    throw DeviceError("unknown static schema");
-}
-
-template <class K>
-static void allow_smem(K kernel, size_t bytes) {
-    CPDE_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes)));
-}
-
-static CUtensorMap tensor_map(const float* base, int inner, long rows, int box_rows) {
-    CUtensorMap map;
-    cuuint64_t dims[2] = {cuuint64_t(inner), cuuint64_t(rows)};
-    cuuint64_t strides[1] = {cuuint64_t(inner) * sizeof(float)};
-    cuuint32_t box[2] = {cuuint32_t(tcg::KS), cuuint32_t(box_rows)};
-    cuuint32_t element_strides[2] = {1, 1};
-    driver_check(driver_api().encode_tiled(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims,
-                                           strides, box, element_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE),
-                 "cuTensorMapEncodeTiled");
-    return map;
-}
-
-// Unswizzled box of 128 neurons x 32 columns (raw slabs of the weight-gradient kernel).
-static CUtensorMap raw_map(const float* base, int inner, long rows) {
-    CUtensorMap map;
-    cuuint64_t dims[2] = {cuuint64_t(inner), cuuint64_t(rows)};
-    cuuint64_t strides[1] = {cuuint64_t(inner) * sizeof(float)};
-    cuuint32_t box[2] = {cuuint32_t(tcg::BM), cuuint32_t(tcg::KS)};
-    cuuint32_t element_strides[2] = {1, 1};
-    driver_check(driver_api().encode_tiled(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims,
-                                           strides, box, element_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                                           CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE),
-                 "cuTensorMapEncodeTiled");
-    return map;
-}
-
-// Box of 32 neurons x 32 columns in the 128-byte swizzle with 32-byte atoms
-// (MN-major TF32 operands of the weight-gradient kernel).
-static CUtensorMap mn32_map(const float* base, int inner, long rows) {
-    CUtensorMap map;
-    cuuint64_t dims[2] = {cuuint64_t(inner), cuuint64_t(rows)};
-    cuuint64_t strides[1] = {cuuint64_t(inner) * sizeof(float)};
-    cuuint32_t box[2] = {32, 32};
-    cuuint32_t element_strides[2] = {1, 1};
-    driver_check(driver_api().encode_tiled(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims,
-                                           strides, box, element_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                                           CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE),
-                 "cuTensorMapEncodeTiled");
-    return map;
-}
-
 bool Engine::fast_ok(NetRecord& n, Context& ctx) const {
     if (tier == 1 || ctx.static_id < 0) return false;
     const int L = n.layers;
@@ -622,386 +485,6 @@ bool Engine::fast_ok(NetRecord& n, Context& ctx) const {
     for (int l = 1; l < L; ++l)
         if (n.linear[l] == 1 || n.linear[l] != n.linear[1] || n.neurons[l] % 32 != 0) return false;
     return true;
-}
-
-namespace {
-struct FastForward {
-    Engine& e;
-    NetRecord& n;
-    long P;
-    bool tensor;  // tcgen05 3xTF32 GEMMs where the shapes allow
-    bool hidden_only;  // leave the output layer to a fused head
-    template <int SID, class Act>
-    void layers() {
-        using namespace fast;
-        constexpr int R = StaticJet<SID>::R;
-        using T = Tiling<R>;
-        const size_t smem = Smem<T::BN>::FLOATS * sizeof(float);
-        static bool ready[64] = {};
-        if (!ready[e.device & 63]) {
-            allow_smem(k_forward<SID, Act>, smem);
-            ready[e.device & 63] = true;
-        }
-        const int L = n.layers;
-        for (int l = 1; l < L; ++l) {
-            const int M = n.neurons[l], K = n.neurons[l - 1];
-            const float* W = n.weights(l - 1);
-            const float* b = W + long(M) * K;
-            if (l == 1) {
-                CPDE_RUN(e, "input_forward",
-                         (k_input_forward<SID, Act><<<grid_for(long(M) * P, THREADS, 148 * 32), THREADS, 0,
-                                                      e.stream>>>(M, K, P, W, b, n.act[0].ptr, n.act[1].ptr)));
-            } else if (tensor && M % tcg::BM == 0 && K % tcg::KS == 0 && K <= ws::kMaxK) {
-                // warp-specialised: weights resident in tensor memory, slab ring in shared memory
-                using WT = ws::Tiling<R>;
-                static bool ws_ready[64] = {};
-                if (!ws_ready[e.device & 63]) {
-                    allow_smem(ws::k_forward_ws<SID, Act>, WT::SMEM);
-                    ws_ready[e.device & 63] = true;
-                }
-                const CUtensorMap mx = tensor_map(n.act[l - 1].ptr, K, P * R, WT::N);
-                const long tiles = (P + WT::PTS - 1) / WT::PTS;
-                dim3 grid(unsigned(std::min<long>(tiles, std::max(1, 148 / (M / tcg::BM)))), unsigned(M / tcg::BM));
-                CPDE_RUN(e, "forward_ws", (ws::k_forward_ws<SID, Act><<<grid, ws::THREADS, WT::SMEM, e.stream>>>(
-                                              mx, M, K, P, W, n.act[l].ptr, e.tc_error.ptr)));
-            } else if (tensor && M % tcg::BM == 0 && K % tcg::KS == 0) {
-                using TT = tcg::Tiling<R>;
-                static bool tc_ready[64] = {};
-                if (!tc_ready[e.device & 63]) {
-                    allow_smem(tcg::k_forward_tc<SID, Act>, TT::SMEM);
-                    tc_ready[e.device & 63] = true;
-                }
-                n.w_hi.reserve(n.params);
-                n.w_lo.reserve(n.params);
-                float* hi = n.w_hi.ptr + n.offset[l - 1];
-                float* lo = n.w_lo.ptr + n.offset[l - 1];
-                CPDE_RUN(e, "split_weights", (tcg::k_split_tf32<<<grid_for(long(M) * K), 256, 0, e.stream>>>(
-                                                 W, hi, lo, M, K, 1)));
-                const CUtensorMap mh = tensor_map(hi, K, M, tcg::BM), ml = tensor_map(lo, K, M, tcg::BM);
-                const CUtensorMap mx = tensor_map(n.act[l - 1].ptr, K, P * R, TT::N);
-                const long tiles = (P + TT::PTS - 1) / TT::PTS;
-                dim3 grid(unsigned(std::min<long>(tiles, std::max(1, 444 / (M / tcg::BM)))), unsigned(M / tcg::BM));
-                CPDE_RUN(e, "forward_tc",
-                         (tcg::k_forward_tc<SID, Act><<<grid, tcg::THREADS, TT::SMEM, e.stream>>>(
-                             mh, ml, mx, M, K, P, b, n.act[l].ptr, e.tc_error.ptr)));
-            } else {
-                dim3 grid(unsigned((P + T::PTS - 1) / T::PTS), unsigned((M + BM - 1) / BM));
-                CPDE_RUN(e, "forward",
-                         (k_forward<SID, Act><<<grid, THREADS, smem, e.stream>>>(M, K, P, W, b, n.act[l - 1].ptr,
-                                                                                  n.act[l].ptr)));
-            }
-        }
-        if (hidden_only) return;
-        const int O = n.neurons[L], K = n.neurons[L - 1];
-        const float* W = n.weights(L - 1);
-        CPDE_RUN(e, "output_forward",
-                 (k_output_forward<<<grid_for(P * R * 32, THREADS, 148 * 64), THREADS, 0, e.stream>>>(
-                     O, K, P, R, W, W + long(O) * K, n.act[L - 1].ptr, n.act[L].ptr)));
-    }
-    template <int SID>
-    void run() {
-        if (n.linear[1] == kTanhAct) layers<SID, Tanh>();
-        else layers<SID, Sigmoid>();
-    }
-};
-
-struct FastBackward {
-    Engine& e;
-    NetRecord& n;
-    long P;
-    float* target;
-    bool use_tensor;
-    bool skip_output;  // a fused head already produced dZ of the last hidden layer
-    template <int SID, class Act>
-    void layers() {
-        using namespace fast;
-        constexpr int R = StaticJet<SID>::R;
-        using T = Tiling<R>;
-        const size_t smem = Smem<T::BN>::FLOATS * sizeof(float);
-        static bool ready[64] = {};
-        if (!ready[e.device & 63]) {
-            allow_smem(k_backward<SID, Act, false>, smem);
-            allow_smem(k_backward<SID, Act, true>, smem);
-            ready[e.device & 63] = true;
-        }
-        const int L = n.layers;
-        const long cols = P * R;
-        // output layer: adjoint into the last hidden layer, output weight gradient
-        if (!skip_output) {
-            const int O = n.neurons[L], K = n.neurons[L - 1];
-            const int bx = int(std::min<long>(148 * 4, std::max(1L, (P + 15) / 16)));
-            dim3 grid(bx, (K + BM - 1) / BM);
-            n.partial.reserve(size_t(bx) * O * (K + 1));
-            CPDE_RUN(e, "output_backward",
-                     (k_output_backward<SID, Act><<<grid, THREADS, 0, e.stream>>>(
-                         O, K, P, n.weights(L - 1), n.dz[0].ptr, n.act[L - 1].ptr, n.dz[1].ptr, n.partial.ptr)));
-            long size = long(O) * (K + 1);
-            CPDE_RUN(e, "sum_partials", (k_sum_partials<<<fast::sum_grid(size), 256, 0, e.stream>>>(
-                                            n.partial.ptr, bx, size, n.gradient_base(L - 1, target))));
-        }
-        float* cur = n.dz[1].ptr;
-        const bool tensor = use_tensor;
-        if (tensor) {
-            static bool tc_ready[64] = {};
-            if (!tc_ready[e.device & 63]) {
-                using TT = tcg::Tiling<R>;
-                allow_smem(tcg::k_backward_tc<SID, Act, false>, TT::SMEM);
-                allow_smem(tcg::k_backward_tc<SID, Act, true>, TT::SMEM);
-                allow_smem(tcg::k_weight_gradient_tc, tcg::kWgSmem);
-                tc_ready[e.device & 63] = true;
-            }
-            n.wb_hi.reserve(n.params);
-            n.wb_lo.reserve(n.params);
-        }
-        for (int l = L - 1; l >= 2; --l) {
-            const int M = n.neurons[l], N = n.neurons[l - 1];
-            // weight gradient of layer l (M x N plus bias), split over columns
-            // enough column splits to fill two CTAs per SM, but at least 64
-            // columns (FFMA) or 128 columns (tensor cores) per split
-            const int tiles = ((N + BM - 1) / BM) * ((M + BM - 1) / BM);
-            const bool tc_wgrad = tensor && M % tcg::BM == 0 && N % tcg::BM == 0;
-            const long min_cols = tc_wgrad ? 128 : 64, align = tc_wgrad ? tcg::KS : BK;
-            long splits = std::max(1L, std::min<long>((2L * 148 + tiles - 1) / tiles, (cols + min_cols - 1) / min_cols));
-            long per = ((cols + splits - 1) / splits + align - 1) / align * align;
-            splits = (cols + per - 1) / per;
-            n.partial.reserve(size_t(splits) * M * (N + 1));
-            dim3 wg(unsigned(splits), (N + BM - 1) / BM, (M + BM - 1) / BM);
-            if (tc_wgrad && M == tcg::BM) {
-                // warp-specialised: dZ through registers into tensor memory, Y_prev MN-major from TMA
-                static bool wg_ready[64] = {};
-                if (!wg_ready[e.device & 63]) {
-                    allow_smem(ws::k_wgrad_ws, ws::kWgSmem);
-                    wg_ready[e.device & 63] = true;
-                }
-                const int ny = N / tcg::BM;
-                splits = std::max(1L, std::min<long>(148 / ny, (cols + 31) / 32));
-                n.partial.reserve(size_t(splits) * M * (N + 1));
-                const CUtensorMap md = mn32_map(cur, M, cols), ma = mn32_map(n.act[l - 1].ptr, N, cols);
-                CPDE_RUN(e, "weight_gradient_ws",
-                         (ws::k_wgrad_ws<<<dim3(unsigned(splits), unsigned(ny)), ws::kWgThreads, ws::kWgSmem,
-                                           e.stream>>>(md, ma, N, cols, R, n.partial.ptr, e.tc_error.ptr)));
-            } else if (tc_wgrad) {
-                const CUtensorMap md = raw_map(cur, M, cols), ma = raw_map(n.act[l - 1].ptr, N, cols);
-                CPDE_RUN(e, "weight_gradient_tc",
-                         (tcg::k_weight_gradient_tc<<<wg, tcg::THREADS, tcg::kWgSmem, e.stream>>>(
-                             md, ma, M, N, cols, R, per, n.partial.ptr, e.tc_error.ptr)));
-            } else {
-                CPDE_RUN(e, "weight_gradient", (k_weight_gradient<<<wg, THREADS, 0, e.stream>>>(
-                                                   M, N, cols, R, per, cur, n.act[l - 1].ptr, n.partial.ptr)));
-            }
-            long size = long(M) * (N + 1);
-            CPDE_RUN(e, "sum_partials", (k_sum_partials<<<fast::sum_grid(size), 256, 0, e.stream>>>(
-                                            n.partial.ptr, int(splits), size, n.gradient_base(l - 1, target))));
-            // adjoint into layer l-1
-            const float* W = n.weights(l - 1);
-            const long tiles_p = (P + T::PTS - 1) / T::PTS;
-            const bool input = l - 1 == 1;
-            float* next = cur == n.dz[0].ptr ? n.dz[1].ptr : n.dz[0].ptr;
-            const int K0 = n.neurons[0];
-            if (tensor && N % tcg::BM == 0 && M % tcg::KS == 0 && M <= ws::kMaxK) {
-                // warp-specialised: W^T resident in tensor memory, dZ slab ring in shared memory
-                using WT = ws::Tiling<R>;
-                static bool bw_ready[64] = {};
-                if (!bw_ready[e.device & 63]) {
-                    allow_smem(ws::k_backward_ws<SID, Act, false>, WT::SMEM);
-                    allow_smem(ws::k_backward_ws<SID, Act, true>, WT::SMEM);
-                    bw_ready[e.device & 63] = true;
-                }
-                const CUtensorMap mz = tensor_map(cur, M, cols, WT::N);
-                const long tt = (P + WT::PTS - 1) / WT::PTS;
-                const int bx = int(std::min<long>(tt, std::max(1, 148 / (N / tcg::BM))));
-                dim3 grid(bx, N / tcg::BM);
-                if (input) {
-                    n.input_partial.reserve(size_t(2 * bx) * N * (K0 + 1));
-                    CPDE_RUN(e, "backward_input_ws",
-                             (ws::k_backward_ws<SID, Act, true><<<grid, ws::THREADS, WT::SMEM, e.stream>>>(
-                                 mz, M, N, P, W, n.act[1].ptr, nullptr, n.act[0].ptr, K0, n.input_partial.ptr,
-                                 e.tc_error.ptr)));
-                    long isize = long(N) * (K0 + 1);
-                    CPDE_RUN(e, "sum_partials", (k_sum_partials<<<fast::sum_grid(isize), 256, 0, e.stream>>>(
-                                                    n.input_partial.ptr, 2 * bx, isize, n.gradient_base(0, target))));
-                } else {
-                    CPDE_RUN(e, "backward_ws",
-                             (ws::k_backward_ws<SID, Act, false><<<grid, ws::THREADS, WT::SMEM, e.stream>>>(
-                                 mz, M, N, P, W, n.act[l - 1].ptr, next, nullptr, 0, nullptr, e.tc_error.ptr)));
-                    cur = next;
-                }
-                continue;
-            }
-            if (tensor && N % tcg::BM == 0 && M % tcg::KS == 0) {
-                using TT = tcg::Tiling<R>;
-                float* hi = n.wb_hi.ptr + n.offset[l - 1];
-                float* lo = n.wb_lo.ptr + n.offset[l - 1];
-                CPDE_RUN(e, "split_weights", (tcg::k_split_tf32<<<grid_for(long(M) * N), 256, 0, e.stream>>>(
-                                                 W, hi, lo, N, M, 0)));
-                const CUtensorMap mh = tensor_map(hi, M, N, tcg::BM), ml = tensor_map(lo, M, N, tcg::BM);
-                const CUtensorMap mz = tensor_map(cur, M, cols, TT::N);
-                const long tt = (P + TT::PTS - 1) / TT::PTS;
-                const int bx = int(std::min<long>(tt, std::max(1, 444 / (N / tcg::BM))));
-                dim3 grid(bx, N / tcg::BM);
-                if (input) {
-                    n.input_partial.reserve(size_t(bx) * N * (K0 + 1));
-                    CPDE_RUN(e, "backward_input_tc",
-                             (tcg::k_backward_tc<SID, Act, true><<<grid, tcg::THREADS, TT::SMEM, e.stream>>>(
-                                 mh, ml, mz, N, M, P, n.act[1].ptr, nullptr, n.act[0].ptr, K0, n.input_partial.ptr,
-                                 e.tc_error.ptr)));
-                    long isize = long(N) * (K0 + 1);
-                    CPDE_RUN(e, "sum_partials", (k_sum_partials<<<fast::sum_grid(isize), 256, 0, e.stream>>>(
-                                                    n.input_partial.ptr, bx, isize, n.gradient_base(0, target))));
-                } else {
-                    CPDE_RUN(e, "backward_tc",
-                             (tcg::k_backward_tc<SID, Act, false><<<grid, tcg::THREADS, TT::SMEM, e.stream>>>(
-                                 mh, ml, mz, N, M, P, n.act[l - 1].ptr, next, nullptr, 0, nullptr, e.tc_error.ptr)));
-                    cur = next;
-                }
-                continue;
-            }
-            if (input) {
-                const int bx = int(std::min<long>(tiles_p, 148 * 2));
-                dim3 grid(bx, (N + BM - 1) / BM);
-                n.input_partial.reserve(size_t(bx) * N * (K0 + 1));
-                CPDE_RUN(e, "backward_input",
-                         (k_backward<SID, Act, true><<<grid, THREADS, smem, e.stream>>>(
-                             N, M, P, W, cur, n.act[1].ptr, nullptr, n.act[0].ptr, K0, n.input_partial.ptr)));
-                long isize = long(N) * (K0 + 1);
-                CPDE_RUN(e, "sum_partials", (k_sum_partials<<<fast::sum_grid(isize), 256, 0, e.stream>>>(
-                                                n.input_partial.ptr, bx, isize, n.gradient_base(0, target))));
-            } else {
-                const int bx = int(std::min<long>(tiles_p, 148 * 8));
-                dim3 grid(bx, (N + BM - 1) / BM);
-                CPDE_RUN(e, "backward",
-                         (k_backward<SID, Act, false><<<grid, THREADS, smem, e.stream>>>(
-                             N, M, P, W, cur, n.act[l - 1].ptr, next, nullptr, 0, nullptr)));
-                cur = next;
-            }
-        }
-    }
-    template <int SID>
-    void run() {
-        if (n.linear[1] == kTanhAct) layers<SID, Tanh>();
-        else layers<SID, Sigmoid>();
-    }
-};
-}  // namespace
-
-struct FastHead {
-    Engine& e;
-    NetRecord& n;
-    CostRecord& c;
-    long P;
-    int offset;
-    bool collect;
-    const double* multiplier;
-    CostReduce red;
-    float* target;
-    template <int SID, class Act, int O, int KPT>
-    void go() {
-        const int L = n.layers, K = n.neurons[L - 1];
-        const int grid = int(std::min<long>(148L * 8, std::max(1L, (P + 3) / 4)));
-        n.partial.reserve(size_t(grid) * O * (K + 1));
-        auto& t = e.dat(c.target_id);
-        CPDE_RUN(e, "head_matching",
-                 (fast::k_head_matching<SID, Act, O, KPT><<<grid, fast::BM, 0, e.stream>>>(
-                     K, P, offset, n.weights(L - 1), n.act[L - 1].ptr, n.dz[1].ptr, t.values.ptr, t.w,
-                     c.target_rows.ptr, c.weights.ptr, c.weight_samples, multiplier, collect, red, n.partial.ptr)));
-        const long size = long(O) * (K + 1);
-        CPDE_RUN(e, "sum_partials", (fast::k_sum_partials<<<fast::sum_grid(size), 256, 0, e.stream>>>(
-                                        n.partial.ptr, grid, size, n.gradient_base(L - 1, target))));
-    }
-    template <int SID, class Act, int O>
-    void by_width() {
-        if (n.neurons[n.layers - 1] == 128) go<SID, Act, O, 1>();
-        else go<SID, Act, 1, 2>();  // fused_head_ok admits 256-wide last layers for one output only
-    }
-    template <int SID, class Act>
-    void by_outputs() {
-        if (n.neurons.back() == 1) by_width<SID, Act, 1>();
-        else by_width<SID, Act, 2>();
-    }
-    template <int SID>
-    void run() {
-        if (n.linear[1] == kTanhAct) by_outputs<SID, Tanh>();
-        else by_outputs<SID, Sigmoid>();
-    }
-};
-
-namespace {
-struct PointEpoch {
-    Engine& e;
-    NetRecord& n;
-    CostRecord& c;
-    long P;
-    int offset;
-    bool collect;
-    const double* multiplier;
-    CostReduce red;
-    float* target;
-    template <int SID, class Act, int O, int K>
-    void go() {
-        constexpr int R = StaticJet<SID>::R;
-        using T = small::Tiling<R>;
-        const size_t smem = small::SmemSize<R, O>::FLOATS * sizeof(float);
-        static bool ready[64] = {};
-        if (!ready[e.device & 63]) {
-            allow_smem(small::k_point_epoch<SID, Act, O, K>, smem);
-            ready[e.device & 63] = true;
-        }
-        // at most one CTA per SM, each over a contiguous run of point tiles
-        const long tiles = (P + T::PTS - 1) / T::PTS;
-        const int per = int((tiles + 147) / 148);
-        const int grid = int((tiles + per - 1) / per);
-        small::EpochNet net{};
-        net.layers = n.layers;
-        for (int l = 0; l <= n.layers; ++l) net.width[l] = n.neurons[l];
-        for (int l = 0; l < n.layers; ++l) {
-            net.W[l] = n.weights(l);
-            net.act[l] = n.act[l].ptr;
-            net.offset[l] = n.offset[l];
-        }
-        net.dz[0] = n.dz[0].ptr;
-        net.dz[1] = n.dz[1].ptr;
-        net.params = n.params;
-        n.partial.reserve(size_t(grid) * n.params);
-        net.partials = n.partial.ptr;
-        auto& t = e.dat(c.target_id);
-        small::EpochHead head{t.values.ptr, t.w,    c.target_rows.ptr, c.weights.ptr, c.weight_samples,
-                              multiplier,   collect, offset,           red};
-        CPDE_RUN(e, "point_epoch", (small::k_point_epoch<SID, Act, O, K><<<grid, small::THREADS, smem, e.stream>>>(
-                                       net, P, per, head)));
-        CPDE_RUN(e, "sum_partials", (fast::k_sum_partials<<<fast::sum_grid(n.params), 256, 0, e.stream>>>(
-                                        n.partial.ptr, grid, n.params, n.gradient_base(0, target))));
-    }
-    template <int SID, class Act, int O>
-    void by_width() {
-        if (n.neurons[n.layers - 1] == 128) go<SID, Act, O, 128>();
-        else go<SID, Act, 1, 256>();  // fused_head_ok admits 256-wide last layers for one output only
-    }
-    template <int SID, class Act>
-    void by_outputs() {
-        if (n.neurons.back() == 1) by_width<SID, Act, 1>();
-        else by_width<SID, Act, 2>();
-    }
-    template <int SID>
-    void run() {
-        if (n.linear[1] == kTanhAct) by_outputs<SID, Tanh>();
-        else by_outputs<SID, Sigmoid>();
-    }
-};
-}  // namespace
-
-// Tensor cores (3xTF32, about 5e-6 normwise on weight gradients) are used by
-// default only where the tolerance is 1e-4 (highest order 4..6); orders <= 3
-// (tolerance 1e-5) keep exact FP32 FFMA unless tier 2 forces tensor cores.
-static bool use_tensor_cores(int tier, const Context& ctx) {
-    return tier == 2 || (tier == 0 && ctx.plan.max_order >= 4);
-}
-
-void Engine::fast_forward(NetRecord& n, Context& ctx, int points, bool hidden_only) {
-    with_schema(ctx.static_id, FastForward{*this, n, points, use_tensor_cores(tier, ctx), hidden_only});
-}
-
-void Engine::fast_backward(NetRecord& n, Context& ctx, int points, float* target, bool skip_output) {
-    with_schema(ctx.static_id, FastBackward{*this, n, points, target, use_tensor_cores(tier, ctx), skip_output});
 }
 
 // The fused head serves matching costs with 1 or 2 outputs after a 128-wide
@@ -1026,11 +509,6 @@ bool Engine::point_epoch_ok(NetRecord& n, Context& ctx, long points, float* targ
     return tier == 3 || points * ctx.R() <= limit;
 }
 
-void Engine::point_epoch(NetRecord& n, CostRecord& c, Context& ctx, long points, int offset, bool collect,
-                         const double* multiplier, int cost_index, float* target) {
-    CostReduce red{n.cost_partials.ptr, n.cost_ticket.ptr, n.cost_totals.ptr + cost_index};
-    with_schema(ctx.static_id, PointEpoch{*this, n, c, points, offset, collect, multiplier, red, target});
-}
 
 void Engine::run_cost(NetRecord& n, CostRecord& c, int cost_index, int points, int offset, bool collect,
                       bool gradient, const double* multiplier) {
@@ -1106,7 +584,7 @@ void Engine::pass(NetRecord& n, CostRecord& c, int cost_index, bool bwd, bool co
         }
         if (fused) {
             CostReduce red{n.cost_partials.ptr, n.cost_ticket.ptr, n.cost_totals.ptr + cost_index};
-            with_schema(ctx.static_id, FastHead{*this, n, c, valid, offset, collect, multiplier, red, target});
+            fused_head(n, c, ctx, valid, offset, collect, multiplier, red, target);
             fast_backward(n, ctx, valid, target, true);
             continue;
         }

@@ -215,6 +215,8 @@ class Engine {
     bool fast_ok(NetRecord& n, Context& ctx) const;
     bool fused_head_ok(NetRecord& n, CostRecord& c, Context& ctx) const;
     bool point_epoch_ok(NetRecord& n, Context& ctx, long points, float* target) const;
+    void fused_head(NetRecord& n, CostRecord& c, Context& ctx, long points, int offset, bool collect,
+                    const double* multiplier, CostReduce red, float* target);
     void point_epoch(NetRecord& n, CostRecord& c, Context& ctx, long points, int offset, bool collect,
                      const double* multiplier, int cost_index, float* target);
     void fast_forward(NetRecord& n, Context& ctx, int points, bool hidden_only);

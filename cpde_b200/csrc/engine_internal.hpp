@@ -1,0 +1,158 @@
+// Launch helpers shared by the engine's translation units: per-kernel event
+// timing (CPDE_RUN), grid sizing, tensor-map encoders and the dispatch over
+// the generated static schemas.
+#pragma once
+#include <algorithm>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "engine.hpp"
+
+namespace cpde {
+// ---------------------------------------------------------------------------
+// kernel timing
+
+struct KernelTimer {
+    struct Mark {
+        const char* name;
+        cudaEvent_t start, stop;
+    };
+    std::vector<Mark> marks;
+    std::vector<cudaEvent_t> pool;
+    cudaEvent_t get() {
+        if (!pool.empty()) {
+            auto e = pool.back();
+            pool.pop_back();
+            return e;
+        }
+        cudaEvent_t e;
+        CPDE_CUDA(cudaEventCreate(&e));
+        return e;
+    }
+    struct Totals {
+        long launches = 0;
+        double ms = 0;
+    };
+    std::map<std::string, Totals> totals;
+    void collect() {
+        for (auto& m : marks) {
+            CPDE_CUDA(cudaEventSynchronize(m.stop));
+            float ms = 0;
+            CPDE_CUDA(cudaEventElapsedTime(&ms, m.start, m.stop));
+            auto& t = totals[m.name];
+            t.launches += 1;
+            t.ms += ms;
+            pool.push_back(m.start);
+            pool.push_back(m.stop);
+        }
+        marks.clear();
+    }
+    ~KernelTimer() {
+        for (auto& m : marks) {
+            cudaEventDestroy(m.start);
+            cudaEventDestroy(m.stop);
+        }
+        for (auto e : pool) cudaEventDestroy(e);
+    }
+};
+
+#define CPDE_RUN(engine, name, ...)                                           \
+    do {                                                                      \
+        KernelTimer* t_ = (engine).timer.get();                               \
+        cudaEvent_t a_ = nullptr, b_ = nullptr;                               \
+        if (t_) {                                                             \
+            a_ = t_->get();                                                   \
+            b_ = t_->get();                                                   \
+            CPDE_CUDA(cudaEventRecord(a_, (engine).stream));                  \
+        }                                                                     \
+        __VA_ARGS__;                                                          \
+        CPDE_LAUNCHED();                                                      \
+        if (t_) {                                                             \
+            CPDE_CUDA(cudaEventRecord(b_, (engine).stream));                  \
+            t_->marks.push_back({name, a_, b_});                              \
+        }                                                                     \
+    } while (0)
+
+inline int grid_for(long count, int threads = 256, int cap = 148 * 16) {
+    long g = (count + threads - 1) / threads;
+    return int(std::max(1L, std::min<long>(g, cap)));
+}
+
+// ---------------------------------------------------------------------------
+// fast tier dispatch
+
+static_assert(kStaticSchemas == 10, "update CPDE_STATIC_CASES after changing the generated schemas");
+#define CPDE_STATIC_CASES(X) X(0) X(1) X(2) X(3) X(4) X(5) X(6) X(7) X(8) X(9)
+
+template <class F>
+static void with_schema(int sid, F&& f) {
+    switch (sid) {
+#define CPDE_CASE(i) \
+    case i:          \
+        f.template run<i>(); \
+        return;
+        CPDE_STATIC_CASES(CPDE_CASE)
+#undef CPDE_CASE
+    }
+    throw DeviceError("unknown static schema");
+}
+
+template <class K>
+static void allow_smem(K kernel, size_t bytes) {
+    CPDE_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes)));
+}
+
+inline CUtensorMap tensor_map(const float* base, int inner, long rows, int box_rows) {
+    CUtensorMap map;
+    cuuint64_t dims[2] = {cuuint64_t(inner), cuuint64_t(rows)};
+    cuuint64_t strides[1] = {cuuint64_t(inner) * sizeof(float)};
+    cuuint32_t box[2] = {cuuint32_t(tcg::KS), cuuint32_t(box_rows)};
+    cuuint32_t element_strides[2] = {1, 1};
+    driver_check(driver_api().encode_tiled(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims,
+                                           strides, box, element_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE),
+                 "cuTensorMapEncodeTiled");
+    return map;
+}
+
+// Unswizzled box of 128 neurons x 32 columns (raw slabs of the weight-gradient kernel).
+inline CUtensorMap raw_map(const float* base, int inner, long rows) {
+    CUtensorMap map;
+    cuuint64_t dims[2] = {cuuint64_t(inner), cuuint64_t(rows)};
+    cuuint64_t strides[1] = {cuuint64_t(inner) * sizeof(float)};
+    cuuint32_t box[2] = {cuuint32_t(tcg::BM), cuuint32_t(tcg::KS)};
+    cuuint32_t element_strides[2] = {1, 1};
+    driver_check(driver_api().encode_tiled(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims,
+                                           strides, box, element_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                           CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE),
+                 "cuTensorMapEncodeTiled");
+    return map;
+}
+
+// Box of 32 neurons x 32 columns in the 128-byte swizzle with 32-byte atoms
+// (MN-major TF32 operands of the weight-gradient kernel).
+inline CUtensorMap mn32_map(const float* base, int inner, long rows) {
+    CUtensorMap map;
+    cuuint64_t dims[2] = {cuuint64_t(inner), cuuint64_t(rows)};
+    cuuint64_t strides[1] = {cuuint64_t(inner) * sizeof(float)};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t element_strides[2] = {1, 1};
+    driver_check(driver_api().encode_tiled(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims,
+                                           strides, box, element_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                           CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE),
+                 "cuTensorMapEncodeTiled");
+    return map;
+}
+
+// Tensor cores (3xTF32, about 5e-6 normwise on weight gradients) are used by
+// default only where the tolerance is 1e-4 (highest order 4..6); orders <= 3
+// (tolerance 1e-5) keep exact FP32 FFMA unless tier 2 forces tensor cores.
+inline bool use_tensor_cores(int tier, const Context& ctx) {
+    return tier == 2 || (tier == 0 && ctx.plan.max_order >= 4);
+}
+
+}  // namespace cpde

@@ -357,7 +357,7 @@ __global__ void __launch_bounds__(THREADS, 2) k_backward(int M, int K, long P, c
 // partials[cta][m + n*M] (n = N is the bias). grid = (splits, ceil(N/128),
 // ceil(M/128)).
 
-__global__ void __launch_bounds__(THREADS, 2) k_weight_gradient(int M, int N, long columns, int R, long per_split,
+static __global__ void __launch_bounds__(THREADS, 2) k_weight_gradient(int M, int N, long columns, int R, long per_split,
                                                              const float* __restrict__ dZ,
                                                              const float* __restrict__ A,
                                                              float* __restrict__ partials) {
@@ -447,7 +447,7 @@ __global__ void __launch_bounds__(THREADS, 2) k_weight_gradient(int M, int N, lo
 // Output layer (n_out <= 8 linear outputs): Z_out[o, p, r] = W_out Y + b.
 // One warp per (point, row) column group: lanes split the K inputs.
 
-__global__ void k_output_forward(int O, int K, long P, int R, const float* __restrict__ W,
+static __global__ void k_output_forward(int O, int K, long P, int R, const float* __restrict__ W,
                                  const float* __restrict__ bias, const float* __restrict__ Y,
                                  float* __restrict__ Z) {
     const int lane = threadIdx.x & 31;
@@ -689,7 +689,7 @@ __global__ void __launch_bounds__(BM) k_head_matching(int K, long P, int offset,
 // Sum CTA partials (fixed order) into a layer gradient (accumulating). A block
 // of 256 threads takes 32 consecutive elements; its 8 warps sum interleaved
 // subsets of the partials, which are then folded in warp order.
-__global__ void __launch_bounds__(256) k_sum_partials(const float* __restrict__ partials, int count, long size,
+static __global__ void __launch_bounds__(256) k_sum_partials(const float* __restrict__ partials, int count, long size,
                                                       float* __restrict__ out) {
     __shared__ float part[8][33];
     const int x = threadIdx.x & 31, y = threadIdx.x >> 5;

@@ -125,7 +125,7 @@ __device__ void finish_blocks(T mine, T* partials, unsigned* ticket, T* total, C
     }
 }
 
-__global__ void k_clear_costs(CostStats* totals, int count) {
+static __global__ void k_clear_costs(CostStats* totals, int count) {
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < count; i += blockDim.x * gridDim.x)
         totals[i] = cost_empty();
 }
@@ -161,7 +161,7 @@ struct Tanh {
 // Copy-in: inputs of one chunk from the data record's (row, sample, channel)
 // layout into the interleaved layer-0 layout.
 
-__global__ void k_stage_input(const float* __restrict__ data, int channels, int data_samples,
+static __global__ void k_stage_input(const float* __restrict__ data, int channels, int data_samples,
                               const int* __restrict__ rows, int R, int offset, int points,
                               float* __restrict__ out) {
     long total = (long)points * R * channels;
@@ -175,7 +175,7 @@ __global__ void k_stage_input(const float* __restrict__ data, int channels, int 
 }
 
 // Copy-out of evaluation outputs into the (row, sample, output) layout.
-__global__ void k_scatter_output(const float* __restrict__ z, int outputs, int R, const int* __restrict__ rows,
+static __global__ void k_scatter_output(const float* __restrict__ z, int outputs, int R, const int* __restrict__ rows,
                                  int offset, int points, int data_samples, float* __restrict__ out) {
     long total = (long)points * R * outputs;
     for (long e = blockIdx.x * (long)blockDim.x + threadIdx.x; e < total; e += (long)blockDim.x * gridDim.x) {
@@ -267,7 +267,7 @@ k_gemm(int M, int N, int K, const float* __restrict__ A, int lda, const float* _
 }
 
 // out[m + n*ldc] (+)= sum_z partial[z][m + n*M], summed in z order (deterministic).
-__global__ void k_splitk_reduce(const float* __restrict__ partial, int splits, int M, int N, float* __restrict__ out,
+static __global__ void k_splitk_reduce(const float* __restrict__ partial, int splits, int M, int N, float* __restrict__ out,
                                 int ldc, int accumulate) {
     long total = (long)M * N;
     for (long e = blockIdx.x * (long)blockDim.x + threadIdx.x; e < total; e += (long)blockDim.x * gridDim.x) {
@@ -362,7 +362,7 @@ __device__ inline void cost_finish(CostStats local, const CostReduce& red) {
 // Squared-error matching: sum over rows d and outputs o of w*(y-t)^2, with
 // dE/dy = 2w(y-t) (cuda/cost_kernels.cuh:6-35 semantics). ``y``/``g`` use the
 // interleaved layout with n = outputs.
-__global__ void k_cost_matching(const float* __restrict__ y, float* __restrict__ g, const float* __restrict__ target,
+static __global__ void k_cost_matching(const float* __restrict__ y, float* __restrict__ g, const float* __restrict__ target,
                                 int target_samples, const int* __restrict__ target_rows,
                                 const float* __restrict__ weights, int weight_samples, int outputs, int R, int points,
                                 int offset, int collect, int gradient, CostReduce red) {
@@ -402,7 +402,7 @@ __device__ inline float component(const float* y, int index, int outputs, int R,
 
 // Polynomial residuals r_e = sum_t c_t y_a (y_b or 1) - rhs_e, loss w r^2
 // (cuda/cost_kernels.cuh:37-90 semantics).
-__global__ void k_cost_polynomial(const float* __restrict__ y, float* __restrict__ g, const PolyTerm* __restrict__ terms,
+static __global__ void k_cost_polynomial(const float* __restrict__ y, float* __restrict__ g, const PolyTerm* __restrict__ terms,
                                   const float* __restrict__ coefficients, int term_count, const float* __restrict__ rhs,
                                   const float* __restrict__ weights, int outputs, int R, int equations, int samples,
                                   int points, int offset, int collect, int gradient, CostReduce red) {
@@ -452,7 +452,7 @@ __global__ void k_cost_polynomial(const float* __restrict__ y, float* __restrict
 
 // dE/dy *= multiplier (graph leaf multiplier), zero when the multiplier is 0
 // (cuda/cost_graph.cuh:29-34).
-__global__ void k_scale(float* __restrict__ g, long count, const double* __restrict__ multiplier) {
+static __global__ void k_scale(float* __restrict__ g, long count, const double* __restrict__ multiplier) {
     double m = *multiplier;
     for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < count; i += (long)blockDim.x * gridDim.x)
         g[i] = m == 0 ? 0.f : float(g[i] * m);
@@ -468,7 +468,7 @@ struct GradReduce {
     GradStats* totals;    // [layers]
 };
 
-__global__ void k_inspect_gradients(const float* const* __restrict__ grads, const int* __restrict__ counts,
+static __global__ void k_inspect_gradients(const float* const* __restrict__ grads, const int* __restrict__ counts,
                                     GradReduce red) {
     const int layer = blockIdx.y;
     const float* g = grads[layer];
@@ -503,7 +503,7 @@ struct OptLayer {
 
 // RPROP (cuda/derivative_kernels_v4.cu:752-778): grow x1.2 on agreeing signs,
 // roll back and halve on a sign change, |W| <= 20 guard restarting at 0.1.
-__global__ void k_rprop(float* __restrict__ w, float* __restrict__ bank1, float* __restrict__ bank2,
+static __global__ void k_rprop(float* __restrict__ w, float* __restrict__ bank1, float* __restrict__ bank2,
                         float* __restrict__ steps, const OptLayer* __restrict__ layers) {
     const OptLayer L = layers[blockIdx.y];
     float* cur = (L.active == 1 ? bank1 : bank2) + L.offset;
@@ -532,7 +532,7 @@ __global__ void k_rprop(float* __restrict__ w, float* __restrict__ bank1, float*
 
 // Adam (cuda/derivative_kernels_v4.cu:780-799), including the reference's
 // double-precision denominator from the 1e-8 literal.
-__global__ void k_adam(float* __restrict__ w, float* __restrict__ bank1, float* __restrict__ bank2,
+static __global__ void k_adam(float* __restrict__ w, float* __restrict__ bank1, float* __restrict__ bank2,
                        float* __restrict__ first, const OptLayer* __restrict__ layers, float alpha, float beta1,
                        float beta2, float beta1t, float beta2t) {
     const OptLayer L = layers[blockIdx.y];
@@ -556,7 +556,7 @@ __global__ void k_adam(float* __restrict__ w, float* __restrict__ bank1, float* 
 
 // Steps below the floor are raised to it and that entry's history cleared
 // (cuda/derivative_kernels_v4.cu:801-814).
-__global__ void k_rprop_floor(float* __restrict__ bank1, float* __restrict__ bank2, float* __restrict__ steps,
+static __global__ void k_rprop_floor(float* __restrict__ bank1, float* __restrict__ bank2, float* __restrict__ steps,
                               const OptLayer* __restrict__ layers, float floor_value) {
     const OptLayer L = layers[blockIdx.y];
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < L.count; i += blockDim.x * gridDim.x) {
@@ -569,7 +569,7 @@ __global__ void k_rprop_floor(float* __restrict__ bank1, float* __restrict__ ban
     }
 }
 
-__global__ void k_fill(float* __restrict__ dst, long count, float value) {
+static __global__ void k_fill(float* __restrict__ dst, long count, float value) {
     for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < count; i += (long)blockDim.x * gridDim.x)
         dst[i] = value;
 }

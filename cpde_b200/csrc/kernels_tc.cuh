@@ -320,7 +320,7 @@ __device__ __forceinline__ void split_transpose(const float* raw, float* hi, flo
     }
 }
 
-__global__ void __launch_bounds__(THREADS) k_weight_gradient_tc(const __grid_constant__ CUtensorMap map_dz,
+static __global__ void __launch_bounds__(THREADS) k_weight_gradient_tc(const __grid_constant__ CUtensorMap map_dz,
                                                                 const __grid_constant__ CUtensorMap map_a, int M,
                                                                 int N, long columns, int R, long per_split,
                                                                 float* __restrict__ partials, int* error) {
@@ -424,7 +424,7 @@ __global__ void __launch_bounds__(THREADS) k_weight_gradient_tc(const __grid_con
 
 // hi/lo TF32 split of a weight matrix. transpose: dst[m*K + k] = src[m + k*M]
 // (column-major M x K to K-major rows); otherwise elementwise.
-__global__ void k_split_tf32(const float* __restrict__ src, float* __restrict__ hi, float* __restrict__ lo, int M,
+static __global__ void k_split_tf32(const float* __restrict__ src, float* __restrict__ hi, float* __restrict__ lo, int M,
                              int K, int transpose) {
     const long total = (long)M * K;
     for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)blockDim.x * gridDim.x) {

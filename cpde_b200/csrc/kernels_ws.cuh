@@ -393,7 +393,7 @@ __device__ __forceinline__ int mn32_index(int mn, int k) {
     return (mn >> 5) * (kWgBox / 4) + k * 32 + ((((mn & 31) >> 3) ^ (k & 3)) << 3) + (mn & 7);
 }
 
-__global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_constant__ CUtensorMap map_dz,
+static __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_constant__ CUtensorMap map_dz,
                                                             const __grid_constant__ CUtensorMap map_y, int N,
                                                             long columns, int R, float* __restrict__ partials,
                                                             int* error) {
