@@ -95,6 +95,55 @@ def measured_peaks():
     return {'hbm_gbs': 6650.0, 'bf16_tflops': 1590.0}, 'fallback'
 
 
+# Algorithmic HBM bytes of one launch of each kernel on the config-2 network
+# (2->128^4->1, C = points x rows columns, 4-byte floats): what the kernel
+# must read and write at least once. forward: X_{l-1} in, Y_l out; backward:
+# dZ_l and Y_{l-1} in, dZ_{l-1} out; backward_input: dZ_2, Y_1 and the inputs
+# in; weight_gradient: dZ_l and Y_{l-1} in; head: Y_4 in, dZ_4 out, targets
+# in; input_forward: inputs in, Y_1 out. Tensor-core kernels also carry
+# 2 x 128 x 128 x C algorithmic FLOPs per launch (3 TF32 passes each).
+def algorithmic_bytes(points, rows):
+    c = points * rows * 4
+    return {'forward_ws': (128 + 128) * c, 'backward_ws': (128 + 2 * 128) * c, 'backward_input_ws': (2 * 128 + 2) * c,
+            'weight_gradient_ws': (128 + 128) * c, 'head_matching': (2 * 128 + 2) * c, 'input_forward': (2 + 128) * c,
+            'forward_tc': (128 + 128) * c, 'backward_tc': (128 + 2 * 128) * c, 'backward_input_tc': (2 * 128 + 2) * c,
+            'weight_gradient_tc': (128 + 128) * c}
+
+
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch measured
+# by ncu on the same kernels at 16,384 points and scaled x4 to a 65,536-point
+# launch (the traffic is linear in the columns).
+MEASURED_TRAFFIC = {'forward_ws': int(4 * (234.978 + 185.196) * 1e6), 'weight_gradient_ws': int(4 * (469.817 + 3.787) * 1e6),
+                    'backward_ws': int(4 * (469.887 + 200.892) * 1e6), 'backward_input_ws': int(4 * (473.561 + 5.594) * 1e6),
+                    'head_matching': int(4 * (236.812 + 190.445) * 1e6), 'input_forward': int(4 * (3.709 + 174.699) * 1e6)}
+
+
+def hbm_roofline(kernels, steps, points, rows, peaks, source):
+    """Achieved HBM bandwidth of every kernel class (algorithmic bytes per
+    launch / mean launch time) and the roofline object of the class with the
+    largest share of the step."""
+    bytes_per_launch = algorithmic_bytes(points, rows)
+    total = sum(v[1] for v in kernels.values())
+    peak = peaks['hbm_gbs']
+    rows_out = {}
+    for name, (count, ms) in kernels.items():
+        if name not in bytes_per_launch or count == 0:
+            continue
+        per_launch_s = ms / count / 1000
+        achieved = bytes_per_launch[name] / per_launch_s / 1e9
+        rows_out[name] = dict(achieved=achieved, frac=achieved / peak, share=ms / total,
+                              ms_per_launch=per_launch_s * 1000, algorithmic_bytes=bytes_per_launch[name])
+    if not rows_out:
+        return None, rows_out
+    top = max(rows_out, key=lambda k: rows_out[k]['share'])
+    t = rows_out[top]
+    roofline = dict(kernel=top, bound='hbm', achieved=t['achieved'], peak=peak, unit='GB/s', frac=t['frac'],
+                    traffic=MEASURED_TRAFFIC.get(top), share=t['share'],
+                    peak_source=f'hbm_gbs of MEASURED_PEAKS.json ({source}): {peak} GB/s, of measured',
+                    algorithmic_bytes_per_launch=t['algorithmic_bytes'])
+    return roofline, rows_out
+
+
 def cpu_baseline(points=128, steps=2):
     """Reference CPU server (built from the reference's own sources) on a
     bounded sample of the same workload; serial engine, 1 core."""
@@ -310,25 +359,7 @@ def run_b200(args):
     fwd, dgrad, wgrad = gemm_flops(args.points, R)
     peaks, source = measured_peaks()
     launches = sum(v[0] for v in kernels.values()) // args.steps
-    top = max(kernels.items(), key=lambda kv: kv[1][1])
-    # Algorithmic FLOPs per kernel class and step (hidden 128 x 128 layers):
-    # 'forward' = layers 2..4, 'backward'/'backward_input' = input-gradient GEMMs
-    # of layers 4,3 / 2, 'weight_gradient' = layers 4..2 (bias column included).
-    hidden = 2 * 128 * 128 * args.points * R
-    class_flops = {'gemm': fwd + dgrad, 'gemm_wgrad': wgrad, 'forward': 3 * hidden, 'forward_tc': 3 * hidden,
-                   'backward': 2 * hidden, 'backward_tc': 2 * hidden, 'backward_input_tc': hidden,
-                   'weight_gradient_tc': 3 * 2 * 128 * 129 * args.points * R,
-                   'backward_input': hidden, 'weight_gradient': 3 * 2 * 128 * 129 * args.points * R}
-    flops = class_flops.get(top[0])
-    fp32_peak = 148 * 128 * 2 * (clock['sm_max_mhz'] if clock and clock['sm_max_mhz'] else 1965.0) / 1e6
-    roofline = None
-    if flops is not None:
-        achieved = flops / (top[1][1] / args.steps / 1000) / 1e12
-        roofline = dict(kernel=top[0], bound='fp32-ffma', achieved=achieved, peak=fp32_peak, unit='TFLOP/s',
-                        frac=achieved / fp32_peak, traffic=None,
-                        peak_source='nominal FP32 CUDA-core peak (148 SMs x 128 lanes x 2 x max SM clock); '
-                                    f'MEASURED_PEAKS.json ({source}) has no FP32 figure',
-                        share=top[1][1] / sum(v[1] for v in kernels.values()))
+    roofline, kernel_rooflines = hbm_roofline(kernels, args.steps, args.points, R, peaks, source)
     if rank == 0:
         line = dict(metric=METRIC, value=value, unit=UNIT, n_gpus=world, steps=args.steps, warmup=args.warmup,
                     ms_per_step=ms, higher_is_better=True, scaling='weak', vs_baseline=None, dtype='f32',
@@ -341,7 +372,7 @@ def run_b200(args):
                              d2h_bytes_per_step=int(world * (params * 4 + 8)), timer='host wall clock',
                              note='all ranks together copy the whole input once per step (each its shard) '
                                   'and each rank reads the all-reduced objective and gradient'),
-                    gpu_launches=int(launches), roofline=roofline, clocks=clock,
+                    gpu_launches=int(launches), roofline=roofline, kernel_rooflines=kernel_rooflines, clocks=clock,
                     kernels={k: dict(launches=v[0] // args.steps, ms_per_step=v[1] / args.steps)
                              for k, v in sorted(kernels.items())},
                     gemm_gflop_per_step=(fwd + dgrad + wgrad) / 1e9, loss=loss)
