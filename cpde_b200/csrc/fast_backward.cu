@@ -103,8 +103,8 @@ struct FastBackward {
                 using WT = ws::Tiling<R>;
                 static bool bw_ready[64] = {};
                 if (!bw_ready[e.device & 63]) {
-                    allow_smem(ws::k_backward_ws<SID, Act, false>, WT::SMEM);
-                    allow_smem(ws::k_backward_ws<SID, Act, true>, WT::SMEM);
+                    allow_smem(ws::k_backward_ws<SID, Act, false>, WT::BSMEM);
+                    allow_smem(ws::k_backward_ws<SID, Act, true>, WT::BSMEM);
                     bw_ready[e.device & 63] = true;
                 }
                 const CUtensorMap mz = tensor_map(cur, M, cols, WT::N);
@@ -114,7 +114,7 @@ struct FastBackward {
                 if (input) {
                     n.input_partial.reserve(size_t(2 * bx) * N * (K0 + 1));
                     CPDE_RUN(e, "backward_input_ws",
-                             (ws::k_backward_ws<SID, Act, true><<<grid, ws::THREADS, WT::SMEM, e.stream>>>(
+                             (ws::k_backward_ws<SID, Act, true><<<grid, ws::THREADS, WT::BSMEM, e.stream>>>(
                                  mz, M, N, P, W, n.act[1].ptr, nullptr, n.act[0].ptr, K0, n.input_partial.ptr,
                                  e.tc_error.ptr)));
                     long isize = long(N) * (K0 + 1);
@@ -122,7 +122,7 @@ struct FastBackward {
                                                     n.input_partial.ptr, 2 * bx, isize, n.gradient_base(0, target))));
                 } else {
                     CPDE_RUN(e, "backward_ws",
-                             (ws::k_backward_ws<SID, Act, false><<<grid, ws::THREADS, WT::SMEM, e.stream>>>(
+                             (ws::k_backward_ws<SID, Act, false><<<grid, ws::THREADS, WT::BSMEM, e.stream>>>(
                                  mz, M, N, P, W, n.act[l - 1].ptr, next, nullptr, 0, nullptr, e.tc_error.ptr)));
                     cur = next;
                 }

@@ -3,12 +3,14 @@
 // a ring of shared-memory stages while the tensor cores and the jet epilogue
 // work on earlier tiles.
 //
-// Roles (14 warps):
+// Roles (15 warps):
 //   warp 0 (one lane)  TMA producer: one 32-wide K slab of a tile per stage;
-//   warp 1 (one lane)  MMA issuer; the warp also owns the tensor-memory block;
+//   warps 1, 6 (lane 0) MMA issuers for the even and the odd tiles of the CTA
+//                      (local tile index), each into its own accumulator;
+//                      warp 1 also owns the tensor-memory block;
 //   warps 2-5          split each landed slab into TF32 hi (in place) and lo;
-//   warps 6-13         load the layer's weights (hi and lo) into tensor memory
-//                      once (warps 6-9), then run the jet epilogue on each
+//   warps 7-14         load the layer's weights (hi and lo) into tensor memory
+//                      once (warps 7-10), then run the jet epilogue on each
 //                      finished tile: warp w reads TMEM lanes 32 (w % 4) .. +31
 //                      and takes every other point of the tile.
 // Tensor memory (512 columns): weights hi [0, 128), weights lo [128, 256),
@@ -26,12 +28,18 @@
 namespace cpde {
 namespace ws {
 
-constexpr int kProducerWarp = 0, kMmaWarp = 1, kSplitWarp = 2, kEpilogueWarp = 6;
+// Two MMA issuers take alternate tiles (each always into its own accumulator):
+// one thread alone leaves the tensor pipe idle while it waits on a stage or an
+// accumulator, and at these tile sizes that idle time was about a third of
+// the layer.
+constexpr int kProducerWarp = 0, kMmaWarp = 1, kSplitWarp = 2, kSecondMmaWarp = 6, kEpilogueWarp = 7;
+constexpr int kMmaIssuers = 2;
 constexpr int kEpilogueGroups = 2;  // two warps per TMEM lane quarter, alternating points
 constexpr int THREADS = (kEpilogueWarp + 4 * kEpilogueGroups) * 32;
 constexpr int STAGES = 6;
 constexpr int kMaxK = 128;  // weights resident in tensor memory
 constexpr uint32_t kTmemColumns = 512, kAccColumn = 256;
+constexpr int kSmemLimit = 232448;  // dynamic shared memory of one CTA (227 KB)
 
 template <int R>
 struct Tiling {
@@ -40,6 +48,15 @@ struct Tiling {
     static constexpr int N = ((COLS + 15) / 16) * 16;              // MMA N: multiple of 16 for M = 128
     static constexpr int SLAB = ((N * 128 + 1023) / 1024) * 1024;  // one K slab: N rows of 128 bytes
     static constexpr int SMEM = 2 * STAGES * SLAB + 1024 + 256;
+    // backward: two R-float staging slots per epilogue thread for the
+    // previous layer's values, copied asynchronously one work item ahead;
+    // the slab ring gives up stages where both do not fit
+    static constexpr int YBUF = 2 * R * 4 * 32 * 4 * kEpilogueGroups;
+    static constexpr int BSTAGES = (kSmemLimit - 1024 - 256 - YBUF) / (2 * SLAB) < STAGES
+                                       ? (kSmemLimit - 1024 - 256 - YBUF) / (2 * SLAB)
+                                       : STAGES;
+    static constexpr int BSMEM = 2 * BSTAGES * SLAB + 1024 + 256 + YBUF;
+    static_assert(BSTAGES >= 3, "slab ring too shallow beside the staging slots");
 };
 
 // A wait taken by every lane of a warp; the warp leaves together when any
@@ -84,34 +101,37 @@ __device__ __forceinline__ void split_range(float4* h4, float4* l4, int count, i
 }
 
 struct Ring {
-    float *hi, *lo;  // [STAGES][SLAB / 4]
-    uint64_t *full, *split, *empty, *acc_full, *acc_empty, *a_ready, *drain;
+    float *hi, *lo;  // [stages][SLAB / 4]
+    float* staging;   // after the barriers: backward staging slots
+    uint64_t *full, *split, *empty, *acc_full, *acc_empty, *a_ready, *drain;  // drain: one per MMA issuer
     uint32_t* tmem_slot;
     volatile int* abort;
 };
 
-template <int SLAB>
+template <int SLAB, int S = STAGES>
 __device__ __forceinline__ Ring carve_ring(uint8_t* raw) {
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
     Ring r;
     r.hi = reinterpret_cast<float*>(base);
-    r.lo = reinterpret_cast<float*>(base + STAGES * SLAB);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(base + 2 * STAGES * SLAB);
+    r.lo = reinterpret_cast<float*>(base + S * SLAB);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(base + 2 * S * SLAB);
     r.full = bars;
-    r.split = bars + STAGES;
-    r.empty = bars + 2 * STAGES;
-    r.acc_full = bars + 3 * STAGES;
+    r.split = bars + S;
+    r.empty = bars + 2 * S;
+    r.acc_full = bars + 3 * S;
     r.acc_empty = r.acc_full + 2;
     r.a_ready = r.acc_empty + 2;
     r.drain = r.a_ready + 1;
-    r.tmem_slot = reinterpret_cast<uint32_t*>(r.drain + 1);
+    r.tmem_slot = reinterpret_cast<uint32_t*>(r.drain + kMmaIssuers);
     r.abort = reinterpret_cast<volatile int*>(r.tmem_slot + 1);
+    r.staging = reinterpret_cast<float*>(base + 2 * S * SLAB + 256);
     return r;
 }
 
+template <int S = STAGES>
 __device__ __forceinline__ void ring_init(Ring& r) {
     if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; ++s) {
+        for (int s = 0; s < S; ++s) {
             tc::mbar_init(r.full + s, 1);
             tc::mbar_init(r.split + s, 4);
             tc::mbar_init(r.empty + s, 1);
@@ -121,7 +141,7 @@ __device__ __forceinline__ void ring_init(Ring& r) {
             tc::mbar_init(r.acc_empty + a, 4 * kEpilogueGroups);
         }
         tc::mbar_init(r.a_ready, 4);
-        tc::mbar_init(r.drain, 1);
+        for (int i = 0; i < kMmaIssuers; ++i) tc::mbar_init(r.drain + i, 1);
         *r.abort = 0;
         tc::fence_barrier_init();
     }
@@ -136,33 +156,32 @@ __device__ __forceinline__ void ring_init(Ring& r) {
 
 // Producer: the X slabs of every tile this CTA owns, in order. After the last
 // issue (or an abort) it waits for the loads still in flight.
-template <int SLAB>
+template <int SLAB, int S = STAGES>
 __device__ __forceinline__ void produce(const Ring& r, const CUtensorMap* map, long tiles, int tile_columns, int N,
                                         int slabs) {
     uint32_t it = 0;
     for (long tile = blockIdx.x; tile < tiles && !*r.abort; tile += gridDim.x) {
         const int col0 = int(tile * tile_columns);
         for (int s = 0; s < slabs; ++s) {
-            const int st = it % STAGES;
-            if (!tc::mbar_wait_or_abort(r.empty + st, ((it / STAGES) & 1) ^ 1, tcg::kWaitCycles, r.abort)) break;
+            const int st = it % S;
+            if (!tc::mbar_wait_or_abort(r.empty + st, ((it / S) & 1) ^ 1, tcg::kWaitCycles, r.abort)) break;
             tc::mbar_expect_tx(r.full + st, uint32_t(N) * 128);
             tc::tma_load_2d(r.hi + st * (SLAB / 4), map, r.full + st, s * 32, col0);
             ++it;
         }
     }
-    for (uint32_t k = it > STAGES ? it - STAGES : 0; k < it; ++k)
-        tc::mbar_wait(r.full + k % STAGES, (k / STAGES) & 1, tcg::kWaitCycles);
+    for (uint32_t k = it > S ? it - S : 0; k < it; ++k) tc::mbar_wait(r.full + k % S, (k / S) & 1, tcg::kWaitCycles);
 }
 
 // Split warps: TF32 hi in place and lo beside it, for every slab in order.
-template <int SLAB>
+template <int SLAB, int S = STAGES>
 __device__ __forceinline__ void split_all(const Ring& r, long tiles, int N, int slabs) {
     const int tid = threadIdx.x - kSplitWarp * 32;  // 0..127
     uint32_t it = 0;
     for (long tile = blockIdx.x; tile < tiles; tile += gridDim.x)
         for (int s = 0; s < slabs; ++s, ++it) {
-            const int st = it % STAGES;
-            if (!warp_wait(r.full + st, (it / STAGES) & 1, r.abort)) return;
+            const int st = it % S;
+            if (!warp_wait(r.full + st, (it / S) & 1, r.abort)) return;
             split_range(reinterpret_cast<float4*>(r.hi + st * (SLAB / 4)),
                         reinterpret_cast<float4*>(r.lo + st * (SLAB / 4)), N * 8, tid, [](int) { return true; });
             tc::fence_proxy_async();
@@ -171,23 +190,26 @@ __device__ __forceinline__ void split_all(const Ring& r, long tiles, int N, int 
         }
 }
 
-// MMA issuer: per tile, lo*hi + hi*lo + hi*hi over the K slabs into one of the
-// two accumulators; each slab's stage is released by a commit once its MMAs
-// have read it.
-template <int N, int SLAB>
-__device__ __forceinline__ void issue_mmas(const Ring& r, uint32_t tmem, long tiles, int slabs) {
+// MMA issuer `which` (0 or 1): for the CTA's tiles of local index
+// which, which + 2, ..., lo*hi + hi*lo + hi*hi over the K slabs into
+// accumulator `which`; each slab's stage is released by a commit once its
+// MMAs have read it. Slab counter `it` runs over all the CTA's slabs in ring
+// order, the other issuer's included.
+template <int N, int SLAB, int S = STAGES>
+__device__ __forceinline__ void issue_mmas(const Ring& r, uint32_t tmem, long tiles, int slabs, int which) {
     constexpr uint32_t idesc = tc::idesc_tf32(128, N);
     bool ok = tc::mbar_wait_or_abort(r.a_ready, 0, tcg::kWaitCycles, r.abort);
     tc::tc_fence_after();
-    uint32_t it = 0, local = 0;
-    for (long tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x, ++local) {
+    uint32_t it = which * slabs, local = which;
+    for (long tile = blockIdx.x + which * gridDim.x; ok && tile < tiles;
+         tile += kMmaIssuers * gridDim.x, local += kMmaIssuers, it += (kMmaIssuers - 1) * slabs) {
         const int a = local & 1;
         ok = tc::mbar_wait_or_abort(r.acc_empty + a, ((local >> 1) & 1) ^ 1, tcg::kWaitCycles, r.abort);
         tc::tc_fence_after();
         const uint32_t d = tmem + kAccColumn + a * 128;
         for (int s = 0; ok && s < slabs; ++s, ++it) {
-            const int st = it % STAGES;
-            ok = tc::mbar_wait_or_abort(r.split + st, (it / STAGES) & 1, tcg::kWaitCycles, r.abort);
+            const int st = it % S;
+            ok = tc::mbar_wait_or_abort(r.split + st, (it / S) & 1, tcg::kWaitCycles, r.abort);
             if (!ok) break;
             tc::tc_fence_after();
             const uint32_t bh = tc::smem_u32(r.hi + st * (SLAB / 4)), bl = tc::smem_u32(r.lo + st * (SLAB / 4));
@@ -202,9 +224,9 @@ __device__ __forceinline__ void issue_mmas(const Ring& r, uint32_t tmem, long ti
         }
         if (ok) tc::mma_commit(r.acc_full + a);
     }
-    // every MMA issued so far has completed once this commit arrives
-    tc::mma_commit(r.drain);
-    tc::mbar_wait(r.drain, 0, tcg::kWaitCycles);
+    // every MMA this thread issued has completed once this commit arrives
+    tc::mma_commit(r.drain + which);
+    tc::mbar_wait(r.drain + which, 0, tcg::kWaitCycles);
 }
 
 // Epilogue warps 6-9: the A operand's row `m` (K values) split into TF32 hi
@@ -259,8 +281,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_forward_ws(const __grid_constant
     const int slabs = K / 32;
     if (warp == kProducerWarp) {
         if (lane == 0) produce<T::SLAB>(r, &map_x, tiles, T::COLS, T::N, slabs);
-    } else if (warp == kMmaWarp) {
-        if (lane == 0) issue_mmas<T::N, T::SLAB>(r, tmem, tiles, slabs);
+    } else if (warp == kMmaWarp || warp == kSecondMmaWarp) {
+        if (lane == 0) issue_mmas<T::N, T::SLAB>(r, tmem, tiles, slabs, warp == kMmaWarp ? 0 : 1);
     } else if (warp < kEpilogueWarp) {
         split_all<T::SLAB>(r, tiles, T::N, slabs);
     } else {
@@ -300,6 +322,10 @@ __global__ void __launch_bounds__(THREADS, 1) k_forward_ws(const __grid_constant
 // one: dZ_prev is not stored and the first layer's gradient is accumulated
 // per thread into input_partials[2 blockIdx.x + group][n + k N] (bias at
 // k = K0), one partial per epilogue group.
+// The epilogue's reads of Y_prev (and, with INPUT_GRAD, of the inputs) do not
+// depend on the accumulator, so each thread copies those of its next work
+// item (tile, point) into a shared-memory staging slot while it works on the
+// current one, and the DRAM latency of the loads leaves the critical path.
 // grid = (CTAs over column tiles, N / 128); Ml a multiple of 32, at most 128.
 template <int SID, class Act, bool INPUT_GRAD>
 __global__ void __launch_bounds__(THREADS, 1) k_backward_ws(const __grid_constant__ CUtensorMap map_dz, int Ml, int N,
@@ -309,24 +335,50 @@ __global__ void __launch_bounds__(THREADS, 1) k_backward_ws(const __grid_constan
                                                             int K0, float* __restrict__ input_partials, int* error) {
     constexpr int R = StaticJet<SID>::R;
     using T = Tiling<R>;
+    constexpr int S = T::BSTAGES;
     extern __shared__ uint8_t smem_raw[];
-    Ring r = carve_ring<T::SLAB>(smem_raw);
-    ring_init(r);
+    Ring r = carve_ring<T::SLAB, S>(smem_raw);
+    ring_init<S>(r);
     const uint32_t tmem = *r.tmem_slot;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const long tiles = (P + T::PTS - 1) / T::PTS;
     const int slabs = Ml / 32;
     if (warp == kProducerWarp) {
-        if (lane == 0) produce<T::SLAB>(r, &map_dz, tiles, T::COLS, T::N, slabs);
-    } else if (warp == kMmaWarp) {
-        if (lane == 0) issue_mmas<T::N, T::SLAB>(r, tmem, tiles, slabs);
+        if (lane == 0) produce<T::SLAB, S>(r, &map_dz, tiles, T::COLS, T::N, slabs);
+    } else if (warp == kMmaWarp || warp == kSecondMmaWarp) {
+        if (lane == 0) issue_mmas<T::N, T::SLAB, S>(r, tmem, tiles, slabs, warp == kMmaWarp ? 0 : 1);
     } else if (warp < kEpilogueWarp) {
-        split_all<T::SLAB>(r, tiles, T::N, slabs);
+        split_all<T::SLAB, S>(r, tiles, T::N, slabs);
     } else {
         const int quarter = warp & 3, group = (warp - kEpilogueWarp) >> 2;
+        const int et = threadIdx.x - kEpilogueWarp * 32;  // epilogue thread 0 .. 32 * 4 * groups - 1
         const int n = blockIdx.y * 128 + quarter * 32 + lane;
         if (group == 0) load_weights(r, tmem, W, N, Ml, n, true);
         const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
+        constexpr int SLOT = R * 32 * 4 * kEpilogueGroups;  // floats of one slot: [q][epilogue thread]
+        float* staging = r.staging + et;
+        // The thread's work items in order: points group, group + groups, ...
+        // of each of the CTA's tiles. (ft, fp) is the next item to stage.
+        long ft = blockIdx.x;
+        int fp = group;
+        auto stage = [&](int slot) {
+            if (ft < tiles && ft * T::PTS + fp < P) {
+                const long point = ft * T::PTS + fp;
+                const float* yp = Yprev + ((size_t)point * R) * N + n;
+#pragma unroll
+                for (int q = 0; q < R; ++q)
+                    tc::copy_async4(staging + slot * SLOT + q * 32 * 4 * kEpilogueGroups, yp + (size_t)q * N);
+                if (INPUT_GRAD && lane * 32 < R * K0) tc::prefetch_l2(X0 + (size_t)point * R * K0 + lane * 32);
+            }
+            tc::copy_async_commit();
+            fp += kEpilogueGroups;
+            if (fp >= T::PTS || ft * T::PTS + fp >= P) {
+                fp = group;
+                ft += gridDim.x;
+            }
+        };
+        stage(0);
+        int slot = 0;
         float gacc[9];
 #pragma unroll
         for (int k = 0; k < 9; ++k) gacc[k] = 0.f;
@@ -338,11 +390,13 @@ __global__ void __launch_bounds__(THREADS, 1) k_backward_ws(const __grid_constan
             const long p0 = tile * T::PTS;
             for (int p = group; p < T::PTS; p += kEpilogueGroups) {
                 if (p0 + p >= P) break;
+                stage(slot ^ 1);
                 float g[R], y[R];
                 tc::tmem_read<R>(lane_base + kAccColumn + a * 128 + p * R, g);
-                const float* yp = Yprev + ((size_t)(p0 + p) * R) * N + n;
+                tc::copy_async_wait<1>();
 #pragma unroll
-                for (int q = 0; q < R; ++q) y[q] = __ldg(yp + (size_t)q * N);
+                for (int q = 0; q < R; ++q) y[q] = staging[slot * SLOT + q * 32 * 4 * kEpilogueGroups];
+                slot ^= 1;
                 StaticJet<SID>::template adjoint<Act>(y, g);
                 if (INPUT_GRAD) {
                     fast::input_gradient<R>(g, X0 + (size_t)(p0 + p) * R * K0, K0, gacc);
@@ -356,6 +410,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_backward_ws(const __grid_constan
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(r.acc_empty + a);
         }
+        tc::copy_async_wait<0>();  // no copy may land after the CTA ends
         if (INPUT_GRAD) {
             float* out = input_partials + (size_t)(2 * blockIdx.x + group) * N * (K0 + 1);
 #pragma unroll
@@ -385,6 +440,7 @@ constexpr int kWgBox = 32 * 32 * 4;       // 32 neurons x 32 columns
 constexpr int kWgOperand = 4 * kWgBox;    // 128 neurons
 constexpr int kWgStage = 3 * kWgOperand;  // dZ raw, Y hi, Y lo
 constexpr int kWgSmem = kWgStages * kWgStage + 1024 + 256;
+constexpr int kWgEpilogueWarp = 6;
 constexpr int kWgThreads = 320;  // producer, MMA, 4 split warps, 4 epilogue warps
 constexpr uint32_t kWgAccColumns = 128, kWgTmemColumns = 512;
 
@@ -470,7 +526,7 @@ static __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_
             tc::mma_commit(drain);
             tc::mbar_wait(drain, 0, tcg::kWaitCycles);
         }
-    } else if (warp < kEpilogueWarp) {
+    } else if (warp < kWgEpilogueWarp) {
         // split warps: thread = neuron m (its TMEM lane); the stage's dZ row of
         // that neuron into tensor memory (hi, lo) and its bias over value-row columns
         const int quarter = warp & 3, m = quarter * 32 + lane;
@@ -507,7 +563,7 @@ static __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_
     } else {
         // epilogue warps: split Y_prev of every stage in place, then write the
         // accumulator (lane m, column n) into the partial
-        const int quarter = warp & 3, m = quarter * 32 + lane, tid = threadIdx.x - kEpilogueWarp * 32;
+        const int quarter = warp & 3, m = quarter * 32 + lane, tid = threadIdx.x - kWgEpilogueWarp * 32;
         for (int it = 0; it < chunks; ++it) {
             const int st = it % kWgStages;
             if (!warp_wait(full + st, (it / kWgStages) & 1, abort)) break;
