@@ -145,6 +145,35 @@ struct ColumnLoad {
 // or load is predicated off for the unused inputs (a predicated 8-wide loop
 // issues 2.5x the instructions at K = 2).
 
+// Calls f(e, x[e]) for e = 0 .. L-1 in order, reading the row with the
+// widest loads its alignment allows: the inputs of point p start at
+// X + p L, X 16-byte aligned, so rows of L % 4 == 0 floats are 16-byte
+// aligned and rows of even L 8-byte aligned. Every lane of a warp reads the
+// same row (one broadcast transaction per load).
+template <int L, class F>
+__device__ __forceinline__ void for_row(const float* x, F f) {
+    if constexpr (L % 4 == 0) {
+#pragma unroll
+        for (int i = 0; i < L / 4; ++i) {
+            const float4 v = __ldg(reinterpret_cast<const float4*>(x) + i);
+            f(4 * i, v.x);
+            f(4 * i + 1, v.y);
+            f(4 * i + 2, v.z);
+            f(4 * i + 3, v.w);
+        }
+    } else if constexpr (L % 2 == 0) {
+#pragma unroll
+        for (int i = 0; i < L / 2; ++i) {
+            const float2 v = __ldg(reinterpret_cast<const float2*>(x) + i);
+            f(2 * i, v.x);
+            f(2 * i + 1, v.y);
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < L; ++i) f(i, __ldg(x + i));
+    }
+}
+
 // z[r] = sum_k W[m + k M] x[r K + k]
 template <int R, int K>
 __device__ __forceinline__ void input_rows_k(const float* __restrict__ W, int M, int m, const float* x,
@@ -187,10 +216,7 @@ __device__ __forceinline__ void input_rows(const float* __restrict__ W, int M, i
 // gacc[k] += sum_r g[r] x[r K + k] (k < K), gacc[8] += g[0] (bias)
 template <int R, int K>
 __device__ __forceinline__ void input_gradient_k(const float (&g)[R], const float* x, float (&gacc)[9]) {
-#pragma unroll
-    for (int r = 0; r < R; ++r)
-#pragma unroll
-        for (int k = 0; k < K; ++k) gacc[k] = fmaf(g[r], __ldg(x + r * K + k), gacc[k]);
+    for_row<R * K>(x, [&](int e, float v) { gacc[e % K] = fmaf(g[e / K], v, gacc[e % K]); });
     gacc[8] += g[0];
 }
 template <int R>

@@ -440,9 +440,9 @@ constexpr int kWgBox = 32 * 32 * 4;       // 32 neurons x 32 columns
 constexpr int kWgOperand = 4 * kWgBox;    // 128 neurons
 constexpr int kWgStage = 3 * kWgOperand;  // dZ raw, Y hi, Y lo
 constexpr int kWgSmem = kWgStages * kWgStage + 1024 + 256;
-constexpr int kWgEpilogueWarp = 6;
-constexpr int kWgThreads = 320;  // producer, MMA, 4 split warps, 4 epilogue warps
-constexpr uint32_t kWgAccColumns = 128, kWgTmemColumns = 512;
+constexpr int kWgEpilogueWarp = 6, kWgSecondMmaWarp = 10;
+constexpr int kWgThreads = 352;  // producer, MMA, 4 split warps, 4 epilogue warps, second MMA issuer
+constexpr uint32_t kWgAccColumns = 128, kWgTmemColumns = 512, kWgSecondAcc = 384;
 
 // element (mn, k) of such an operand, in floats from its start
 __device__ __forceinline__ int mn32_index(int mn, int k) {
@@ -467,7 +467,7 @@ static __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_
             tc::mbar_init(split + s, 8);
             tc::mbar_init(empty + s, 1);
         }
-        tc::mbar_init(drain, 1);
+        tc::mbar_init(drain, 2);  // one commit per MMA issuer
         *abort = 0;
         tc::fence_barrier_init();
     }
@@ -485,7 +485,8 @@ static __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_
     const long total_chunks = (columns + 31) / 32;
     const int chunks = blockIdx.x < total_chunks ? int((total_chunks - 1 - blockIdx.x) / gridDim.x + 1) : 0;
     auto chunk_start = [&](int it) { return 32L * ((long)blockIdx.x + (long)it * gridDim.x); };
-    // stage st: [dZ raw][Y hi][Y lo]; tensor memory: G [0, 128), stage st's dZ hi/lo at 128 + 64 st (+32)
+    // stage st: [dZ raw][Y hi][Y lo]; tensor memory: G of the even chunks [0, 128), stage st's dZ hi/lo at
+    // 128 + 64 st (+32), G of the odd chunks [384, 512)
     auto stage_ptr = [&](int st, int part) { return reinterpret_cast<float*>(base + st * kWgStage + part * kWgOperand); };
     auto dz_column = [](int st) { return kWgAccColumns + 64u * uint32_t(st); };
     float* out = partials + (size_t)blockIdx.x * M * (N + 1);
@@ -505,10 +506,13 @@ static __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_
             for (int k = it > kWgStages ? it - kWgStages : 0; k < it; ++k)
                 tc::mbar_wait(full + k % kWgStages, (k / kWgStages) & 1, tcg::kWaitCycles);
         }
-    } else if (warp == kMmaWarp) {
+    } else if (warp == kMmaWarp || warp == kWgSecondMmaWarp) {
+        // two issuers, the even and the odd chunks, each into its own accumulator
         if (lane == 0) {
             constexpr uint32_t idesc = tc::idesc_tf32(M, 128) | (1u << 16);  // B (Y) MN-major, A (dZ) from TMEM
-            for (int it = 0; it < chunks; ++it) {
+            const int which = warp == kMmaWarp ? 0 : 1;
+            const uint32_t acc = which ? tmem + kWgSecondAcc : tmem;
+            for (int it = which; it < chunks; it += 2) {
                 const int st = it % kWgStages;
                 if (!tc::mbar_wait_or_abort(split + st, (it / kWgStages) & 1, tcg::kWaitCycles, abort)) break;
                 tc::tc_fence_after();
@@ -517,9 +521,10 @@ static __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
                     const uint32_t off = kk * 1024;  // 8 columns of Y
-                    tc::mma_tf32_ts(tmem, al + kk * 8, tc::desc_mn32_sw128(yh + off, kWgBox), idesc, (it | kk) != 0);
-                    tc::mma_tf32_ts(tmem, ah + kk * 8, tc::desc_mn32_sw128(yl + off, kWgBox), idesc, 1);
-                    tc::mma_tf32_ts(tmem, ah + kk * 8, tc::desc_mn32_sw128(yh + off, kWgBox), idesc, 1);
+                    tc::mma_tf32_ts(acc, al + kk * 8, tc::desc_mn32_sw128(yh + off, kWgBox), idesc,
+                                    it != which || kk != 0);
+                    tc::mma_tf32_ts(acc, ah + kk * 8, tc::desc_mn32_sw128(yl + off, kWgBox), idesc, 1);
+                    tc::mma_tf32_ts(acc, ah + kk * 8, tc::desc_mn32_sw128(yh + off, kWgBox), idesc, 1);
                 }
                 tc::mma_commit(empty + st);
             }
@@ -562,7 +567,7 @@ static __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_
         if (blockIdx.y == 0) out[(size_t)N * M + m] = bias;
     } else {
         // epilogue warps: split Y_prev of every stage in place, then write the
-        // accumulator (lane m, column n) into the partial
+        // sum of the two accumulators (lane m, column n) into the partial
         const int quarter = warp & 3, m = quarter * 32 + lane, tid = threadIdx.x - kWgEpilogueWarp * 32;
         for (int it = 0; it < chunks; ++it) {
             const int st = it % kWgStages;
@@ -578,13 +583,13 @@ static __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_
             tc::tc_fence_after();
             const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
             for (int c0 = 0; c0 < 128; c0 += 16) {
-                float v[16];
-                if (chunks) {
-                    tc::tmem_read<16>(lane_base + c0, v);
-                } else {
+                float v[16], odd[16];
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) v[j] = 0.f;
-                }
+                for (int j = 0; j < 16; ++j) v[j] = odd[j] = 0.f;
+                if (chunks > 0) tc::tmem_read<16>(lane_base + c0, v);
+                if (chunks > 1) tc::tmem_read<16>(lane_base + kWgSecondAcc + c0, odd);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[j] += odd[j];
 #pragma unroll
                 for (int j = 0; j < 16; ++j) out[m + (size_t)(n_base + c0 + j) * M] = v[j];
             }
