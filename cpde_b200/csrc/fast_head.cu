@@ -21,8 +21,15 @@ struct FastHead {
         const int grid = int(std::min<long>(148L * 8, std::max(1L, (P + 3) / 4)));
         n.partial.reserve(size_t(grid) * O * (K + 1));
         auto& t = e.dat(c.target_id);
+        // two staging slots of a point's values (R rows x K neurons)
+        const size_t smem = size_t(2) * StaticJet<SID>::R * KPT * fast::BM * sizeof(float);
+        static bool ready[64] = {};
+        if (!ready[e.device & 63]) {
+            allow_smem(fast::k_head_matching<SID, Act, O, KPT>, smem);
+            ready[e.device & 63] = true;
+        }
         CPDE_RUN(e, "head_matching",
-                 (fast::k_head_matching<SID, Act, O, KPT><<<grid, fast::BM, 0, e.stream>>>(
+                 (fast::k_head_matching<SID, Act, O, KPT><<<grid, fast::BM, smem, e.stream>>>(
                      K, P, offset, n.weights(L - 1), n.act[L - 1].ptr, n.dz[1].ptr, t.values.ptr, t.w,
                      c.target_rows.ptr, c.weights.ptr, c.weight_samples, multiplier, collect, red, n.partial.ptr)));
         const long size = long(O) * (K + 1);

@@ -11,6 +11,7 @@
 #pragma once
 #include "generated/jets_static.cuh"
 #include "kernels_generic.cuh"
+#include "tc.cuh"
 
 namespace cpde {
 namespace fast {
@@ -630,12 +631,30 @@ __global__ void __launch_bounds__(BM) k_head_matching(int K, long P, int offset,
     for (int o = 0; o < O; ++o) gb[o] = 0.f;
     const double scale = multiplier ? *multiplier : 1.0;
     CostStats local = cost_empty();
+    // The thread's values of its next point go into a shared-memory staging
+    // slot (per-thread asynchronous copies) while it works on the current one.
+    extern __shared__ float ystage[];  // [2][R][KPT * BM]
+    auto stage = [&](long q, int slot) {
+        if (q < P)
+#pragma unroll
+            for (int j = 0; j < KPT; ++j)
+#pragma unroll
+                for (int r = 0; r < R; ++r)
+                    tc::copy_async4(ystage + (slot * R + r) * KPT * BM + t + BM * j,
+                                    Y + ((size_t)q * R + r) * K + t + BM * j);
+        tc::copy_async_commit();
+    };
+    int slot = 0;
+    stage(blockIdx.x, 0);
     for (long p = blockIdx.x; p < P; p += gridDim.x) {
+        stage(p + gridDim.x, slot ^ 1);
+        tc::copy_async_wait<1>();
         float y[KPT][R];
 #pragma unroll
         for (int j = 0; j < KPT; ++j)
 #pragma unroll
-            for (int r = 0; r < R; ++r) y[j][r] = __ldg(Y + ((size_t)p * R + r) * K + t + BM * j);
+            for (int r = 0; r < R; ++r) y[j][r] = ystage[(slot * R + r) * KPT * BM + t + BM * j];
+        slot ^= 1;
 #pragma unroll
         for (int g = 0; g < GROUPS; ++g) {
             float v[32];
@@ -701,6 +720,7 @@ __global__ void __launch_bounds__(BM) k_head_matching(int K, long P, int offset,
             for (int r = 0; r < R; ++r) out[(size_t)r * K] = dy[r];
         }
     }
+    tc::copy_async_wait<0>();
     float* out = partials + (size_t)blockIdx.x * O * (K + 1);
 #pragma unroll
     for (int j = 0; j < KPT; ++j)

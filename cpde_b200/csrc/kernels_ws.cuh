@@ -8,7 +8,8 @@
 //   warps 1, 6 (lane 0) MMA issuers for the even and the odd tiles of the CTA
 //                      (local tile index), each into its own accumulator;
 //                      warp 1 also owns the tensor-memory block;
-//   warps 2-5          split each landed slab into TF32 hi (in place) and lo;
+//   warps 2-5          write the TF32 lo part of each landed slab beside it
+//                      (the raw slab is the hi part);
 //   warps 7-14         load the layer's weights (hi and lo) into tensor memory
 //                      once (warps 7-10), then run the jet epilogue on each
 //                      finished tile: warp w reads TMEM lanes 32 (w % 4) .. +31
@@ -64,40 +65,6 @@ struct Tiling {
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
     const bool ok = tc::mbar_wait_or_abort(bar, parity, tcg::kWaitCycles, abort);
     return __all_sync(0xffffffffu, ok);
-}
-
-// TF32 hi (in place) and lo of float4 elements [0, count) of h4 strided over
-// 128 threads, eight loads in flight per thread; elements for which
-// keep(i) is false become zero in both.
-template <class Keep>
-__device__ __forceinline__ void split_range(float4* h4, float4* l4, int count, int tid, Keep keep) {
-    constexpr int U = 8;
-    for (int base = 0; base < count; base += 128 * U) {
-        float4 v[U];
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int i = base + tid + 128 * u;
-            v[u] = i < count ? h4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int i = base + tid + 128 * u;
-            if (i >= count) break;
-            float4 h = make_float4(0.f, 0.f, 0.f, 0.f), l = h;
-            if (keep(i)) {
-                h.x = tc::tf32_round(v[u].x);
-                h.y = tc::tf32_round(v[u].y);
-                h.z = tc::tf32_round(v[u].z);
-                h.w = tc::tf32_round(v[u].w);
-                l.x = tc::tf32_round(v[u].x - h.x);
-                l.y = tc::tf32_round(v[u].y - h.y);
-                l.z = tc::tf32_round(v[u].z - h.z);
-                l.w = tc::tf32_round(v[u].w - h.w);
-            }
-            h4[i] = h;
-            l4[i] = l;
-        }
-    }
 }
 
 struct Ring {
@@ -173,7 +140,32 @@ __device__ __forceinline__ void produce(const Ring& r, const CUtensorMap* map, l
     for (uint32_t k = it > S ? it - S : 0; k < it; ++k) tc::mbar_wait(r.full + k % S, (k / S) & 1, tcg::kWaitCycles);
 }
 
-// Split warps: TF32 hi in place and lo beside it, for every slab in order.
+// lo parts of float4 elements [0, count) of x4 into l4, strided over 128
+// threads, eight loads in flight per thread. The tensor core reads an fp32
+// operand of a kind::tf32 MMA as its top 19 bits (sign, exponent, 10 mantissa
+// bits), so the raw slab already is the hi part, hi = trunc(x), and
+// lo = RN_tf32(x - trunc(x)) leaves x - hi - lo below 2^-21 |x|, the accuracy
+// of a split that rounds both parts.
+__device__ __forceinline__ void split_lo_range(const float4* x4, float4* l4, int count, int tid) {
+    constexpr int U = 8;
+    auto lo = [](float x) { return tc::tf32_round(x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u)); };
+    for (int base = 0; base < count; base += 128 * U) {
+        float4 v[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int i = base + tid + 128 * u;
+            v[u] = i < count ? x4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int i = base + tid + 128 * u;
+            if (i >= count) break;
+            l4[i] = make_float4(lo(v[u].x), lo(v[u].y), lo(v[u].z), lo(v[u].w));
+        }
+    }
+}
+
+// Split warps: the TF32 lo part of every slab, in order, beside the raw slab.
 template <int SLAB, int S = STAGES>
 __device__ __forceinline__ void split_all(const Ring& r, long tiles, int N, int slabs) {
     const int tid = threadIdx.x - kSplitWarp * 32;  // 0..127
@@ -182,8 +174,8 @@ __device__ __forceinline__ void split_all(const Ring& r, long tiles, int N, int 
         for (int s = 0; s < slabs; ++s, ++it) {
             const int st = it % S;
             if (!warp_wait(r.full + st, (it / S) & 1, r.abort)) return;
-            split_range(reinterpret_cast<float4*>(r.hi + st * (SLAB / 4)),
-                        reinterpret_cast<float4*>(r.lo + st * (SLAB / 4)), N * 8, tid, [](int) { return true; });
+            split_lo_range(reinterpret_cast<const float4*>(r.hi + st * (SLAB / 4)),
+                           reinterpret_cast<float4*>(r.lo + st * (SLAB / 4)), N * 8, tid);
             tc::fence_proxy_async();
             __syncwarp();
             if ((threadIdx.x & 31) == 0) tc::mbar_arrive(r.split + st);
@@ -191,9 +183,10 @@ __device__ __forceinline__ void split_all(const Ring& r, long tiles, int N, int 
 }
 
 // MMA issuer `which` (0 or 1): for the CTA's tiles of local index
-// which, which + 2, ..., lo*hi + hi*lo + hi*hi over the K slabs into
-// accumulator `which`; each slab's stage is released by a commit once its
-// MMAs have read it. Slab counter `it` runs over all the CTA's slabs in ring
+// which, which + 2, ..., lo*hi + hi*hi + hi*lo over the K slabs into
+// accumulator `which`, once the split warps have written the slab's lo part
+// (issuing the two terms of the raw slab before that wait measured slower);
+// each slab's stage is released by a commit once its MMAs have read it. Slab counter `it` runs over all the CTA's slabs in ring
 // order, the other issuer's included.
 template <int N, int SLAB, int S = STAGES>
 __device__ __forceinline__ void issue_mmas(const Ring& r, uint32_t tmem, long tiles, int slabs, int which) {
@@ -430,15 +423,17 @@ __global__ void __launch_bounds__(THREADS, 1) k_backward_ws(const __grid_constan
 // 32-byte atoms, the layout of MN-major TF32 operands). The split warps move
 // dZ through registers into tensor memory as the K-major A operand (thread =
 // neuron: its 32 columns, TF32 hi and lo, plus its bias sum over value-row
-// columns) while the epilogue warps split Y_prev in place into hi and lo as
-// the MN-major B operand, so shared memory carries each operand once per MMA
-// term instead of also serving the A side. The 128 x 128 accumulator stays in
-// tensor memory for the whole kernel. grid = (CTAs, N / 128).
+// columns) while the epilogue warps write the lo part of Y_prev beside the
+// raw operand (its hi part) as the MN-major B operand, so shared memory
+// carries each operand once per MMA term instead of also serving the A side.
+// Two MMA issuers take the even and the odd stages, each into its own
+// 128 x 128 accumulator, which stay in tensor memory for the whole kernel and
+// are summed in the epilogue. grid = (CTAs, N / 128).
 
 constexpr int kWgStages = 4;
 constexpr int kWgBox = 32 * 32 * 4;       // 32 neurons x 32 columns
 constexpr int kWgOperand = 4 * kWgBox;    // 128 neurons
-constexpr int kWgStage = 3 * kWgOperand;  // dZ raw, Y hi, Y lo
+constexpr int kWgStage = 3 * kWgOperand;  // dZ raw, Y raw (= hi), Y lo
 constexpr int kWgSmem = kWgStages * kWgStage + 1024 + 256;
 constexpr int kWgEpilogueWarp = 6, kWgSecondMmaWarp = 10;
 constexpr int kWgThreads = 352;  // producer, MMA, 4 split warps, 4 epilogue warps, second MMA issuer
@@ -485,7 +480,7 @@ static __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_
     const long total_chunks = (columns + 31) / 32;
     const int chunks = blockIdx.x < total_chunks ? int((total_chunks - 1 - blockIdx.x) / gridDim.x + 1) : 0;
     auto chunk_start = [&](int it) { return 32L * ((long)blockIdx.x + (long)it * gridDim.x); };
-    // stage st: [dZ raw][Y hi][Y lo]; tensor memory: G of the even chunks [0, 128), stage st's dZ hi/lo at
+    // stage st: [dZ raw][Y raw = hi][Y lo]; tensor memory: G of the even chunks [0, 128), stage st's dZ hi/lo at
     // 128 + 64 st (+32), G of the odd chunks [384, 512)
     auto stage_ptr = [&](int st, int part) { return reinterpret_cast<float*>(base + st * kWgStage + part * kWgOperand); };
     auto dz_column = [](int st) { return kWgAccColumns + 64u * uint32_t(st); };
@@ -566,15 +561,16 @@ static __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_
         }
         if (blockIdx.y == 0) out[(size_t)N * M + m] = bias;
     } else {
-        // epilogue warps: split Y_prev of every stage in place, then write the
-        // sum of the two accumulators (lane m, column n) into the partial
+        // epilogue warps: the TF32 lo part of Y_prev of every stage (the raw
+        // operand is its hi part; the columns past the end of the data arrive
+        // as zeros from the tensor map), then write the sum of the two
+        // accumulators (lane m, column n) into the partial
         const int quarter = warp & 3, m = quarter * 32 + lane, tid = threadIdx.x - kWgEpilogueWarp * 32;
         for (int it = 0; it < chunks; ++it) {
             const int st = it % kWgStages;
             if (!warp_wait(full + st, (it / kWgStages) & 1, abort)) break;
-            const int valid = int(min(32L, columns - chunk_start(it)));
-            split_range(reinterpret_cast<float4*>(stage_ptr(st, 1)), reinterpret_cast<float4*>(stage_ptr(st, 2)),
-                        kWgOperand / 16, tid, [valid](int i) { return ((i >> 3) & 31) < valid; });
+            split_lo_range(reinterpret_cast<const float4*>(stage_ptr(st, 1)), reinterpret_cast<float4*>(stage_ptr(st, 2)),
+                           kWgOperand / 16, tid);
             tc::fence_proxy_async();
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(split + st);
