@@ -113,9 +113,9 @@ def algorithmic_bytes(points, rows):
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch measured
 # by ncu on the same kernels at 16,384 points and scaled x4 to a 65,536-point
 # launch (the traffic is linear in the columns).
-MEASURED_TRAFFIC = {'forward_ws': int(4 * (234.978 + 185.196) * 1e6), 'weight_gradient_ws': int(4 * (469.817 + 3.787) * 1e6),
-                    'backward_ws': int(4 * (469.887 + 200.892) * 1e6), 'backward_input_ws': int(4 * (473.561 + 5.594) * 1e6),
-                    'head_matching': int(4 * (236.812 + 190.445) * 1e6), 'input_forward': int(4 * (3.709 + 174.699) * 1e6)}
+MEASURED_TRAFFIC = {'forward_ws': int(4 * (234.98 + 183.97) * 1e6), 'weight_gradient_ws': int(4 * (469.79 + 4.07) * 1e6),
+                    'backward_ws': int(4 * (469.87 + 199.63) * 1e6), 'backward_input_ws': int(4 * (473.57 + 3.77) * 1e6),
+                    'head_matching': int(4 * (236.82 + 187.90) * 1e6), 'input_forward': int(4 * (3.71 + 174.55) * 1e6)}
 
 
 def hbm_roofline(kernels, steps, points, rows, peaks, source):
