@@ -41,6 +41,7 @@ constexpr int STAGES = 6;
 constexpr int kMaxK = 128;  // weights resident in tensor memory
 constexpr uint32_t kTmemColumns = 512, kAccColumn = 256;
 constexpr int kSmemLimit = 232448;  // dynamic shared memory of one CTA (227 KB)
+constexpr int kStagingSlots = 3;    // backward: Y_prev staged two work items ahead
 
 template <int R>
 struct Tiling {
@@ -49,10 +50,10 @@ struct Tiling {
     static constexpr int N = ((COLS + 15) / 16) * 16;              // MMA N: multiple of 16 for M = 128
     static constexpr int SLAB = ((N * 128 + 1023) / 1024) * 1024;  // one K slab: N rows of 128 bytes
     static constexpr int SMEM = 2 * STAGES * SLAB + 1024 + 256;
-    // backward: two R-float staging slots per epilogue thread for the
-    // previous layer's values, copied asynchronously one work item ahead;
-    // the slab ring gives up stages where both do not fit
-    static constexpr int YBUF = 2 * R * 4 * 32 * 4 * kEpilogueGroups;
+    // backward: kStagingSlots R-float staging slots per epilogue thread for
+    // the previous layer's values, copied asynchronously kStagingSlots - 1 work
+    // items ahead; the slab ring gives up stages where both do not fit
+    static constexpr int YBUF = kStagingSlots * R * 4 * 32 * 4 * kEpilogueGroups;
     static constexpr int BSTAGES = (kSmemLimit - 1024 - 256 - YBUF) / (2 * SLAB) < STAGES
                                        ? (kSmemLimit - 1024 - 256 - YBUF) / (2 * SLAB)
                                        : STAGES;
@@ -316,9 +317,9 @@ __global__ void __launch_bounds__(THREADS, 1) k_forward_ws(const __grid_constant
 // per thread into input_partials[2 blockIdx.x + group][n + k N] (bias at
 // k = K0), one partial per epilogue group.
 // The epilogue's reads of Y_prev (and, with INPUT_GRAD, of the inputs) do not
-// depend on the accumulator, so each thread copies those of its next work
-// item (tile, point) into a shared-memory staging slot while it works on the
-// current one, and the DRAM latency of the loads leaves the critical path.
+// depend on the accumulator, so each thread copies those of the work item
+// (tile, point) two ahead of its current one into a shared-memory staging
+// slot, and the DRAM latency of the loads leaves the critical path.
 // grid = (CTAs over column tiles, N / 128); Ml a multiple of 32, at most 128.
 template <int SID, class Act, bool INPUT_GRAD>
 __global__ void __launch_bounds__(THREADS, 1) k_backward_ws(const __grid_constant__ CUtensorMap map_dz, int Ml, int N,
@@ -370,7 +371,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_backward_ws(const __grid_constan
                 ft += gridDim.x;
             }
         };
-        stage(0);
+#pragma unroll
+        for (int k = 0; k < kStagingSlots - 1; ++k) stage(k);
         int slot = 0;
         float gacc[9];
 #pragma unroll
@@ -383,13 +385,13 @@ __global__ void __launch_bounds__(THREADS, 1) k_backward_ws(const __grid_constan
             const long p0 = tile * T::PTS;
             for (int p = group; p < T::PTS; p += kEpilogueGroups) {
                 if (p0 + p >= P) break;
-                stage(slot ^ 1);
+                stage(slot == 0 ? kStagingSlots - 1 : slot - 1);  // the slot read one item ago
                 float g[R], y[R];
                 tc::tmem_read<R>(lane_base + kAccColumn + a * 128 + p * R, g);
-                tc::copy_async_wait<1>();
+                tc::copy_async_wait<kStagingSlots - 1>();
 #pragma unroll
                 for (int q = 0; q < R; ++q) y[q] = staging[slot * SLOT + q * 32 * 4 * kEpilogueGroups];
-                slot ^= 1;
+                slot = slot + 1 == kStagingSlots ? 0 : slot + 1;
                 StaticJet<SID>::template adjoint<Act>(y, g);
                 if (INPUT_GRAD) {
                     fast::input_gradient<R>(g, X0 + (size_t)(p0 + p) * R * K0, K0, gacc);

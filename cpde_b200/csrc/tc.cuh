@@ -149,9 +149,19 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const float (&v)[8]) {
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// Reads columns [col, col + COUNT) of this thread's lane into v (COUNT <= 64).
+// After tmem_wait_ld: marks the registers of v as written here, so that no use
+// of them can be scheduled above the wait (the loads' asm statements already
+// name them as outputs).
 template <int COUNT>
-__device__ __forceinline__ void tmem_read(uint32_t taddr, float (&v)[COUNT]) {
+__device__ __forceinline__ void tmem_landed(float (&v)[COUNT]) {
+#pragma unroll
+    for (int i = 0; i < COUNT; ++i) asm volatile("" : "+f"(v[i]));
+}
+
+// Issues the loads of columns [col, col + COUNT) of this thread's lane into v
+// (COUNT <= 64); v is valid after tmem_wait_ld() and tmem_landed(v).
+template <int COUNT>
+__device__ __forceinline__ void tmem_load(uint32_t taddr, float (&v)[COUNT]) {
     int c = 0;
 #pragma unroll
     for (; c + 16 <= COUNT; c += 16) {
@@ -176,7 +186,14 @@ __device__ __forceinline__ void tmem_read(uint32_t taddr, float (&v)[COUNT]) {
     }
 #pragma unroll
     for (; c < COUNT; ++c) tmem_ld1(taddr + c, v[c]);
+}
+
+// Reads columns [col, col + COUNT) of this thread's lane into v (COUNT <= 64).
+template <int COUNT>
+__device__ __forceinline__ void tmem_read(uint32_t taddr, float (&v)[COUNT]) {
+    tmem_load<COUNT>(taddr, v);
     tmem_wait_ld();
+    tmem_landed(v);
 }
 
 // --- MMA ---------------------------------------------------------------------
