@@ -29,11 +29,17 @@ struct FastBackward {
         // output layer: adjoint into the last hidden layer, output weight gradient
         if (!skip_output) {
             const int O = n.neurons[L], K = n.neurons[L - 1];
-            const int bx = int(std::min<long>(148 * 4, std::max(1L, (P + 15) / 16)));
-            dim3 grid(bx, (K + BM - 1) / BM);
+            const int bx = int(std::min<long>(148 * 8, std::max(1L, (P + 15) / 16)));
+            const int slice = output_slice(K);
+            dim3 grid(bx, (K + slice - 1) / slice);
             n.partial.reserve(size_t(bx) * O * (K + 1));
+            static bool out_ready[64] = {};
+            if (!out_ready[e.device & 63]) {
+                allow_smem(k_output_backward<SID, Act>, output_backward_smem<R>());
+                out_ready[e.device & 63] = true;
+            }
             CPDE_RUN(e, "output_backward",
-                     (k_output_backward<SID, Act><<<grid, THREADS, 0, e.stream>>>(
+                     (k_output_backward<SID, Act><<<grid, THREADS, output_backward_smem<R>(), e.stream>>>(
                          O, K, P, n.weights(L - 1), n.dz[0].ptr, n.act[L - 1].ptr, n.dz[1].ptr, n.partial.ptr)));
             long size = long(O) * (K + 1);
             CPDE_RUN(e, "sum_partials", (k_sum_partials<<<fast::sum_grid(size), 256, 0, e.stream>>>(

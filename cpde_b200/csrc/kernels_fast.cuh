@@ -477,61 +477,95 @@ static __global__ void __launch_bounds__(THREADS, 2) k_weight_gradient(int M, in
 static __global__ void k_output_forward(int O, int K, long P, int R, const float* __restrict__ W,
                                  const float* __restrict__ bias, const float* __restrict__ Y,
                                  float* __restrict__ Z) {
+    // a warp per column, four columns in flight (their loads issued together)
+    constexpr int U = 4;
     const int lane = threadIdx.x & 31;
     const long warps = ((long)gridDim.x * blockDim.x) >> 5;
     const long columns = P * R;
-    for (long c = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5; c < columns; c += warps) {
-        const float* y = Y + (size_t)c * K;
-        float acc[8];
+    for (long c0 = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5; c0 < columns; c0 += U * warps) {
+        float acc[U][8];
 #pragma unroll
-        for (int o = 0; o < 8; ++o) acc[o] = 0.f;
+        for (int u = 0; u < U; ++u)
+#pragma unroll
+            for (int o = 0; o < 8; ++o) acc[u][o] = 0.f;
         for (int k = lane; k < K; k += 32) {
-            const float v = __ldg(y + k);
+            float v[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const long c = c0 + u * warps;
+                v[u] = c < columns ? __ldg(Y + (size_t)c * K + k) : 0.f;
+            }
 #pragma unroll
             for (int o = 0; o < 8; ++o)
-                if (o < O) acc[o] = fmaf(__ldg(W + o + (size_t)k * O), v, acc[o]);
+                if (o < O) {
+                    const float w = __ldg(W + o + (size_t)k * O);
+#pragma unroll
+                    for (int u = 0; u < U; ++u) acc[u][o] = fmaf(w, v[u], acc[u][o]);
+                }
         }
 #pragma unroll
-        for (int o = 0; o < 8; ++o) {
-            if (o >= O) break;
-            float v = acc[o];
-            for (int s = 16; s; s >>= 1) v += __shfl_xor_sync(0xffffffffu, v, s);
-            if (lane == 0) Z[(size_t)c * O + o] = v + ((c % R) == 0 ? __ldg(bias + o) : 0.f);
+        for (int u = 0; u < U; ++u) {
+            const long c = c0 + u * warps;
+#pragma unroll
+            for (int o = 0; o < 8; ++o) {
+                if (o >= O) break;
+                float v = acc[u][o];
+                for (int s = 16; s; s >>= 1) v += __shfl_xor_sync(0xffffffffu, v, s);
+                if (lane == 0 && c < columns) Z[(size_t)c * O + o] = v + ((c % R) == 0 ? __ldg(bias + o) : 0.f);
+            }
         }
     }
 }
 
 // Output layer backward: dY = W_out^T dZ_out, adjoint with Y -> dZ of the
 // last hidden layer; weight gradient of the output layer accumulated per CTA
-// (partials[cta][o + k*O], bias at k = K). One thread per (neuron, point).
+// (partials[cta][o + k*O], bias at k = K). One thread per (neuron, point):
+// a CTA covers output_slice(K) neurons (K itself when it divides 128, so no
+// thread idles at widths 32 and 64) and THREADS / slice point lanes; each
+// thread copies the values of its next point into shared memory while it
+// works on the current one.
+__host__ __device__ constexpr int output_slice(int K) { return K <= BM && BM % K == 0 ? K : BM; }
+template <int R>
+constexpr size_t output_backward_smem() { return size_t(2) * R * THREADS * sizeof(float); }
+
 template <int SID, class Act>
 __global__ void __launch_bounds__(THREADS) k_output_backward(int O, int K, long P, const float* __restrict__ W,
                                                              const float* __restrict__ dZout,
                                                              const float* __restrict__ Y, float* __restrict__ dZ,
                                                              float* __restrict__ partials) {
     constexpr int R = StaticJet<SID>::R;
-    __shared__ float red[8][BM + 1];
-    float gw[8];
+    extern __shared__ float ystage[];  // [2][R][THREADS], output_backward_smem<R>() bytes
+    __shared__ float red[THREADS];
+    const int NB = output_slice(K), lanes = THREADS / NB;
+    float gw[8], gb[8];
 #pragma unroll
-    for (int o = 0; o < 8; ++o) gw[o] = 0.f;
-    float gb[8];
-#pragma unroll
-    for (int o = 0; o < 8; ++o) gb[o] = 0.f;
-    // blocks own neuron slices of 128 (blockIdx.y) and stride over points
-    const int m = blockIdx.y * BM + (threadIdx.x % BM);
-    const int lane_p = threadIdx.x / BM;  // 0..1
-    const bool active = m < K;
+    for (int o = 0; o < 8; ++o) gw[o] = gb[o] = 0.f;
+    const int t = threadIdx.x, ml = t % NB, m = blockIdx.y * NB + ml;
+    const int lane_p = t / NB;  // 0 .. lanes - 1 (threads beyond lanes * NB idle)
+    const bool active = m < K && lane_p < lanes;
     float w[8];
 #pragma unroll
     for (int o = 0; o < 8; ++o) w[o] = (o < O && active) ? __ldg(W + o + (size_t)m * O) : 0.f;
-    for (long p = (long)blockIdx.x * 2 + lane_p; p < P; p += (long)gridDim.x * 2) {
+    const long stride = (long)gridDim.x * lanes;
+    auto stage = [&](long q, int slot) {
+        if (active && q < P)
+#pragma unroll
+            for (int r = 0; r < R; ++r)
+                tc::copy_async4(ystage + (slot * R + r) * THREADS + t, Y + ((size_t)q * R + r) * K + m);
+        tc::copy_async_commit();
+    };
+    int slot = 0;
+    long p = (long)blockIdx.x * lanes + lane_p;
+    stage(p, 0);
+    for (; p < P; p += stride) {
+        stage(p + stride, slot ^ 1);
+        tc::copy_async_wait<1>();
         if (!active) continue;
         const float* dzo = dZout + (size_t)p * R * O;
-        const float* yp = Y + (size_t)p * R * K + m;
         float g[R], y[R];
 #pragma unroll
         for (int r = 0; r < R; ++r) {
-            y[r] = yp[(size_t)r * K];
+            y[r] = ystage[(slot * R + r) * THREADS + t];
             float acc = 0.f;
 #pragma unroll
             for (int o = 0; o < 8; ++o)
@@ -543,29 +577,37 @@ __global__ void __launch_bounds__(THREADS) k_output_backward(int O, int K, long 
                 }
             g[r] = acc;
         }
+        slot ^= 1;
         StaticJet<SID>::template adjoint<Act>(y, g);
         float* out = dZ + (size_t)p * R * K + m;
 #pragma unroll
         for (int r = 0; r < R; ++r) out[(size_t)r * K] = g[r];
     }
-    // fold the two point-lanes of each neuron
-    for (int o = 0; o < 8; ++o) {
-        if (o >= O) break;
-        if (lane_p == 1) red[o][threadIdx.x % BM] = gw[o];
+    tc::copy_async_wait<0>();
+    // fold the point lanes of each neuron, lane order
+    float* out = partials + (size_t)blockIdx.x * O * (K + 1);
+    for (int o = 0; o < O && o < 8; ++o) {
+        red[t] = gw[o];
         __syncthreads();
-        if (lane_p == 0) gw[o] += red[o][threadIdx.x % BM];
+        if (lane_p == 0 && active) {
+            float sum = red[ml];
+            for (int l = 1; l < lanes; ++l) sum += red[l * NB + ml];
+            out[o + (size_t)m * O] = sum;
+        }
         __syncthreads();
     }
-    // partial of CTA column x: full O x (K+1) column-major; y-blocks write disjoint neuron slices
-    float* out = partials + (size_t)blockIdx.x * O * (K + 1);
-    if (lane_p == 0 && active)
-        for (int o = 0; o < O; ++o) out[o + (size_t)m * O] = gw[o];
-    // bias: every neuron thread saw the same output adjoints; use neuron 0's two point lanes
-    if (blockIdx.y == 0 && threadIdx.x == BM)
-        for (int o = 0; o < O; ++o) red[o][0] = gb[o];
-    __syncthreads();
-    if (blockIdx.y == 0 && threadIdx.x == 0)
-        for (int o = 0; o < O; ++o) out[o + (size_t)K * O] = gb[o] + red[o][0];
+    // bias: every neuron saw the same output adjoints; neuron 0 of each lane
+    if (blockIdx.y == 0)
+        for (int o = 0; o < O && o < 8; ++o) {
+            red[t] = gb[o];
+            __syncthreads();
+            if (t == 0) {
+                float sum = 0.f;
+                for (int l = 0; l < lanes; ++l) sum += red[l * NB];
+                out[o + (size_t)K * O] = sum;
+            }
+            __syncthreads();
+        }
 }
 
 // Sum over the 32 lanes of a warp of each of 32 per-lane values, transposed:

@@ -102,6 +102,36 @@ def test_fast_tier_wide_layers_and_single_output(engine):
     assert gc.layer_error(grads, expected) < 1e-4
 
 
+@pytest.mark.parametrize('sid', [2, 6])
+@pytest.mark.parametrize('width,outputs', [(32, 1), (64, 3), (96, 2), (128, 3)])
+def test_output_layer_widths(engine, sid, width, outputs):
+    """The separate output-layer kernels (every cost except a matching cost on
+    a 128- or 256-wide last layer with few outputs): last hidden widths that
+    divide 128 (one neuron slice per CTA, several point lanes), one that does
+    not, and several outputs; the point count is not a multiple of any lane
+    count."""
+    rows = codegen.SCHEMAS[sid][1]
+    V = len(rows[0])
+    layers = [V, 64, width, outputs]
+    linear = [1, 0, 0, 1]
+    t, x, weights, net, data = setup(engine, rows, layers, linear, 1001, 40 + sid + width)
+    schema = jets.Schema(t[:, 1:])
+    pre, acts = jets.forward(schema, weights, layers, linear, x)
+    tol = gc.tolerance(t)
+    out = engine.download(engine.evaluate(net, data))
+    assert gc.rowwise_error(out, acts[-1]).max() < tol
+    R = len(t)
+    targets = (acts[-1] * 0.5).astype(np.float32)
+    tgt = engine.data(targets, t)
+    mw = np.random.default_rng(2).uniform(0.5, 1.5, (R, 1, outputs)).astype(np.float32)
+    cost = engine.matching(net, data, tgt, list(range(R)), list(range(R)), 1, mw)
+    value, grads = engine.graph_evaluate(net, [cost], sum_graph(1))
+    loss, dout = jets.matching(acts[-1], targets, mw.transpose(0, 2, 1))
+    expected = jets.backward(schema, weights, layers, linear, pre, acts, dout)
+    assert abs(value - loss) <= tol * abs(loss)
+    assert gc.layer_error(grads, expected) < tol
+
+
 POINT_SHAPES = {'o1': [128, 64, 128, 1], 'o2': [128, 128, 2], 'wide': [96, 256, 1]}
 
 
