@@ -91,6 +91,14 @@ struct FastBackward {
                 CPDE_RUN(e, "weight_gradient_tc",
                          (tcg::k_weight_gradient_tc<<<wg, tcg::THREADS, tcg::kWgSmem, e.stream>>>(
                              md, ma, M, N, cols, R, per, n.partial.ptr, e.tc_error.ptr)));
+            } else if (M <= 64 && N <= 64) {
+                // 64 x 64 tiles of 64 threads, about eight CTAs per SM
+                splits = std::max(1L, std::min<long>(148L * 8, (cols + 63) / 64));
+                per = ((cols + splits - 1) / splits + BK - 1) / BK * BK;
+                splits = (cols + per - 1) / per;
+                n.partial.reserve(size_t(splits) * M * (N + 1));
+                CPDE_RUN(e, "weight_gradient", (k_weight_gradient64<<<dim3(unsigned(splits), 1, 1), 64, 0, e.stream>>>(
+                                                   M, N, cols, R, per, cur, n.act[l - 1].ptr, n.partial.ptr)));
             } else {
                 CPDE_RUN(e, "weight_gradient", (k_weight_gradient<<<wg, THREADS, 0, e.stream>>>(
                                                    M, N, cols, R, per, cur, n.act[l - 1].ptr, n.partial.ptr)));

@@ -379,31 +379,33 @@ __global__ void __launch_bounds__(THREADS, 2) k_backward(int M, int K, long P, c
 
 // ---------------------------------------------------------------------------
 // Weight gradient of a hidden layer, split over columns: each CTA sums
-// dZ[:, c] A[:, c]^T over its column range into a 128 x 128 tile (plus the
+// dZ[:, c] A[:, c]^T over its column range into a TILE x TILE tile (plus the
 // bias column: sum of dZ over value-row columns) and stores a partial
-// partials[cta][m + n*M] (n = N is the bias). grid = (splits, ceil(N/128),
-// ceil(M/128)).
+// partials[cta][m + n*M] (n = N is the bias). grid = (splits, ceil(N/TILE),
+// ceil(M/TILE)), (TILE/8)^2 threads.
 
-static __global__ void __launch_bounds__(THREADS, 2) k_weight_gradient(int M, int N, long columns, int R, long per_split,
-                                                             const float* __restrict__ dZ,
-                                                             const float* __restrict__ A,
-                                                             float* __restrict__ partials) {
-    constexpr int LD = BM + 4;
+template <int TILE>
+__device__ __forceinline__ void weight_gradient_tile(int M, int N, long columns, int R, long per_split,
+                                                     const float* __restrict__ dZ, const float* __restrict__ A,
+                                                     float* __restrict__ partials) {
+    constexpr int TT = TILE / 8, NT = TT * TT;  // threads per tile side, per CTA (8 x 8 outputs each)
+    constexpr int LOADS = 4 * TILE / NT;        // float4 loads of each slab per thread
+    constexpr int LD = TILE + 4;
     __shared__ __align__(16) float As[2][BK][LD];  // dZ slab: [k = column][m]
     __shared__ __align__(16) float Bs[2][BK][LD];  // A slab:  [k = column][n]
-    const int t = threadIdx.x, tx = t & 15, ty = t >> 4;
-    const int n_base = blockIdx.y * BM, m_base = blockIdx.z * BM;
+    const int t = threadIdx.x, tx = t % TT, ty = t / TT;
+    const int n_base = blockIdx.y * TILE, m_base = blockIdx.z * TILE;
     const long c_begin = (long)blockIdx.x * per_split;
     const long c_end = min(columns, c_begin + per_split);
     float acc[8][8] = {};
-    float bias_acc = 0.f;  // thread t < 128: neuron m_base + t
-    float4 ra[2], rb[2];
-    // slab loads: 16 columns x 128 rows = 512 float4; thread loads 2 of each
+    float bias_acc = 0.f;  // thread t < TILE: neuron m_base + t
+    float4 ra[LOADS], rb[LOADS];
+    // slab loads: 16 columns x TILE rows = 4 TILE float4 of each operand
     auto fetch = [&](long c0) {
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
-            int idx = t + j * THREADS;
-            int c = idx >> 5, r4 = idx & 31;  // column in slab, float4 index along rows
+        for (int j = 0; j < LOADS; ++j) {
+            int idx = t + j * NT;
+            int c = idx / (TILE / 4), r4 = idx % (TILE / 4);  // column in slab, float4 index along rows
             long col = c0 + c;
             bool ok = col < c_end;
             int m = m_base + r4 * 4, n = n_base + r4 * 4;
@@ -415,9 +417,9 @@ static __global__ void __launch_bounds__(THREADS, 2) k_weight_gradient(int M, in
     };
     auto store = [&](int buf) {
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
-            int idx = t + j * THREADS;
-            int c = idx >> 5, r4 = idx & 31;
+        for (int j = 0; j < LOADS; ++j) {
+            int idx = t + j * NT;
+            int c = idx / (TILE / 4), r4 = idx % (TILE / 4);
             *reinterpret_cast<float4*>(&As[buf][c][r4 * 4]) = ra[j];
             *reinterpret_cast<float4*>(&Bs[buf][c][r4 * 4]) = rb[j];
         }
@@ -443,7 +445,7 @@ static __global__ void __launch_bounds__(THREADS, 2) k_weight_gradient(int M, in
 #pragma unroll
                     for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
             }
-            if (blockIdx.y == 0 && t < BM) {
+            if (blockIdx.y == 0 && t < TILE) {
                 // value-row columns of this slab carry the bias gradient
                 long first = ((c0 + R - 1) / R) * R;
                 for (long c = first; c < c0 + BK && c < c_end; c += R) bias_acc += As[buf][c - c0][t];
@@ -467,7 +469,22 @@ static __global__ void __launch_bounds__(THREADS, 2) k_weight_gradient(int M, in
             if (n < N) out[m + (size_t)n * M] = acc[i][j];
         }
     }
-    if (blockIdx.y == 0 && t < BM && m_base + t < M) out[m_base + t + (size_t)N * M] = bias_acc;
+    if (blockIdx.y == 0 && t < TILE && m_base + t < M) out[m_base + t + (size_t)N * M] = bias_acc;
+}
+
+static __global__ void __launch_bounds__(THREADS, 2) k_weight_gradient(int M, int N, long columns, int R, long per_split,
+                                                             const float* __restrict__ dZ,
+                                                             const float* __restrict__ A,
+                                                             float* __restrict__ partials) {
+    weight_gradient_tile<BM>(M, N, columns, R, per_split, dZ, A, partials);
+}
+
+// The same with 64 x 64 tiles and 64 threads, for layers of at most 64 x 64
+// (a 128 x 128 tile would compute three quarters zeros there).
+static __global__ void __launch_bounds__(64) k_weight_gradient64(int M, int N, long columns, int R, long per_split,
+                                                          const float* __restrict__ dZ, const float* __restrict__ A,
+                                                          float* __restrict__ partials) {
+    weight_gradient_tile<64>(M, N, columns, R, per_split, dZ, A, partials);
 }
 
 // ---------------------------------------------------------------------------
