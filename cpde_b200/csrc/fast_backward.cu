@@ -18,10 +18,13 @@ struct FastBackward {
         constexpr int R = StaticJet<SID>::R;
         using T = Tiling<R>;
         const size_t smem = Smem<T::BN>::FLOATS * sizeof(float);
+        const size_t smem64 = Smem<T::BN, 64>::FLOATS * sizeof(float);  // layers of at most 64 neurons
         static bool ready[64] = {};
         if (!ready[e.device & 63]) {
             allow_smem(k_backward<SID, Act, false>, smem);
             allow_smem(k_backward<SID, Act, true>, smem);
+            allow_smem(k_backward<SID, Act, false, 64>, smem64);
+            allow_smem(k_backward<SID, Act, true, 64>, smem64);
             ready[e.device & 63] = true;
         }
         const int L = n.layers;
@@ -170,22 +173,33 @@ struct FastBackward {
                 }
                 continue;
             }
+            const bool narrow = N <= 64;  // 64-neuron tiles
             if (input) {
                 const int bx = int(std::min<long>(tiles_p, 148 * 2));
-                dim3 grid(bx, (N + BM - 1) / BM);
+                dim3 grid(bx, narrow ? 1 : (N + BM - 1) / BM);
                 n.input_partial.reserve(size_t(bx) * N * (K0 + 1));
-                CPDE_RUN(e, "backward_input",
-                         (k_backward<SID, Act, true><<<grid, THREADS, smem, e.stream>>>(
-                             N, M, P, W, cur, n.act[1].ptr, nullptr, n.act[0].ptr, K0, n.input_partial.ptr)));
+                if (narrow)
+                    CPDE_RUN(e, "backward_input",
+                             (k_backward<SID, Act, true, 64><<<grid, THREADS, smem64, e.stream>>>(
+                                 N, M, P, W, cur, n.act[1].ptr, nullptr, n.act[0].ptr, K0, n.input_partial.ptr)));
+                else
+                    CPDE_RUN(e, "backward_input",
+                             (k_backward<SID, Act, true><<<grid, THREADS, smem, e.stream>>>(
+                                 N, M, P, W, cur, n.act[1].ptr, nullptr, n.act[0].ptr, K0, n.input_partial.ptr)));
                 long isize = long(N) * (K0 + 1);
                 CPDE_RUN(e, "sum_partials", (k_sum_partials<<<fast::sum_grid(isize), 256, 0, e.stream>>>(
                                                 n.input_partial.ptr, bx, isize, n.gradient_base(0, target))));
             } else {
                 const int bx = int(std::min<long>(tiles_p, 148 * 8));
-                dim3 grid(bx, (N + BM - 1) / BM);
-                CPDE_RUN(e, "backward",
-                         (k_backward<SID, Act, false><<<grid, THREADS, smem, e.stream>>>(
-                             N, M, P, W, cur, n.act[l - 1].ptr, next, nullptr, 0, nullptr)));
+                dim3 grid(bx, narrow ? 1 : (N + BM - 1) / BM);
+                if (narrow)
+                    CPDE_RUN(e, "backward",
+                             (k_backward<SID, Act, false, 64><<<grid, THREADS, smem64, e.stream>>>(
+                                 N, M, P, W, cur, n.act[l - 1].ptr, next, nullptr, 0, nullptr)));
+                else
+                    CPDE_RUN(e, "backward",
+                             (k_backward<SID, Act, false><<<grid, THREADS, smem, e.stream>>>(
+                                 N, M, P, W, cur, n.act[l - 1].ptr, next, nullptr, 0, nullptr)));
                 cur = next;
             }
         }

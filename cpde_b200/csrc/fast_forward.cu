@@ -17,9 +17,11 @@ struct FastForward {
         constexpr int R = StaticJet<SID>::R;
         using T = Tiling<R>;
         const size_t smem = Smem<T::BN>::FLOATS * sizeof(float);
+        const size_t smem64 = Smem<T::BN, 64>::FLOATS * sizeof(float);  // layers of at most 64 neurons
         static bool ready[64] = {};
         if (!ready[e.device & 63]) {
             allow_smem(k_forward<SID, Act>, smem);
+            allow_smem(k_forward<SID, Act, 64>, smem64);
             ready[e.device & 63] = true;
         }
         const int L = n.layers;
@@ -64,6 +66,11 @@ struct FastForward {
                 CPDE_RUN(e, "forward_tc",
                          (tcg::k_forward_tc<SID, Act><<<grid, tcg::THREADS, TT::SMEM, e.stream>>>(
                              mh, ml, mx, M, K, P, b, n.act[l].ptr, e.tc_error.ptr)));
+            } else if (M <= 64) {
+                dim3 grid(unsigned((P + T::PTS - 1) / T::PTS), 1);
+                CPDE_RUN(e, "forward",
+                         (k_forward<SID, Act, 64><<<grid, THREADS, smem64, e.stream>>>(M, K, P, W, b, n.act[l - 1].ptr,
+                                                                                        n.act[l].ptr)));
             } else {
                 dim3 grid(unsigned((P + T::PTS - 1) / T::PTS), unsigned((M + BM - 1) / BM));
                 CPDE_RUN(e, "forward",

@@ -30,38 +30,40 @@ struct Tiling {
     static constexpr int TN = BN / 16;  // columns per thread
 };
 
-// Shared memory of the GEMM main loop, reused by the epilogue as a Z tile.
-template <int BN>
+// Shared memory of the GEMM main loop, reused by the epilogue as a Z tile
+// (BMT neurons: 128, or 64 for layers of at most 64 neurons).
+template <int BN, int BMT = BM>
 struct Smem {
-    static constexpr int LDA = BM + 4, LDB = BN + 4, LDZ = BM + 4;
+    static constexpr int LDA = BMT + 4, LDB = BN + 4, LDZ = BMT + 4;
     static constexpr int MAIN = 2 * BK * LDA + 2 * BK * LDB;
     static constexpr int EPI = BN * LDZ;
     static constexpr int FLOATS = MAIN > EPI ? MAIN : EPI;
 };
 
 // ---------------------------------------------------------------------------
-// Main loop: acc[8][TN] += A (128 x K) * B (K x BN); thread (ty, tx) owns rows
-// ty*8..ty*8+7 and columns tx + 16 j. A and B slabs are staged through
-// registers so the next slab's global loads overlap the current FMAs.
-//   A loader: a(m, k) for m < 128, k < K (zero outside)
+// Main loop: acc[RM][TN] += A (BMT x K) * B (K x BN), RM = BMT / 16; thread
+// (ty, tx) owns rows ty*RM..ty*RM+RM-1 and columns tx + 16 j. A and B slabs
+// are staged through registers so the next slab's global loads overlap the
+// current FMAs.
+//   A loader: a(m, k) for m < BMT, k < K (zero outside)
 //   B loader: b4(c, k4) returns float4 of b(k4*4 .. k4*4+3, c) (zero outside)
 
-template <int BN, class ALoad, class BLoad>
-__device__ __forceinline__ void gemm_main(float (&acc)[8][BN / 16], float* smem, int K, const ALoad& aload,
+template <int BN, int BMT = BM, class ALoad, class BLoad>
+__device__ __forceinline__ void gemm_main(float (&acc)[BMT / 16][BN / 16], float* smem, int K, const ALoad& aload,
                                           const BLoad& bload) {
-    using S = Smem<BN>;
-    constexpr int TN = BN / 16;
+    using S = Smem<BN, BMT>;
+    constexpr int TN = BN / 16, RM = BMT / 16;
     float* As = smem;                   // [2][BK][LDA]
     float* Bs = smem + 2 * BK * S::LDA;  // [2][BK][LDB]
     const int t = threadIdx.x, tx = t & 15, ty = t >> 4;
-    // A slab: 16 x 128 = 2048 values, 8 per thread: k = t/16 (0..15), m = (t%16)*8 + i
+    // A slab: 16 x BMT values, RM per thread: k = t/16 (0..15), m = (t%16)*RM + i
     constexpr int BLOADS = (BN * 4 + THREADS - 1) / THREADS;  // float4 loads of the B slab per thread
-    float ra[8];
+    float ra[RM];
     float4 rb[BLOADS];
     auto fetch = [&](int k0) {
-        const int k = t >> 4, m0 = (t & 15) * 8;
+        const int k = t >> 4, m0 = (t & 15) * RM;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) ra[i] = aload(m0 + i, k0 + k);
+        for (int i = 0; i < RM; ++i) ra[i] = aload(m0 + i, k0 + k);
 #pragma unroll
         for (int j = 0; j < BLOADS; ++j) {
             int idx = t + j * THREADS;  // (column, k-quad)
@@ -72,9 +74,9 @@ __device__ __forceinline__ void gemm_main(float (&acc)[8][BN / 16], float* smem,
     auto store = [&](int buf) {
         float* a = As + buf * BK * S::LDA;
         float* b = Bs + buf * BK * S::LDB;
-        const int k = t >> 4, m0 = (t & 15) * 8;
+        const int k = t >> 4, m0 = (t & 15) * RM;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) a[k * S::LDA + m0 + i] = ra[i];
+        for (int i = 0; i < RM; ++i) a[k * S::LDA + m0 + i] = ra[i];
 #pragma unroll
         for (int j = 0; j < BLOADS; ++j) {
             int idx = t + j * THREADS;
@@ -98,14 +100,20 @@ __device__ __forceinline__ void gemm_main(float (&acc)[8][BN / 16], float* smem,
         const float* b = Bs + buf * BK * S::LDB;
 #pragma unroll
         for (int k = 0; k < BK; ++k) {
-            const float4 a0 = *reinterpret_cast<const float4*>(a + k * S::LDA + ty * 8);
-            const float4 a1 = *reinterpret_cast<const float4*>(a + k * S::LDA + ty * 8 + 4);
-            const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            float av[RM];
+#pragma unroll
+            for (int i4 = 0; i4 < RM / 4; ++i4) {
+                const float4 a4 = *reinterpret_cast<const float4*>(a + k * S::LDA + ty * RM + 4 * i4);
+                av[4 * i4] = a4.x;
+                av[4 * i4 + 1] = a4.y;
+                av[4 * i4 + 2] = a4.z;
+                av[4 * i4 + 3] = a4.w;
+            }
             float bv[TN];
 #pragma unroll
             for (int j = 0; j < TN; ++j) bv[j] = b[k * S::LDB + tx + 16 * j];
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
+            for (int i = 0; i < RM; ++i)
 #pragma unroll
                 for (int j = 0; j < TN; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
         }
@@ -117,15 +125,18 @@ __device__ __forceinline__ void gemm_main(float (&acc)[8][BN / 16], float* smem,
     __syncthreads();  // smem is reused by the epilogue
 }
 
-template <int BN>
-__device__ __forceinline__ void stage_tile(const float (&acc)[8][BN / 16], float* smem) {
-    using S = Smem<BN>;
+template <int BN, int BMT = BM>
+__device__ __forceinline__ void stage_tile(const float (&acc)[BMT / 16][BN / 16], float* smem) {
+    using S = Smem<BN, BMT>;
+    constexpr int RM = BMT / 16;
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
 #pragma unroll
     for (int j = 0; j < BN / 16; ++j) {
-        float* z = smem + (tx + 16 * j) * S::LDZ + ty * 8;
-        *reinterpret_cast<float4*>(z) = make_float4(acc[0][j], acc[1][j], acc[2][j], acc[3][j]);
-        *reinterpret_cast<float4*>(z + 4) = make_float4(acc[4][j], acc[5][j], acc[6][j], acc[7][j]);
+        float* z = smem + (tx + 16 * j) * S::LDZ + ty * RM;
+#pragma unroll
+        for (int i4 = 0; i4 < RM / 4; ++i4)
+            *reinterpret_cast<float4*>(z + 4 * i4) =
+                make_float4(acc[4 * i4][j], acc[4 * i4 + 1][j], acc[4 * i4 + 2][j], acc[4 * i4 + 3][j]);
     }
     __syncthreads();
 }
@@ -241,28 +252,28 @@ __device__ __forceinline__ void input_gradient(const float (&g)[R], const float*
 // Hidden layer forward: Y = f(W X + b) with the jet combine in the epilogue.
 // grid = (ceil(P / PTS), ceil(M / 128)). Requires K % 4 == 0.
 
-template <int SID, class Act>
+template <int SID, class Act, int BMT = BM>
 __global__ void __launch_bounds__(THREADS, 2) k_forward(int M, int K, long P, const float* __restrict__ W,
                                                      const float* __restrict__ bias, const float* __restrict__ X,
                                                      float* __restrict__ Y) {
     constexpr int R = StaticJet<SID>::R;
     using T = Tiling<R>;
-    using S = Smem<T::BN>;
+    using S = Smem<T::BN, BMT>;
     extern __shared__ float4 smem4[];
     float* smem = reinterpret_cast<float*>(smem4);
     const long p0 = (long)blockIdx.x * T::PTS;
-    const int m_base = blockIdx.y * BM;
+    const int m_base = blockIdx.y * BMT;
     const long points = min((long)T::PTS, P - p0);
-    float acc[8][T::TN] = {};
+    float acc[BMT / 16][T::TN] = {};
     auto aload = [&](int m, int k) -> float {
         int mm = m_base + m;
         return (mm < M && k < K) ? __ldg(W + mm + (size_t)k * M) : 0.f;
     };
     ColumnLoad bload{X + (size_t)p0 * R * K, K, points * R};
-    gemm_main<T::BN>(acc, smem, K, aload, bload);
-    stage_tile<T::BN>(acc, smem);
-    for (int e = threadIdx.x; e < BM * T::PTS; e += THREADS) {
-        const int m = e % BM, p = e / BM;
+    gemm_main<T::BN, BMT>(acc, smem, K, aload, bload);
+    stage_tile<T::BN, BMT>(acc, smem);
+    for (int e = threadIdx.x; e < BMT * T::PTS; e += THREADS) {
+        const int m = e % BMT, p = e / BMT;
         const int mm = m_base + m;
         if (p >= points || mm >= M) continue;
         float z[R], y[R];
@@ -304,17 +315,17 @@ __global__ void __launch_bounds__(THREADS) k_input_forward(int M, int K, long P,
 // gradient partial (M x (K0+1) with K0 input channels, bias last) is
 // accumulated per CTA and dZ_prev is not stored.
 
-template <int SID, class Act, bool INPUT_GRAD>
+template <int SID, class Act, bool INPUT_GRAD, int BMT = BM>
 __global__ void __launch_bounds__(THREADS, 2) k_backward(int M, int K, long P, const float* __restrict__ W,
                                                       const float* __restrict__ dZ, const float* __restrict__ Yprev,
                                                       float* __restrict__ dZprev, const float* __restrict__ X0,
                                                       int K0, float* __restrict__ input_partials) {
     constexpr int R = StaticJet<SID>::R;
     using T = Tiling<R>;
-    using S = Smem<T::BN>;
+    using S = Smem<T::BN, BMT>;
     extern __shared__ float4 smem4[];
     float* smem = reinterpret_cast<float*>(smem4);
-    const int m_base = blockIdx.y * BM;
+    const int m_base = blockIdx.y * BMT;
     // INPUT_GRAD: up to 8 input channels + bias of this thread's neuron (every
     // role of a thread has the same neuron because THREADS is a multiple of BM)
     float gacc[9];
@@ -324,17 +335,17 @@ __global__ void __launch_bounds__(THREADS, 2) k_backward(int M, int K, long P, c
     for (long tile = blockIdx.x; tile * T::PTS < P; tile += gridDim.x) {
         const long p0 = tile * T::PTS;
         const long points = min((long)T::PTS, P - p0);
-        float acc[8][T::TN] = {};
+        float acc[BMT / 16][T::TN] = {};
         // A = W^T: a(m, k) = W[k + m*K] (W is K x M column-major)
         auto aload = [&](int m, int k) -> float {
             int mm = m_base + m;
             return (mm < M && k < K) ? __ldg(W + k + (size_t)mm * K) : 0.f;
         };
         ColumnLoad bload{dZ + (size_t)p0 * R * K, K, points * R};
-        gemm_main<T::BN>(acc, smem, K, aload, bload);
-        stage_tile<T::BN>(acc, smem);
-        for (int e = threadIdx.x; e < BM * T::PTS; e += THREADS) {
-            const int m = e % BM, p = e / BM;
+        gemm_main<T::BN, BMT>(acc, smem, K, aload, bload);
+        stage_tile<T::BN, BMT>(acc, smem);
+        for (int e = threadIdx.x; e < BMT * T::PTS; e += THREADS) {
+            const int m = e % BMT, p = e / BMT;
             const int mm = m_base + m;
             if (p >= points || mm >= M) continue;
             float g[R], y[R];
@@ -358,20 +369,20 @@ __global__ void __launch_bounds__(THREADS, 2) k_backward(int M, int K, long P, c
     if (INPUT_GRAD) {
         // Fold this thread's roles into per-neuron sums in smem, then store the
         // CTA partial: input_partials[cta][m][k], k = 0..K0 (bias last).
-        float* red = smem;  // [BM][9]
-        for (int i = threadIdx.x; i < BM * 9; i += THREADS) red[i] = 0.f;
+        float* red = smem;  // [BMT][9]
+        for (int i = threadIdx.x; i < BMT * 9; i += THREADS) red[i] = 0.f;
         __syncthreads();
-        const int m = threadIdx.x % BM;
-        for (int turn = 0; turn < THREADS / BM; ++turn) {
-            if (threadIdx.x / BM == turn)
+        const int m = threadIdx.x % BMT;
+        for (int turn = 0; turn < THREADS / BMT; ++turn) {
+            if (threadIdx.x / BMT == turn)
 #pragma unroll
                 for (int k = 0; k < 9; ++k) red[m * 9 + k] += gacc[k];
             __syncthreads();
         }
         // partial of CTA column x: full M x (K0+1) column-major; y-blocks write disjoint neuron slices
         float* out = input_partials + (size_t)blockIdx.x * M * (K0 + 1);
-        for (int i = threadIdx.x; i < BM * (K0 + 1); i += THREADS) {
-            int ml = i % BM, k = i / BM;
+        for (int i = threadIdx.x; i < BMT * (K0 + 1); i += THREADS) {
+            int ml = i % BMT, k = i / BMT;
             if (m_base + ml < M) out[(m_base + ml) + (size_t)k * M] = red[ml * 9 + (k == K0 ? 8 : k)];
         }
     }
