@@ -187,6 +187,58 @@ def reference_cuda(device, points=POINTS, iterations=3, batches=3):
                     f'op 90, median of {batches} batches x {iterations} epochs, device time')
 
 
+def config3_inputs(points=262144):
+    """Config 3's interior cost: points uniform in the unit disk (seed 2), rows
+    u, u_y, u_x, u_yy, u_xx, integral of (u_xx + u_yy + 1)^2 with weights pi/N,
+    net 2 -> 64^3 -> 1 sigmoid with N(0, 1/fan_in) weights (seed 0)."""
+    from cpde_b200.expressions import Expression, quadrature_inputs, table
+    rng = np.random.default_rng(2)
+    r, th = np.sqrt(rng.uniform(size=points)), 2 * np.pi * rng.uniform(size=points)
+    t = table(['xx', 'yy'], 'xy')
+    x = quadrature_inputs(np.stack([r * np.cos(th), r * np.sin(th)], 1), t)
+    layers = [2, 64, 64, 64, 1]
+    g = np.random.default_rng(0)
+    weights = [np.concatenate([g.normal(0, 1 / np.sqrt(a), (b, a)).ravel(order='F'), np.zeros(b)]).astype(np.float32)
+               for a, b in zip(layers[:-1], layers[1:])]
+    expr = Expression('(u_xx+u_yy+1)**2', table=t, variables='xy', outputs='u', count=points)
+    return t, x, layers, weights, expr, np.full(points, np.pi / points)
+
+
+def config3_integral(device, engine=None, iterations=10, batches=3):
+    """ms/epoch (op 90: forward, integral cost, weight gradients) of config 3's
+    interior cost on this engine and on the reference CUDA server, same GPU."""
+    from cpde_b200 import native
+    from cpde_b200.client import Data, Network, Session
+    t, x, layers, weights, expr, qw = config3_inputs()
+    own = engine or native.Engine(device)
+    try:
+        net = own.network(layers, weights)
+        data = own.data(x, t)
+        cost = own.integral(net, data, len(qw), np.asarray(expr.nodes, np.int32), np.asarray(expr.constants),
+                            expr.field_array(), qw)
+        _, dev, loss, _ = own.benchmark(net, cost, 3, iterations, batches, len(layers) - 1)
+        for kind, h in ((2, cost), (0, data), (1, net)):
+            own.release(kind, h)
+    finally:
+        if engine is None:
+            own.close()
+    out = dict(workload='config 3 interior: 262,144 points in the unit disk, rows u,u_x,u_y,u_xx,u_yy, '
+                        'integral of (u_xx+u_yy+1)^2, 2->64^3->1 sigmoid, op-90 epochs, median device ms',
+               ms=float(np.median(dev)), loss=loss, points_derivs_per_s=len(qw) * len(t) / (float(np.median(dev)) / 1e3))
+    exe = ROOT / 'oracle' / '_ref' / 'cpde_ref_cuda_server'
+    if exe.exists():
+        env = dict(os.environ)
+        env.pop('NVIDIA_TF32_OVERRIDE', None)
+        with Session(exe, device=device, env=env) as s:
+            rnet = Network(s, layers, weights=weights)
+            rd = Data(s, x, t)
+            rc = rnet.integral(rd, expr, weights=qw)
+            _, rdev, rloss, _ = rnet.benchmark(rc, warm=3, iterations=iterations, batches=batches)
+        out.update(reference_cuda_ms=float(np.median(rdev)), reference_loss=rloss,
+                   speedup_vs_reference_cuda=float(np.median(rdev)) / out['ms'])
+    return out
+
+
 PUBLISHED_RTX3090_MS = [0.41, 0.68, 1.10, 1.72, 2.40, 3.59, 5.65]  # docs/benchmarks/fourier-rtx3090.md:23-29
 
 
@@ -380,6 +432,7 @@ def run_b200(args):
             line['cpu_baseline'] = cpu_baseline()
         if world == 1 and not args.no_reference_cuda:
             line['published_workload'] = published_workload(local, engine)
+            line['config3_integral'] = config3_integral(local, engine)
             engine.close()
             ref = reference_cuda(local, args.points)
             if ref is not None:
