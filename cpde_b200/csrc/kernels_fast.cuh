@@ -250,10 +250,12 @@ __device__ __forceinline__ void input_gradient(const float (&g)[R], const float*
 
 // ---------------------------------------------------------------------------
 // Hidden layer forward: Y = f(W X + b) with the jet combine in the epilogue.
-// grid = (ceil(P / PTS), ceil(M / 128)). Requires K % 4 == 0.
+// grid = (ceil(P / PTS), ceil(M / BMT)). Requires K % 4 == 0. The 64-neuron
+// variant is held to 85 registers so that three CTAs share an SM (its tiles
+// are short, and the first slab's load latency is exposed in each).
 
 template <int SID, class Act, int BMT = BM>
-__global__ void __launch_bounds__(THREADS, 2) k_forward(int M, int K, long P, const float* __restrict__ W,
+__global__ void __launch_bounds__(THREADS, BMT == 64 ? 3 : 2) k_forward(int M, int K, long P, const float* __restrict__ W,
                                                      const float* __restrict__ bias, const float* __restrict__ X,
                                                      float* __restrict__ Y) {
     constexpr int R = StaticJet<SID>::R;
@@ -316,7 +318,7 @@ __global__ void __launch_bounds__(THREADS) k_input_forward(int M, int K, long P,
 // accumulated per CTA and dZ_prev is not stored.
 
 template <int SID, class Act, bool INPUT_GRAD, int BMT = BM>
-__global__ void __launch_bounds__(THREADS, 2) k_backward(int M, int K, long P, const float* __restrict__ W,
+__global__ void __launch_bounds__(THREADS, BMT == 64 && !INPUT_GRAD ? 3 : 2) k_backward(int M, int K, long P, const float* __restrict__ W,
                                                       const float* __restrict__ dZ, const float* __restrict__ Yprev,
                                                       float* __restrict__ dZprev, const float* __restrict__ X0,
                                                       int K0, float* __restrict__ input_partials) {
