@@ -81,9 +81,14 @@ struct FastForward {
         if (hidden_only) return;
         const int O = n.neurons[L], K = n.neurons[L - 1];
         const float* W = n.weights(L - 1);
-        CPDE_RUN(e, "output_forward",
-                 (k_output_forward<<<grid_for(P * R * 32, THREADS, 148 * 64), THREADS, 0, e.stream>>>(
-                     O, K, P, R, W, W + long(O) * K, n.act[L - 1].ptr, n.act[L].ptr)));
+        if (O == 1)
+            CPDE_RUN(e, "output_forward",
+                     (k_output_forward1<<<grid_for(P * R, THREADS, 148 * 8), THREADS, 0, e.stream>>>(
+                         K, P, R, W, W + K, n.act[L - 1].ptr, n.act[L].ptr)));
+        else
+            CPDE_RUN(e, "output_forward",
+                     (k_output_forward<<<grid_for(P * R * 32, THREADS, 148 * 64), THREADS, 0, e.stream>>>(
+                         O, K, P, R, W, W + long(O) * K, n.act[L - 1].ptr, n.act[L].ptr)));
     }
     template <int SID>
     void run() {

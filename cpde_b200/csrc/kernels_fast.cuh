@@ -659,6 +659,35 @@ __device__ __forceinline__ float warp_transpose_sum(float (&v)[32]) {
     return v[0];
 }
 
+// Output layer with one linear output: a warp takes 32 columns at a time, each
+// lane sums its slice k = lane + 32 j of every column's dot product (loads
+// coalesced along k), and one transposed butterfly leaves column c0 + lane's
+// sum in lane `lane`: 31 shuffles per 32 columns instead of 5 per column.
+static __global__ void k_output_forward1(int K, long P, int R, const float* __restrict__ W,
+                                         const float* __restrict__ bias, const float* __restrict__ Y,
+                                         float* __restrict__ Z) {
+    const int lane = threadIdx.x & 31;
+    const long warps = ((long)gridDim.x * blockDim.x) >> 5;
+    const long columns = P * R;
+    const float b = __ldg(bias);
+    for (long c0 = (((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5) * 32; c0 < columns; c0 += warps * 32) {
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = 0.f;
+        for (int k = lane; k < K; k += 32) {
+            const float w = __ldg(W + k);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                const long c = c0 + i;
+                v[i] = fmaf(w, c < columns ? __ldg(Y + (size_t)c * K + k) : 0.f, v[i]);
+            }
+        }
+        const float sum = warp_transpose_sum(v);
+        const long c = c0 + lane;
+        if (c < columns) Z[c] = sum + ((c % R) == 0 ? b : 0.f);
+    }
+}
+
 // Fused output head for a matching cost: Z_out = W_out Y + b for O linear
 // outputs, the squared-error loss and its adjoints (the arithmetic and order of
 // k_cost_matching, cuda/cost_kernels.cuh:6-35), the output layer's weight
