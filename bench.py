@@ -165,28 +165,6 @@ def cpu_baseline(points=128, steps=2):
                 ms_per_epoch_sample=ms)
 
 
-def reference_cuda(device, points=POINTS, iterations=3, batches=3):
-    """The reference's own CUDA server, built for sm_100a from its sources by
-    oracle/Makefile, timed with its op-90 command on the same GPU and workload."""
-    exe = ROOT / 'oracle' / '_ref' / 'cpde_ref_cuda_server'
-    if not exe.exists():
-        return None
-    from cpde_b200.client import Data, Network, Session
-    t, x, targets, weights = workload(points)
-    env = dict(os.environ)
-    env.pop('NVIDIA_TF32_OVERRIDE', None)
-    with Session(exe, device=device, env=env) as s:
-        net = Network(s, LAYERS, weights=weights)
-        inp = Data(s, x, t)
-        tgt = Data(s, targets, t)
-        cost = net.matching(inp, tgt, np.ones((1, len(t)), np.float32))
-        wall, gpu, loss, _ = net.benchmark(cost, warm=1, iterations=iterations, batches=batches)
-    ms = float(np.median(gpu))
-    return dict(ms_per_epoch=ms, value=points * len(t) / (ms / 1000), unit=UNIT, loss=loss,
-                how='oracle/_ref/cpde_ref_cuda_server (reference sources, nvcc sm_100a, cuBLAS FP32), '
-                    f'op 90, median of {batches} batches x {iterations} epochs, device time')
-
-
 def config3_inputs(points=262144):
     """Config 3's interior cost: points uniform in the unit disk (seed 2), rows
     u, u_y, u_x, u_yy, u_xx, integral of (u_xx + u_yy + 1)^2 with weights pi/N,
@@ -204,39 +182,396 @@ def config3_inputs(points=262144):
     return t, x, layers, weights, expr, np.full(points, np.pi / points)
 
 
-def config3_integral(device, engine=None, iterations=10, batches=3):
-    """ms/epoch (op 90: forward, integral cost, weight gradients) of config 3's
-    interior cost on this engine and on the reference CUDA server, same GPU."""
+class Workload:
+    """One configuration: derivative table, input jets, network and cost,
+    buildable on this engine (C ABI, cpde_b200.native) and on a reference
+    server session (wire protocol, cpde_b200.client). ``cost`` is
+    ('matching', targets, row_weights) | ('integral', nodes, constants,
+    fields, quadrature_weights) | ('polynomial', terms, coefficients, rhs,
+    point_weights); per-point arrays have the points on their last axis."""
+
+    def __init__(self, name, t, x, layers, linear, weights, cost, chunk=0, reference_chunk=None):
+        self.name, self.t, self.x, self.layers, self.linear = name, t, x, layers, linear
+        self.weights, self.cost, self.chunk = weights, cost, chunk
+        # the reference server refuses chunks whose activation buffers pass
+        # its int32 size limit (cuda/cpde_server.cu:23-25), so wide networks
+        # give it smaller chunks than this engine's
+        self.reference_chunk = chunk if reference_chunk is None else reference_chunk
+
+    @property
+    def points(self):
+        return self.x.shape[2]
+
+    def subset(self, n):
+        """The first n points (every per-point array sliced the same way)."""
+        if n >= self.points:
+            return self
+        kind, *a = self.cost
+        if kind == 'matching':
+            cost = (kind, a[0][:, :, :n], a[1])
+        elif kind == 'integral':
+            cost = (kind, a[0], a[1], a[2][:, :n], a[3][:n])
+        else:
+            cost = (kind, a[0], a[1][:, :n], a[2][:, :n], a[3][:n])
+        return Workload(self.name, self.t, self.x[:, :, :n], self.layers, self.linear, self.weights, cost,
+                        min(self.chunk, n) if self.chunk else 0,
+                        min(self.reference_chunk, n) if self.reference_chunk else 0)
+
+    def own(self, e):
+        """(net, data, cost) on a native engine."""
+        net = e.network(self.layers, self.weights, self.linear)
+        data = e.data(self.x, self.t)
+        kind, *a = self.cost
+        R = len(self.t)
+        if kind == 'matching':
+            tgt = e.data(a[0], self.t)
+            cost = e.matching(net, data, tgt, list(range(R)), list(range(R)), 1, a[1], chunk=self.chunk)
+        elif kind == 'integral':
+            cost = e.integral(net, data, self.points, a[0], a[1], a[2], a[3], chunk=self.chunk)
+        else:
+            cost = e.polynomial(net, data, list(range(R)), 1, a[0], a[1], a[2], a[3], chunk=self.chunk)
+        return net, data, cost
+
+    def reference(self, session):
+        """(net, data, cost) on a reference server; a tanh network goes there
+        as its exact sigmoid reparametrisation (the reference has no tanh)."""
+        from types import SimpleNamespace
+
+        from cpde_b200.client import Data, Network
+        from cpde_b200.expressions import tanh_as_sigmoid
+        linear, weights = tanh_as_sigmoid(self.layers, self.linear, self.weights)
+        net = Network(session, self.layers, weights=weights, linear=linear)
+        data = Data(session, self.x, self.t)
+        kind, *a = self.cost
+        chunk = self.reference_chunk
+        if kind == 'matching':
+            cost = net.matching(data, Data(session, a[0], self.t), a[1][:, 0, :].T, chunk=chunk)
+        elif kind == 'integral':
+            expr = SimpleNamespace(nodes=a[0], constants=a[1], field_array=lambda: a[2], count=self.points)
+            cost = net.integral(data, expr, weights=a[3], chunk=chunk)
+        else:
+            poly = [{(comp,): a[1][k] for k, (_, comp, _) in enumerate(a[0])}]
+            cost = net.polynomial(data, poly, rhs=a[2], weights=a[3][None, :], chunk=chunk)
+        return net, data, cost
+
+    def reference_gradients(self, grads):
+        from cpde_b200.expressions import sigmoid_gradients_to_tanh
+        return sigmoid_gradients_to_tanh(self.layers, self.linear, grads)
+
+
+def config2_workload(points=POINTS):
+    t, x, targets, weights = workload(points)
+    return Workload('config 2', t, x, LAYERS, [1, 0, 0, 0, 0, 1], weights,
+                    ('matching', targets, np.ones((len(t), 1, 1), np.float32)))
+
+
+def config3_workload(points=262144):
+    t, x, layers, weights, expr, qw = config3_inputs(points)
+    return Workload('config 3 interior', t, x, layers, [1, 0, 0, 0, 1], weights,
+                    ('integral', np.asarray(expr.nodes, np.int32), np.asarray(expr.constants), expr.field_array(), qw))
+
+
+def config4_workload(points=1048576, chunk=262144, reference_chunk=65536):
+    t, x, layers, linear, weights, expr, qw = config4_inputs(points)
+    return Workload('config 4', t, x, layers, linear, weights,
+                    ('integral', np.asarray(expr.nodes, np.int32), np.asarray(expr.constants), expr.field_array(), qw),
+                    chunk, reference_chunk)
+
+
+def config5_workload(points=4194304, chunk=131072, reference_chunk=32768):
+    t, x, layers, linear, weights, terms, coeffs, rhs, pw = config5_inputs(points)
+    return Workload('config 5', t, x, layers, linear, weights, ('polynomial', terms, coeffs, rhs, pw), chunk,
+                    reference_chunk)
+
+
+def epoch_gemm_flops(layers, rows, points):
+    """Algorithmic GEMM FLOPs of one epoch: forward, weight gradient (bias
+    column included) and input gradient of every layer but the first."""
+    pairs = list(zip(layers[:-1], layers[1:]))
+    return 2 * rows * points * (sum(a * b for a, b in pairs) + sum((a + 1) * b for a, b in pairs)
+                                + sum(a * b for a, b in pairs[1:]))
+
+
+def tensor_roofline(w, ms, peaks, source):
+    """The epoch's GEMM work against the tensor cores' TF32 rate: a 3xTF32
+    product is three TF32 MMAs, so the algorithmic ceiling is a third of the
+    TF32 rate, which is half the dense bf16 rate (sustained figure of
+    MEASURED_PEAKS.json: the epoch runs for seconds under the power cap)."""
+    flops = epoch_gemm_flops(w.layers, len(w.t), w.points)
+    bf16 = peaks.get('bf16_tflops_sustained', peaks['bf16_tflops'])
+    peak = bf16 / 2 / 3
+    achieved = flops / (ms / 1e3) / 1e12
+    return dict(bound='tensor', achieved=achieved, peak=peak, unit='TFLOP/s', frac=achieved / peak,
+                gemm_tflop_per_epoch=flops / 1e12,
+                peak_source=f'bf16_tflops_sustained of MEASURED_PEAKS.json ({source}) {bf16} / 2 (TF32) / 3 '
+                            '(3xTF32 passes), of measured')
+
+
+def _layer_errors(actual, expected):
+    return [float(np.linalg.norm(np.asarray(a, np.float64) - np.asarray(b, np.float64)) /
+                  max(np.linalg.norm(np.asarray(b, np.float64)), 1e-300)) for a, b in zip(actual, expected)]
+
+
+def _row_errors(actual, expected):
+    a = np.asarray(actual, np.float64).reshape(len(actual), -1)
+    b = np.asarray(expected, np.float64).reshape(len(expected), -1)
+    norm = np.linalg.norm(b, axis=1)
+    return np.linalg.norm(a - b, axis=1) / np.where(norm > 0, norm, 1.0)
+
+
+def same_gpu_comparison(device, w, warm=1, iterations=3, batches=1, reference_points=None, sample_points=4096,
+                        kernels=False):
+    """op-90 epochs (forward, cost, output adjoints, weight gradients) of one
+    workload on this engine and on the reference CUDA server (built from the
+    reference's sources for sm_100a by oracle/Makefile) on the same GPU, with
+    parity: per-layer normwise relative error of the op-90 weight gradients
+    and per-row normwise relative error of op-4 outputs on the first
+    ``sample_points`` points, this engine against the reference. The
+    reference runs on the first ``reference_points`` points when that is
+    smaller than the workload (its time is then scaled by the point ratio and
+    marked extrapolated); the gradients are compared on that same subset."""
     from cpde_b200 import native
-    from cpde_b200.client import Data, Network, Session
-    t, x, layers, weights, expr, qw = config3_inputs()
-    own = engine or native.Engine(device)
-    try:
-        net = own.network(layers, weights)
-        data = own.data(x, t)
-        cost = own.integral(net, data, len(qw), np.asarray(expr.nodes, np.int32), np.asarray(expr.constants),
-                            expr.field_array(), qw)
-        _, dev, loss, _ = own.benchmark(net, cost, 3, iterations, batches, len(layers) - 1)
+    from cpde_b200.client import Session
+    L = len(w.layers) - 1
+    R = len(w.t)
+    sub = w.subset(reference_points or w.points)
+    sample = w.subset(sample_points)
+    out = dict(workload=w.name, points=w.points, rows=R, layers=w.layers, chunk=w.chunk or w.points)
+    with native.Engine(device) as e:
+        net, data, cost = w.own(e)
+        _, dev, loss, grads = e.benchmark(net, cost, warm, iterations, batches, L)
+        out.update(ms=float(np.median(dev)), loss=loss, points_derivs_per_s=w.points * R / (float(np.median(dev)) / 1e3))
+        if kernels:
+            e.timing(True)
+            e.timing_report()
+            e.epoch(net, [cost])
+            e.epoch_result(net, sum(np.asarray(x).size for x in w.weights))
+            rep = e.timing_report()
+            e.timing(False)
+            out['kernels'] = {k: dict(launches=v[0], ms=round(v[1], 4)) for k, v in sorted(rep.items())}
         for kind, h in ((2, cost), (0, data), (1, net)):
-            own.release(kind, h)
-    finally:
-        if engine is None:
-            own.close()
-    out = dict(workload='config 3 interior: 262,144 points in the unit disk, rows u,u_x,u_y,u_xx,u_yy, '
-                        'integral of (u_xx+u_yy+1)^2, 2->64^3->1 sigmoid, op-90 epochs, median device ms',
-               ms=float(np.median(dev)), loss=loss, points_derivs_per_s=len(qw) * len(t) / (float(np.median(dev)) / 1e3))
+            e.release(kind, h)
+        if sub is not w:
+            net, data, cost = sub.own(e)
+            _, _, sub_loss, grads = e.benchmark(net, cost, 0, 1, 1, L)
+        else:
+            sub_loss = loss
+        net, data, _ = sample.own(e)
+        own_rows = e.download(e.evaluate(net, data, chunk=sample.chunk))
     exe = ROOT / 'oracle' / '_ref' / 'cpde_ref_cuda_server'
-    if exe.exists():
+    if not exe.exists():
+        return out
+    env = dict(os.environ)
+    env.pop('NVIDIA_TF32_OVERRIDE', None)
+    try:
+        with Session(exe, device=device, env=env) as s:
+            rnet, _, rcost = sub.reference(s)
+            _, rdev, rloss, rgrads = rnet.benchmark(rcost, warm=warm, iterations=iterations, batches=batches)
+            rnet, rdata, _ = sample.reference(s)
+            ref_rows = rnet.eval(rdata, chunk=sample.reference_chunk).to_numpy()
+    except Exception as exc:  # the reference server exits on CUDA errors (e.g. out of memory)
+        out['reference_error'] = f'{type(exc).__name__}: {exc}'
+        return out
+    rgrads = w.reference_gradients(rgrads)
+    ref_ms = float(np.median(rdev)) * w.points / sub.points
+    out.update(reference_cuda_ms=ref_ms, speedup_vs_reference_cuda=ref_ms / out['ms'],
+               reference_loss=rloss,
+               reference_how=('oracle/_ref/cpde_ref_cuda_server (reference sources, nvcc sm_100a, cuBLAS FP32), '
+                              f'op 90, median of {batches} x {iterations} epochs, device time'
+                              + (f'; timed on the first {sub.points} points and scaled by {w.points / sub.points:g} '
+                                 '(extrapolated: the epoch is linear in the points)' if sub is not w else '')),
+               parity=dict(points=sub.points, loss_relative=abs(sub_loss - rloss) / abs(rloss),
+                           gradient_layer_errors=_layer_errors(grads, rgrads),
+                           output_points=sample.points, output_row_error_max=float(_row_errors(own_rows, ref_rows).max()),
+                           against='reference CUDA server (float32, cuBLAS) on the same inputs'))
+    out['parity']['gradient_error_max'] = max(out['parity']['gradient_layer_errors'])
+    return out
+
+
+def config4_inputs(points=1048576):
+    """Config 4: 3D biharmonic residual (Delta^2 u - g)^2 with
+    g = sin(pi x) sin(pi y) sin(pi z) as a field, every pure and mixed
+    derivative through order 4 (35 rows) on points uniform in [0,1]^3
+    (seed 3), quadrature weights 1/N, net 3 -> 256^5 -> 1 tanh with
+    N(0, 1/fan_in) weights (seed 0)."""
+    from cpde_b200.expressions import Expression, all_mixed, glorot_like, quadrature_inputs
+    pts = np.random.default_rng(3).uniform(0, 1, (points, 3))
+    t = all_mixed(4, 'xyz')
+    x = quadrature_inputs(pts, t)
+    layers = [3, 256, 256, 256, 256, 256, 1]
+    linear = [1, 2, 2, 2, 2, 2, 1]
+    g = np.sin(np.pi * pts[:, 0]) * np.sin(np.pi * pts[:, 1]) * np.sin(np.pi * pts[:, 2])
+    expr = Expression('(u_xxxx+u_yyyy+u_zzzz+2*u_xxyy+2*u_xxzz+2*u_yyzz-g)**2', table=t, variables='xyz',
+                      outputs='u', parameters={'g': g}, count=points)
+    return t, x, layers, linear, glorot_like(layers, seed=0), expr, np.full(points, 1.0 / points)
+
+
+def config5_inputs(points=4194304):
+    """Config 5: value plus pure derivatives through order 6 along 4 axes
+    (25 rows) on points uniform in [-1,1]^4 (seed 4), one polynomial residual
+    sum_a u_{a^6} (unit coefficients, rhs 0) with per-point weights U(0,1)
+    from the same generator, net 4 -> 512^6 -> 1 sigmoid (seed-0 weights)."""
+    from cpde_b200.expressions import glorot_like, pure, quadrature_inputs
+    rng = np.random.default_rng(4)
+    pts = rng.uniform(-1, 1, (points, 4))
+    weights = rng.uniform(0, 1, points).astype(np.float32)
+    t = pure(6, 'xyzw')
+    x = quadrature_inputs(pts, t)
+    layers = [4] + [512] * 6 + [1]
+    linear = [1] + [0] * 6 + [1]
+    sixth = [i for i, row in enumerate(t) if row[0] == 6]
+    terms = [(0, i, -1) for i in sixth]
+    coeffs = np.ones((len(terms), points), np.float32)
+    return t, x, layers, linear, glorot_like(layers, seed=0), terms, coeffs, np.zeros((1, points), np.float32), weights
+
+
+def config3_boundary_inputs(points=4096):
+    """Config 3's boundary cost: equispaced points on the unit circle, weight
+    2 pi / N each, integral of u^2 (value row only)."""
+    from cpde_b200.expressions import Expression, quadrature_inputs, table
+    phi = 2 * np.pi * np.arange(points) / points
+    t = table([''], 'xy')
+    x = quadrature_inputs(np.stack([np.cos(phi), np.sin(phi)], 1), t)
+    expr = Expression('u**2', table=t, variables='xy', outputs='u', count=points)
+    return t, x, expr, np.full(points, 2 * np.pi / points)
+
+
+def train_request(net, costs, epochs, log_every, optimizer=0):
+    """Op-8 payload (cuda/cpde_server.cu:365-371): fresh optimizer state,
+    default steps, values reported every `log_every` epochs."""
+    from cpde_b200.wire import Writer
+    w = (Writer().put('Q', net).array(list(costs), 'u8').put('Q', epochs).put('i', optimizer).put('i', 1)
+         .put('f', 0.0).put('i', 0).put('f', 0.0))
+    for value in (0, log_every, 0, 0, 0):
+        w.put('i', value)
+    return w.string('').put('i', 0).bytes()
+
+
+def _max_over_ranks(dist, value):
+    if dist is None:
+        return value
+    import torch
+    m = torch.tensor([value], device='cuda')
+    dist.all_reduce(m, op=dist.ReduceOp.MAX)
+    return float(m.item())
+
+
+def config3_training(engine, dist, epochs=500, log_every=100, reference_device=None):
+    """Config 3 as specified: `epochs` RPROP epochs (op 8: forward, both
+    integral costs, weight gradients, validation and the update, one host
+    synchronisation per epoch like the reference) of the interior residual
+    (262,144 points in the disk) and the boundary term (4,096 circle points),
+    2 -> 64^3 -> 1 sigmoid. With N ranks the points of both costs are split
+    over them (strong scaling). Device time of the whole run on the engine's
+    stream, max over ranks; the objective every `log_every` epochs. With
+    `reference_device`, the reference CUDA server trains the same problem on
+    that GPU (wall clock of its op 8)."""
+    import torch
+    from cpde_b200.wire import Reader
+    t, x, layers, weights, expr, qw = config3_inputs()
+    tb, xb, eb, qb = config3_boundary_inputs()
+    net = engine.network(layers, weights)
+    data, bdata = engine.data(x, t), engine.data(xb, tb)
+    interior = engine.integral(net, data, len(qw), np.asarray(expr.nodes, np.int32), np.asarray(expr.constants),
+                               expr.field_array(), qw)
+    boundary = engine.integral(net, bdata, len(qb), np.asarray(eb.nodes, np.int32), np.asarray(eb.constants),
+                               eb.field_array(), qb)
+    engine.train(train_request(net, [interior, boundary], 3, 0))  # warm-up: compile, allocate
+    engine.set_weights(net, weights)
+    stream = torch.cuda.ExternalStream(engine.stream())
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    start.record(stream)
+    events = engine.train(train_request(net, [interior, boundary], epochs, log_every))
+    stop.record(stream)
+    torch.cuda.synchronize()
+    ms = _max_over_ranks(dist, start.elapsed_time(stop) / epochs)
+    curve = []
+    for kind, payload in events:
+        if kind == 2:
+            r = Reader(payload)
+            epoch, _, after, values = r.get('Q'), r.get('Q'), r.get('i'), r.array('f8')
+            curve.append([int(epoch), float(values.sum())])
+    for kind, h in ((2, interior), (2, boundary), (0, data), (0, bdata), (1, net)):
+        engine.release(kind, h)
+    world = dist.get_world_size() if dist is not None else 1
+    out = dict(workload='config 3: 500 RPROP epochs (op 8) of the interior (262,144 disk points, '
+                        '(u_xx+u_yy+1)^2) and boundary (4,096 circle points, u^2) integrals, 2->64^3->1 sigmoid',
+               scaling='strong', n_gpus=world, epochs=epochs, ms_per_epoch=ms,
+               points_derivs_per_s=(len(qw) * len(t) + len(qb) * len(tb)) / (ms / 1e3), objective_curve=curve,
+               timer='CUDA events on the engine stream around the whole op-8 run, max over ranks')
+    exe = ROOT / 'oracle' / '_ref' / 'cpde_ref_cuda_server'
+    if reference_device is not None and exe.exists():
+        from cpde_b200.client import Data, Network, Session
         env = dict(os.environ)
         env.pop('NVIDIA_TF32_OVERRIDE', None)
-        with Session(exe, device=device, env=env) as s:
-            rnet = Network(s, layers, weights=weights)
-            rd = Data(s, x, t)
-            rc = rnet.integral(rd, expr, weights=qw)
-            _, rdev, rloss, _ = rnet.benchmark(rc, warm=3, iterations=iterations, batches=batches)
-        out.update(reference_cuda_ms=float(np.median(rdev)), reference_loss=rloss,
-                   speedup_vs_reference_cuda=float(np.median(rdev)) / out['ms'])
+        try:
+            with Session(exe, device=reference_device, env=env) as s:
+                rnet = Network(s, layers, weights=weights)
+                rc = [rnet.integral(Data(s, x, t), expr, weights=qw), rnet.integral(Data(s, xb, tb), eb, weights=qb)]
+                rnet.train(rc, 3, optimizer='rprop', reset=True, log_every=0)
+                rnet.set_weights(weights)
+                t0 = time.perf_counter()
+                result = rnet.train(rc, epochs, optimizer='rprop', reset=True, log_every=log_every)
+                wall = (time.perf_counter() - t0) * 1e3 / epochs
+            rcurve = [[int(ev['epoch']), float(np.sum(ev['values']))] for ev in result['events'] if ev['kind'] == 2]
+            out.update(reference_cuda_ms_per_epoch=wall, reference_objective_curve=rcurve,
+                       speedup_vs_reference_cuda=wall / ms,
+                       reference_how='oracle/_ref/cpde_ref_cuda_server, op 8 through the wire protocol, host wall '
+                                     'clock of the whole run (it synchronises every epoch)')
+        except Exception as exc:
+            out['reference_error'] = f'{type(exc).__name__}: {exc}'
     return out
+
+
+def orders_sweep(engine, dist, points_per_gpu, steps=5, warmup=2, reference_device=None):
+    """ms per fixed-weight epoch of the config-2 network (2 -> 128^4 -> 1
+    sigmoid, matching against sin(2 pi x) e^-y) at orders 0..6, with
+    `points_per_gpu` points per rank (weak scaling), device time, max over
+    ranks; with `reference_device`, op-90 epochs of the reference CUDA
+    server on the same workload and GPU."""
+    import torch
+    world = dist.get_world_size() if dist is not None else 1
+    stream = torch.cuda.ExternalStream(engine.stream())
+    rows = []
+    for order in range(7):
+        t, x, targets, weights = workload(points_per_gpu * world, order=order)
+        R = len(t)
+        net = engine.network(LAYERS, weights)
+        data, tgt = engine.data(x, t), engine.data(targets, t)
+        cost = engine.matching(net, data, tgt, list(range(R)), list(range(R)), 1, np.ones((R, 1, 1), np.float32))
+        for _ in range(warmup):
+            engine.epoch(net, [cost])
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        start.record(stream)
+        for _ in range(steps):
+            engine.epoch(net, [cost])
+        stop.record(stream)
+        torch.cuda.synchronize()
+        ms = _max_over_ranks(dist, start.elapsed_time(stop) / steps)
+        entry = dict(order=order, rows=R, points=points_per_gpu * world, ms=ms,
+                     points_derivs_per_s=points_per_gpu * world * R / (ms / 1e3))
+        for kind, h in ((2, cost), (0, tgt), (0, data), (1, net)):
+            engine.release(kind, h)
+        exe = ROOT / 'oracle' / '_ref' / 'cpde_ref_cuda_server'
+        if reference_device is not None and exe.exists():
+            from cpde_b200.client import Data, Network, Session
+            env = dict(os.environ)
+            env.pop('NVIDIA_TF32_OVERRIDE', None)
+            with Session(exe, device=reference_device, env=env) as s:
+                rnet = Network(s, LAYERS, weights=weights)
+                rc = rnet.matching(Data(s, x, t), Data(s, targets, t), np.ones((1, R), np.float32))
+                _, rdev, _, _ = rnet.benchmark(rc, warm=1, iterations=2, batches=1)
+            entry.update(reference_cuda_ms=float(np.median(rdev)), speedup_vs_reference_cuda=float(np.median(rdev)) / ms)
+        rows.append(entry)
+    return dict(workload=f'2->128^4->1 sigmoid, all mixed derivatives through the order, {points_per_gpu} points '
+                         'per GPU (weak scaling), fixed-weight epochs, device time, max over ranks',
+                orders=rows)
 
 
 PUBLISHED_RTX3090_MS = [0.41, 0.68, 1.10, 1.72, 2.40, 3.59, 5.65]  # docs/benchmarks/fourier-rtx3090.md:23-29
@@ -408,6 +743,14 @@ def run_b200(args):
         dist.all_reduce(m, op=dist.ReduceOp.MAX)
         e2e_ms = float(m.item())
 
+    for h, kind in ((cost, 2), (tgt, 0), (inp, 0), (net, 1)):
+        engine.release(kind, h)
+    legs = {}
+    if not args.no_scaling_legs:
+        ref_dev = local if world == 1 and not args.no_reference_cuda else None
+        legs['orders_weak'] = orders_sweep(engine, dist, args.points, reference_device=ref_dev)
+        legs['config3_training'] = config3_training(engine, dist, reference_device=ref_dev)
+
     fwd, dgrad, wgrad = gemm_flops(args.points, R)
     peaks, source = measured_peaks()
     launches = sum(v[0] for v in kernels.values()) // args.steps
@@ -427,17 +770,29 @@ def run_b200(args):
                     gpu_launches=int(launches), roofline=roofline, kernel_rooflines=kernel_rooflines, clocks=clock,
                     kernels={k: dict(launches=v[0] // args.steps, ms_per_step=v[1] / args.steps)
                              for k, v in sorted(kernels.items())},
-                    gemm_gflop_per_step=(fwd + dgrad + wgrad) / 1e9, loss=loss)
+                    gemm_gflop_per_step=(fwd + dgrad + wgrad) / 1e9, loss=loss, **legs)
         if world == 1 and not args.no_cpu_baseline:
             line['cpu_baseline'] = cpu_baseline()
         if world == 1 and not args.no_reference_cuda:
             line['published_workload'] = published_workload(local, engine)
-            line['config3_integral'] = config3_integral(local, engine)
             engine.close()
-            ref = reference_cuda(local, args.points)
-            if ref is not None:
-                ref['speedup_of_value'] = value / ref['value']
-                line['reference_cuda_same_gpu'] = ref
+            ref = same_gpu_comparison(local, config2_workload(args.points), warm=1, iterations=3, batches=3)
+            if 'reference_cuda_ms' in ref:
+                ref['speedup_of_value'] = ref['reference_cuda_ms'] / ms
+            line['reference_cuda_same_gpu'] = ref
+            line['parity'] = ref.get('parity')
+            line['config3_integral'] = same_gpu_comparison(local, config3_workload(), warm=3, iterations=10,
+                                                           batches=3, kernels=True)
+            if not args.no_large_configs:
+                peaks, source = measured_peaks()
+                for key, make, ref_points in (('config4', config4_workload, 262144),
+                                              ('config5', config5_workload, 262144)):
+                    w = make()
+                    entry = same_gpu_comparison(local, w, warm=1, iterations=1, batches=1,
+                                                reference_points=ref_points, kernels=True)
+                    entry['tensor_roofline'] = tensor_roofline(w, entry['ms'], peaks, source)
+                    line[key] = entry
+                    del w
         print(json.dumps(line))
     engine.close()
     if dist is not None:
@@ -455,6 +810,9 @@ def main():
     p.add_argument('--no-cpu-baseline', action='store_true')
     p.add_argument('--no-reference-cuda', action='store_true')
     p.add_argument('--tier', type=int, default=0, help='0 automatic, 1 generic, 2 tensor cores')
+    p.add_argument('--no-large-configs', action='store_true', help='skip the config-4 and config-5 legs')
+    p.add_argument('--no-scaling-legs', action='store_true',
+                   help='skip the order sweep and the config-3 training run (both run at every N)')
     args = p.parse_args()
     if args.impl == 'reference':
         run_reference(args)

@@ -36,9 +36,22 @@ def pure(variables, order):
     return sorted(rows, key=lambda c: (sum(c), c))
 
 
+def closure_of(tops):
+    """Every sub-multi-index of the given rows (the closure a cost requesting
+    exactly those derivatives propagates), in canonical order."""
+    rows = set()
+    for top in tops:
+        rows.update(itertools.product(*(range(x + 1) for x in top)))
+    return sorted(rows, key=lambda c: (sum(c), c))
+
+
 # (name, rows) of every static schema; ids are positions in this list.
 SCHEMAS = [(f'full{v}d_o{k}', full(v, k)) for v, k in [(2, 0), (2, 1), (2, 2), (2, 3), (2, 4), (2, 5), (2, 6)]]
 SCHEMAS += [('pure2d_o2', pure(2, 2)), ('full3d_o4', full(3, 4)), ('pure4d_o6', pure(4, 6))]
+# the rows a 3D biharmonic residual (u_xxxx + u_yyyy + u_zzzz + 2 u_xxyy +
+# 2 u_xxzz + 2 u_yyzz) propagates, and the 3D Laplacian's
+SCHEMAS += [('bih3d_o4', closure_of([(4, 0, 0), (0, 4, 0), (0, 0, 4), (2, 2, 0), (2, 0, 2), (0, 2, 2)])),
+            ('pure3d_o2', pure(3, 2))]
 
 
 def subs(s):

@@ -89,7 +89,11 @@ void Engine::join(int r, int n, const void* unique_id) {
 Engine::~Engine() {
     cudaSetDevice(device);
     if (stream) cudaStreamSynchronize(stream);
+    if (comm_stream) cudaStreamSynchronize(comm_stream);
     if (comm) Nccl::get().comm_destroy(comm);
+    for (auto e : layer_events) cudaEventDestroy(e);
+    if (comm_done) cudaEventDestroy(comm_done);
+    if (comm_stream) cudaStreamDestroy(comm_stream);
     costs.clear();
     nets.clear();
     data.clear();
@@ -209,23 +213,64 @@ void Engine::reduce_costs(NetRecord& n, const std::vector<uint64_t>& ids) {
                                         n.cost_totals.ptr, count, shard_values.ptr, shard_keys.ptr));
 }
 
-// Sums the weight gradients over the group: one all-reduce over the flat
-// gradient when every layer's active bank is the same buffer.
+// Marks layer `layer`'s gradient as complete so far in this epoch (the
+// backward calls it after the last write of each chunk into that layer); the
+// latest mark before reduce_gradient is the one its reduction waits for.
+static void ensure_events(std::vector<cudaEvent_t>& events, std::vector<char>& marked, size_t count) {
+    const size_t old = events.size();
+    if (count <= old) return;
+    events.resize(count);
+    marked.resize(count, 0);
+    for (size_t i = old; i < count; ++i) CPDE_CUDA(cudaEventCreateWithFlags(&events[i], cudaEventDisableTiming));
+}
+
+void Engine::layer_done(int layer) {
+    if (world == 1) return;
+    ensure_events(layer_events, layer_marked, size_t(layer) + 2);  // the last slot is the "now" event
+    CPDE_CUDA(cudaEventRecord(layer_events[layer], stream));
+    layer_marked[layer] = 1;
+}
+
+// Sums the weight gradients over the group: one all-reduce per layer, from
+// the output layer down, on the communication stream; a layer's reduction
+// waits for its completion mark of this epoch (or, unmarked, for everything
+// enqueued so far), and the compute stream waits for all of them.
 void Engine::reduce_gradient(NetRecord& n, float* target) {
     if (world == 1) return;
     auto& nccl = Nccl::get();
-    bool uniform = true;
-    for (int l = 1; l < n.layers; ++l) uniform = uniform && n.active[l] == n.active[0];
-    if (target || uniform) {
-        float* g = n.gradient_base(0, target);
-        nccl.check(nccl.all_reduce(g, g, size_t(n.params), ncclFloat, ncclSum, comm, stream), "ncclAllReduce");
-        return;
+    if (!comm_stream) {
+        CPDE_CUDA(cudaStreamCreateWithFlags(&comm_stream, cudaStreamNonBlocking));
+        CPDE_CUDA(cudaEventCreateWithFlags(&comm_done, cudaEventDisableTiming));
     }
-    nccl.check(nccl.group_start(), "ncclGroupStart");
-    for (int l = 0; l < n.layers; ++l)
-        nccl.check(nccl.all_reduce(n.gradient(l), n.gradient(l), size_t(n.count[l]), ncclFloat, ncclSum, comm, stream),
-                   "ncclAllReduce");
-    nccl.check(nccl.group_end(), "ncclGroupEnd");
+    ensure_events(layer_events, layer_marked, size_t(n.layers) + 1);
+    cudaEvent_t now = nullptr;
+    KernelTimer* t = timer.get();
+    cudaEvent_t t0 = nullptr, t1 = nullptr;
+    for (int l = n.layers - 1; l >= 0; --l) {
+        cudaEvent_t ready = layer_marked[l] ? layer_events[l] : nullptr;
+        if (!ready) {
+            if (!now) {
+                now = layer_events.back();  // one past every layer index that marks use
+                CPDE_CUDA(cudaEventRecord(now, stream));
+            }
+            ready = now;
+        }
+        CPDE_CUDA(cudaStreamWaitEvent(comm_stream, ready, 0));
+        if (t && !t0) {
+            t0 = t->get();
+            CPDE_CUDA(cudaEventRecord(t0, comm_stream));
+        }
+        float* g = n.gradient_base(l, target);
+        nccl.check(nccl.all_reduce(g, g, size_t(n.count[l]), ncclFloat, ncclSum, comm, comm_stream), "ncclAllReduce");
+    }
+    std::fill(layer_marked.begin(), layer_marked.end(), 0);
+    if (t) {
+        t1 = t->get();
+        CPDE_CUDA(cudaEventRecord(t1, comm_stream));
+        t->marks.push_back({"allreduce_gradient", t0, t1});
+    }
+    CPDE_CUDA(cudaEventRecord(comm_done, comm_stream));
+    CPDE_CUDA(cudaStreamWaitEvent(stream, comm_done, 0));
 }
 
 // ---------------------------------------------------------------------------
@@ -338,13 +383,16 @@ static bool nonlinear_net(const NetRecord& n) {
 
 void Engine::ensure_arena(NetRecord& n, long columns, bool backward) {
     const int widest = *std::max_element(n.neurons.begin(), n.neurons.end());
+    // an evaluation that grows the arena in the middle of training (the
+    // outputs a training run prints) must leave the backward storage in place
+    backward = backward || n.dz[0].ptr;
     if (columns > n.capacity) {
         CPDE_CUDA(cudaStreamSynchronize(stream));
         for (int l = 0; l <= n.layers; ++l) {
             n.act[l].resize(size_t(n.neurons[l]) * columns);
-            if (n.linear[l] != 1) n.pre[l].resize(size_t(n.neurons[l]) * columns);
+            n.pre[l].release();
         }
-        n.jet_scratch.resize(size_t(widest) * columns);
+        n.jet_scratch.release();
         n.dz[0].release();
         n.dz[1].release();
         n.dy.release();
@@ -354,8 +402,18 @@ void Engine::ensure_arena(NetRecord& n, long columns, bool backward) {
     if (backward && n.dz[0].count < size_t(widest) * n.capacity) {
         n.dz[0].resize(size_t(widest) * n.capacity);
         n.dz[1].resize(size_t(widest) * n.capacity);
-        n.dy.resize(size_t(widest) * n.capacity);
     }
+}
+
+// Slabs only the generic tier uses (pre-activations, the jet scratch and the
+// backward's dE/dY), allocated on its first use so the fused tiers, which
+// keep Z and dE/dY on chip, leave that memory to larger chunks.
+static void ensure_generic_storage(NetRecord& n, bool backward) {
+    const int widest = *std::max_element(n.neurons.begin(), n.neurons.end());
+    for (int l = 0; l <= n.layers; ++l)
+        if (n.linear[l] != 1) n.pre[l].reserve(size_t(n.neurons[l]) * n.capacity);
+    n.jet_scratch.reserve(size_t(widest) * n.capacity);
+    if (backward) n.dy.reserve(size_t(widest) * n.capacity);
 }
 
 void Engine::ensure_reductions(NetRecord& n, int count) {
@@ -377,6 +435,7 @@ void Engine::ensure_reductions(NetRecord& n, int count) {
 }
 
 void Engine::begin_costs(NetRecord& n, int count) {
+    std::fill(layer_marked.begin(), layer_marked.end(), 0);  // completion marks belong to one epoch
     CPDE_RUN(*this, "clear_costs", k_clear_costs<<<1, 256, 0, stream>>>(n.cost_totals.ptr, count));
 }
 
@@ -413,6 +472,7 @@ static void launch_gemm(Engine& e, int M, int N, int K, const float* A, int lda,
 
 void Engine::forward(NetRecord& n, Context& ctx, int points) {
     if (fast_ok(n, ctx)) return fast_forward(n, ctx, points, false);
+    ensure_generic_storage(n, false);
     const int R = ctx.R();
     const int cols = points * R;
     for (int l = 1; l <= n.layers; ++l) {
@@ -437,6 +497,7 @@ void Engine::forward(NetRecord& n, Context& ctx, int points) {
 
 void Engine::backward(NetRecord& n, Context& ctx, int points, float* target) {
     if (fast_ok(n, ctx)) return fast_backward(n, ctx, points, target, false);
+    ensure_generic_storage(n, true);
     const int R = ctx.R();
     const long cols = long(points) * R;
     float* cur = n.dz[0].ptr;
@@ -456,6 +517,7 @@ void Engine::backward(NetRecord& n, Context& ctx, int points, float* target) {
         CPDE_RUN(*this, "splitk_reduce",
                  k_splitk_reduce<<<grid_for(long(M) * N), 256, 0, stream>>>(
                      n.partial.ptr, int(splits), M, N, n.gradient_base(l - 1, target), nl, 1));
+        layer_done(l - 1);
         if (l == 1) break;
         float* next = cur == n.dz[0].ptr ? n.dz[1].ptr : n.dz[0].ptr;
         const float* W = n.weights(l - 1);

@@ -152,6 +152,15 @@ class Engine {
     // totals are summed over the group with NCCL on this engine's stream.
     int rank = 0, world = 1;
     ncclComm_t comm = nullptr;
+    // The gradient all-reduce runs per layer on its own stream: each layer's
+    // reduction waits only for the event its backward recorded when that
+    // layer's gradient was complete, so the reductions of the upper layers
+    // overlap the backward of the lower ones.
+    cudaStream_t comm_stream = nullptr;
+    cudaEvent_t comm_done = nullptr;
+    std::vector<cudaEvent_t> layer_events;
+    std::vector<char> layer_marked;
+    void layer_done(int layer);
     void join(int rank, int world, const void* unique_id);
     Shard shard(long total) const { return shard_range(total, rank, world); }
     void reduce_costs(NetRecord& n, const std::vector<uint64_t>& ids);

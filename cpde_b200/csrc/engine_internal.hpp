@@ -82,8 +82,8 @@ inline int grid_for(long count, int threads = 256, int cap = 148 * 16) {
 // ---------------------------------------------------------------------------
 // fast tier dispatch
 
-static_assert(kStaticSchemas == 10, "update CPDE_STATIC_CASES after changing the generated schemas");
-#define CPDE_STATIC_CASES(X) X(0) X(1) X(2) X(3) X(4) X(5) X(6) X(7) X(8) X(9)
+static_assert(kStaticSchemas == 12, "update CPDE_STATIC_CASES after changing the generated schemas");
+#define CPDE_STATIC_CASES(X) X(0) X(1) X(2) X(3) X(4) X(5) X(6) X(7) X(8) X(9) X(10) X(11)
 
 template <class F>
 static void with_schema(int sid, F&& f) {
@@ -112,21 +112,6 @@ inline CUtensorMap tensor_map(const float* base, int inner, long rows, int box_r
     driver_check(driver_api().encode_tiled(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims,
                                            strides, box, element_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
                                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE),
-                 "cuTensorMapEncodeTiled");
-    return map;
-}
-
-// Unswizzled box of 128 neurons x 32 columns (raw slabs of the weight-gradient kernel).
-inline CUtensorMap raw_map(const float* base, int inner, long rows) {
-    CUtensorMap map;
-    cuuint64_t dims[2] = {cuuint64_t(inner), cuuint64_t(rows)};
-    cuuint64_t strides[1] = {cuuint64_t(inner) * sizeof(float)};
-    cuuint32_t box[2] = {cuuint32_t(tcg::BM), cuuint32_t(tcg::KS)};
-    cuuint32_t element_strides[2] = {1, 1};
-    driver_check(driver_api().encode_tiled(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims,
-                                           strides, box, element_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                                           CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE),
                  "cuTensorMapEncodeTiled");
     return map;

@@ -48,6 +48,7 @@ struct FastBackward {
             CPDE_RUN(e, "sum_partials", (k_sum_partials<<<fast::sum_grid(size), 256, 0, e.stream>>>(
                                             n.partial.ptr, bx, size, n.gradient_base(L - 1, target))));
         }
+        e.layer_done(L - 1);
         float* cur = n.dz[1].ptr;
         const bool tensor = use_tensor;
         if (tensor) {
@@ -56,7 +57,6 @@ struct FastBackward {
                 using TT = tcg::Tiling<R>;
                 allow_smem(tcg::k_backward_tc<SID, Act, false>, TT::SMEM);
                 allow_smem(tcg::k_backward_tc<SID, Act, true>, TT::SMEM);
-                allow_smem(tcg::k_weight_gradient_tc, tcg::kWgSmem);
                 tc_ready[e.device & 63] = true;
             }
             n.wb_hi.reserve(n.params);
@@ -75,25 +75,22 @@ struct FastBackward {
             splits = (cols + per - 1) / per;
             n.partial.reserve(size_t(splits) * M * (N + 1));
             dim3 wg(unsigned(splits), (N + BM - 1) / BM, (M + BM - 1) / BM);
-            if (tc_wgrad && M == tcg::BM) {
-                // warp-specialised: dZ through registers into tensor memory, Y_prev MN-major from TMA
+            if (tc_wgrad) {
+                // warp-specialised: dZ through registers into tensor memory, Y_prev MN-major from TMA;
+                // one CTA per SM over the (N/128) x (M/128) tiles
                 static bool wg_ready[64] = {};
                 if (!wg_ready[e.device & 63]) {
                     allow_smem(ws::k_wgrad_ws, ws::kWgSmem);
                     wg_ready[e.device & 63] = true;
                 }
-                const int ny = N / tcg::BM;
-                splits = std::max(1L, std::min<long>(148 / ny, (cols + 31) / 32));
+                const int ny = N / tcg::BM, nz = M / tcg::BM;
+                splits = std::max(1L, std::min<long>(std::max(1, 148 / (ny * nz)), (cols + 31) / 32));
                 n.partial.reserve(size_t(splits) * M * (N + 1));
                 const CUtensorMap md = mn32_map(cur, M, cols), ma = mn32_map(n.act[l - 1].ptr, N, cols);
                 CPDE_RUN(e, "weight_gradient_ws",
-                         (ws::k_wgrad_ws<<<dim3(unsigned(splits), unsigned(ny)), ws::kWgThreads, ws::kWgSmem,
-                                           e.stream>>>(md, ma, N, cols, R, n.partial.ptr, e.tc_error.ptr)));
-            } else if (tc_wgrad) {
-                const CUtensorMap md = raw_map(cur, M, cols), ma = raw_map(n.act[l - 1].ptr, N, cols);
-                CPDE_RUN(e, "weight_gradient_tc",
-                         (tcg::k_weight_gradient_tc<<<wg, tcg::THREADS, tcg::kWgSmem, e.stream>>>(
-                             md, ma, M, N, cols, R, per, n.partial.ptr, e.tc_error.ptr)));
+                         (ws::k_wgrad_ws<<<dim3(unsigned(splits), unsigned(ny), unsigned(nz)), ws::kWgThreads,
+                                           ws::kWgSmem, e.stream>>>(md, ma, M, N, cols, R, n.partial.ptr,
+                                                                    e.tc_error.ptr)));
             } else if (M <= 64 && N <= 64) {
                 // 64 x 64 tiles of 64 threads, about eight CTAs per SM
                 splits = std::max(1L, std::min<long>(148L * 8, (cols + 63) / 64));
@@ -109,6 +106,7 @@ struct FastBackward {
             long size = long(M) * (N + 1);
             CPDE_RUN(e, "sum_partials", (k_sum_partials<<<fast::sum_grid(size), 256, 0, e.stream>>>(
                                             n.partial.ptr, int(splits), size, n.gradient_base(l - 1, target))));
+            e.layer_done(l - 1);
             // adjoint into layer l-1
             const float* W = n.weights(l - 1);
             const long tiles_p = (P + T::PTS - 1) / T::PTS;

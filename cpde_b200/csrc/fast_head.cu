@@ -35,6 +35,7 @@ struct FastHead {
         const long size = long(O) * (K + 1);
         CPDE_RUN(e, "sum_partials", (fast::k_sum_partials<<<fast::sum_grid(size), 256, 0, e.stream>>>(
                                         n.partial.ptr, grid, size, n.gradient_base(L - 1, target))));
+        e.layer_done(L - 1);
     }
     template <int SID, class Act, int O>
     void by_width() {
@@ -97,6 +98,7 @@ struct PointEpoch {
                                        net, P, per, head)));
         CPDE_RUN(e, "sum_partials", (fast::k_sum_partials<<<fast::sum_grid(n.params), 256, 0, e.stream>>>(
                                         n.partial.ptr, grid, n.params, n.gradient_base(0, target))));
+        for (int l = 0; l < n.layers; ++l) e.layer_done(l);
     }
     template <int SID, class Act, int O>
     void by_width() {

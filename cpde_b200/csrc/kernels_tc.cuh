@@ -264,164 +264,6 @@ __global__ void __launch_bounds__(THREADS) k_backward_tc(const __grid_constant__
     teardown<T::TMEM>(tmem);
 }
 
-// Weight gradient on tensor cores: G (M x N, plus the bias column) = sum over
-// a CTA's column range of dZ[:, c] A[:, c]^T. Both operands are stored with
-// the neuron index contiguous per column, i.e. MN-major for this product; the
-// slabs land by TMA unswizzled ([column][neuron]) and the split pass writes
-// them transposed into the K-major 128-byte-swizzled layout (thread = neuron
-// row, 16-byte chunk q of the row at chunk position q ^ (row % 8)), so the
-// MMAs use the same K-major descriptors as the other kernels. The 128 x 128
-// accumulator stays in tensor memory across the whole column range.
-// grid = (splits, ceil(N/128), ceil(M/128)); M, N multiples of 4.
-struct WgShared {
-    float *raw_a, *raw_b, *a_hi, *a_lo, *b_hi, *b_lo;
-    uint64_t *tma_bar, *mma_bar;
-    uint32_t* tmem_slot;
-};
-
-__device__ __forceinline__ WgShared wg_carve(uint8_t* raw) {
-    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
-    WgShared s;
-    s.raw_a = reinterpret_cast<float*>(base);           // [32 cols][128]
-    s.raw_b = reinterpret_cast<float*>(base + 16384);   // [32 cols][128]
-    s.a_hi = reinterpret_cast<float*>(base + 32768);    // K-major swizzled [128 rows][32]
-    s.a_lo = reinterpret_cast<float*>(base + 49152);
-    s.b_hi = reinterpret_cast<float*>(base + 65536);
-    s.b_lo = reinterpret_cast<float*>(base + 81920);
-    s.tma_bar = reinterpret_cast<uint64_t*>(base + 98304);
-    s.mma_bar = s.tma_bar + 1;
-    s.tmem_slot = reinterpret_cast<uint32_t*>(s.tma_bar + 2);
-    return s;
-}
-constexpr int kWgSmem = 98304 + 64 + 1024;
-
-// Transposes one raw [32][128] slab row-per-thread into K-major swizzled hi/lo.
-__device__ __forceinline__ void split_transpose(const float* raw, float* hi, float* lo) {
-    const int row = threadIdx.x;  // 0..127
-    float4* h4 = reinterpret_cast<float4*>(hi + row * 32);
-    float4* l4 = reinterpret_cast<float4*>(lo + row * 32);
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-        float v[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) v[i] = raw[(4 * q + i) * 128 + row];
-        float4 h, l;
-        h.x = tc::tf32_round(v[0]);
-        h.y = tc::tf32_round(v[1]);
-        h.z = tc::tf32_round(v[2]);
-        h.w = tc::tf32_round(v[3]);
-        l.x = tc::tf32_round(v[0] - h.x);
-        l.y = tc::tf32_round(v[1] - h.y);
-        l.z = tc::tf32_round(v[2] - h.z);
-        l.w = tc::tf32_round(v[3] - h.w);
-        const int slot = q ^ (row & 7);
-        h4[slot] = h;
-        l4[slot] = l;
-    }
-}
-
-static __global__ void __launch_bounds__(THREADS) k_weight_gradient_tc(const __grid_constant__ CUtensorMap map_dz,
-                                                                const __grid_constant__ CUtensorMap map_a, int M,
-                                                                int N, long columns, int R, long per_split,
-                                                                float* __restrict__ partials, int* error) {
-    extern __shared__ uint8_t smem_raw[];
-    WgShared s = wg_carve(smem_raw);
-    const int n_base = blockIdx.y * BM, m_base = blockIdx.z * BM;
-    if (threadIdx.x == 0) {
-        tc::mbar_init(s.tma_bar, 1);
-        tc::mbar_init(s.mma_bar, 1);
-        tc::fence_barrier_init();
-    }
-    if (threadIdx.x < 32) {
-        tc::tmem_alloc(s.tmem_slot, 128);
-        tc::tmem_relinquish();
-    }
-    tc::tc_fence_before();
-    __syncthreads();
-    tc::tc_fence_after();
-    const uint32_t tmem = *s.tmem_slot;
-    constexpr uint32_t idesc = tc::idesc_tf32(BM, BM);
-    const long c_begin = (long)blockIdx.x * per_split;
-    const long c_end = min(columns, c_begin + per_split);
-    float bias_acc = 0.f;
-    uint32_t phase = 0;
-    bool ok = true, any = false;
-    for (long c0 = c_begin; c0 < c_end; c0 += KS) {
-        if (threadIdx.x == 0) {
-            tc::mbar_expect_tx(s.tma_bar, 2 * 16384);
-            tc::tma_load_2d(s.raw_a, &map_dz, s.tma_bar, m_base, int(c0));
-            tc::tma_load_2d(s.raw_b, &map_a, s.tma_bar, n_base, int(c0));
-        }
-        ok = __syncthreads_and(tc::mbar_wait(s.tma_bar, phase, kWaitCycles));
-        if (!ok) {
-            if (threadIdx.x == 0) atomicExch(error, kErrTma);
-            break;
-        }
-        // columns past this CTA's range (or past the data) must not contribute
-        const int valid = int(min((long)KS, c_end - c0));
-        if (valid < KS)
-            for (int i = threadIdx.x; i < (KS - valid) * 128; i += THREADS) {
-                s.raw_a[valid * 128 + i] = 0.f;
-                s.raw_b[valid * 128 + i] = 0.f;
-            }
-        __syncthreads();
-        if (blockIdx.y == 0) {
-            const long first = ((c0 + R - 1) / R) * R;
-            for (long c = first; c < c0 + valid; c += R) bias_acc += s.raw_a[(c - c0) * 128 + threadIdx.x];
-        }
-        split_transpose(s.raw_a, s.a_hi, s.a_lo);
-        split_transpose(s.raw_b, s.b_hi, s.b_lo);
-        tc::fence_proxy_async();
-        __syncthreads();
-        tc::tc_fence_after();
-        if (threadIdx.x == 0) {
-            const uint32_t ah = tc::smem_u32(s.a_hi), al = tc::smem_u32(s.a_lo);
-            const uint32_t bh = tc::smem_u32(s.b_hi), bl = tc::smem_u32(s.b_lo);
-#pragma unroll
-            for (int kk = 0; kk < KS / 8; ++kk) {
-                const uint32_t off = kk * 32;
-                tc::mma_tf32(tmem, tc::desc_k_sw128(al + off), tc::desc_k_sw128(bh + off), idesc,
-                             (any || kk) ? 1u : 0u);
-                tc::mma_tf32(tmem, tc::desc_k_sw128(ah + off), tc::desc_k_sw128(bl + off), idesc, 1);
-                tc::mma_tf32(tmem, tc::desc_k_sw128(ah + off), tc::desc_k_sw128(bh + off), idesc, 1);
-            }
-            tc::mma_commit(s.mma_bar);
-        }
-        any = true;
-        ok = __syncthreads_and(tc::mbar_wait(s.mma_bar, phase, kWaitCycles));
-        phase ^= 1;
-        if (!ok) {
-            if (threadIdx.x == 0) atomicExch(error, kErrMma);
-            break;
-        }
-    }
-    float* out = partials + (size_t)blockIdx.x * M * (N + 1);
-    const int m = m_base + threadIdx.x;
-    if (ok) {
-        tc::tc_fence_after();
-        const uint32_t lane_addr = tmem + (uint32_t((threadIdx.x >> 5) * 32) << 16);
-#pragma unroll 1
-        for (int c = 0; c < BM; c += 16) {
-            float v[16];
-            if (any) tc::tmem_read<16>(lane_addr + c, v);
-            else
-#pragma unroll
-                for (int i = 0; i < 16; ++i) v[i] = 0.f;
-            if (m < M)
-#pragma unroll
-                for (int i = 0; i < 16; ++i)
-                    if (n_base + c + i < N) out[m + (size_t)(n_base + c + i) * M] = v[i];
-        }
-        if (blockIdx.y == 0 && m < M) out[m + (size_t)N * M] = bias_acc;
-    }
-    tc::tc_fence_before();
-    __syncthreads();
-    if (threadIdx.x < 32) {
-        tc::tc_fence_after();
-        tc::tmem_dealloc(tmem, 128);
-    }
-}
-
 // hi/lo TF32 split of a weight matrix. transpose: dst[m*K + k] = src[m + k*M]
 // (column-major M x K to K-major rows); otherwise elementwise.
 static __global__ void k_split_tf32(const float* __restrict__ src, float* __restrict__ hi, float* __restrict__ lo, int M,

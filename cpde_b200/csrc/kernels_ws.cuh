@@ -418,9 +418,9 @@ __global__ void __launch_bounds__(THREADS, 1) k_backward_ws(const __grid_constan
 }
 
 // ---------------------------------------------------------------------------
-// Weight gradient of a hidden layer of 128 neurons: G (128 x a 128-neuron
-// slice of the previous layer, plus the bias column) = sum over this CTA's
-// columns of dZ[:, c] Y_prev[:, c]^T. Per 32-column stage, TMA brings 4
+// Weight gradient of a hidden layer: G (a 128-neuron slice of this layer x a
+// 128-neuron slice of the previous layer, plus the bias column) = sum over
+// this CTA's columns of dZ[:, c] Y_prev[:, c]^T. Per 32-column stage, TMA brings 4
 // boxes of 32 neurons x 32 columns of each operand (128-byte swizzle with
 // 32-byte atoms, the layout of MN-major TF32 operands). The split warps move
 // dZ through registers into tensor memory as the K-major A operand (thread =
@@ -430,7 +430,9 @@ __global__ void __launch_bounds__(THREADS, 1) k_backward_ws(const __grid_constan
 // carries each operand once per MMA term instead of also serving the A side.
 // Two MMA issuers take the even and the odd stages, each into its own
 // 128 x 128 accumulator, which stay in tensor memory for the whole kernel and
-// are summed in the epilogue. grid = (CTAs, N / 128).
+// are summed in the epilogue. grid = (CTAs, N / 128, M / 128): CTAs that share
+// blockIdx.x take the same chunks at about the same time, so the slices of
+// dZ and Y_prev that several of them read come from L2.
 
 constexpr int kWgStages = 4;
 constexpr int kWgBox = 32 * 32 * 4;       // 32 neurons x 32 columns
@@ -447,10 +449,9 @@ __device__ __forceinline__ int mn32_index(int mn, int k) {
 }
 
 static __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_constant__ CUtensorMap map_dz,
-                                                            const __grid_constant__ CUtensorMap map_y, int N,
+                                                            const __grid_constant__ CUtensorMap map_y, int M, int N,
                                                             long columns, int R, float* __restrict__ partials,
                                                             int* error) {
-    constexpr int M = 128;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(base + kWgStages * kWgStage);
@@ -476,7 +477,7 @@ static __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_
     __syncthreads();
     tc::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const int n_base = blockIdx.y * 128;
+    const int n_base = blockIdx.y * 128, m_base = blockIdx.z * 128;
     // 32-column chunks dealt round-robin over the CTAs, so the whole grid
     // streams through one region of both operands at a time
     const long total_chunks = (columns + 31) / 32;
@@ -496,7 +497,7 @@ static __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_
                 tc::mbar_expect_tx(full + st, 2 * kWgOperand);
                 const int c0 = int(chunk_start(it));
                 for (int j = 0; j < 4; ++j) {
-                    tc::tma_load_2d(stage_ptr(st, 0) + j * (kWgBox / 4), &map_dz, full + st, 32 * j, c0);
+                    tc::tma_load_2d(stage_ptr(st, 0) + j * (kWgBox / 4), &map_dz, full + st, m_base + 32 * j, c0);
                     tc::tma_load_2d(stage_ptr(st, 1) + j * (kWgBox / 4), &map_y, full + st, n_base + 32 * j, c0);
                 }
             }
@@ -561,7 +562,7 @@ static __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(split + st);
         }
-        if (blockIdx.y == 0) out[(size_t)N * M + m] = bias;
+        if (blockIdx.y == 0) out[(size_t)N * M + m_base + m] = bias;
     } else {
         // epilogue warps: the TF32 lo part of Y_prev of every stage (the raw
         // operand is its hi part; the columns past the end of the data arrive
@@ -589,7 +590,7 @@ static __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_
 #pragma unroll
                 for (int j = 0; j < 16; ++j) v[j] += odd[j];
 #pragma unroll
-                for (int j = 0; j < 16; ++j) out[m + (size_t)(n_base + c0 + j) * M] = v[j];
+                for (int j = 0; j < 16; ++j) out[m_base + m + (size_t)(n_base + c0 + j) * M] = v[j];
             }
         }
     }

@@ -1,21 +1,23 @@
 // Weight gradient of one layer for callers that cannot allocate device memory.
 //
-// Some callers of this library cannot call cudaMalloc: code that enqueues work
-// while a stream is being captured into a CUDA graph (allocation is not a
-// capturable operation), and hosts whose framework allocator already owns the
-// device's memory (a preallocating pool leaves nothing for a second
-// allocator, and a failed cudaMalloc in the middle of a step is not
-// recoverable for them). cpde_layer_gradient_static() serves them: it runs the
-// split-column weight-gradient kernel with its per-split partial sums in a
-// file-scope static device array instead of engine-allocated scratch, and
-// touches no allocator at all. The caller passes device inputs and the output.
+// Some callers of this library cannot call cudaMalloc: hosts whose own
+// allocator already owns the device's memory (a framework's preallocated
+// pool leaves nothing for a second allocator, and an allocation that fails in
+// the middle of their step is not recoverable for them), and code on a
+// latency-bound path that must not take the implicit device synchronisation
+// of cudaMalloc and cudaFree. cpde_layer_gradient_static() serves them: it
+// runs the split-column weight-gradient kernel with its per-split partial
+// sums in a file-scope static device array instead of engine-allocated
+// scratch, and touches no allocator at all. The caller passes device inputs
+// and the output.
 //
 // The array holds kStaticScratchFloats floats (16 MiB); every GPU that loads
 // this library keeps it until the process exits. All calls on a device share
 // it and it keeps the last call's partials: every partial a call reads is
-// written by that call first, so nothing needs clearing, but two calls whose
-// kernels overlap on the GPU (different streams, no ordering between them)
-// race on the array and may corrupt each other's results.
+// written by that call first, so nothing needs clearing (the gradient output,
+// which the partial sum accumulates into, is cleared by each call), but two
+// calls whose kernels overlap on the GPU (different streams, no ordering
+// between them) race on the array and may corrupt each other's results.
 #include <mutex>
 
 namespace cpde {
@@ -24,7 +26,10 @@ constexpr size_t kStaticScratchFloats = size_t(4) << 20;
 static __device__ __align__(256) float g_static_gradient_scratch[kStaticScratchFloats];
 
 // Device address of the array, looked up once per device with that device
-// current (the host-side symbol is not a device address).
+// current (the host-side symbol is not a device address) by the first call on
+// that device. The cached address belongs to the device's primary context: it
+// stays valid for the life of the process unless that context is destroyed
+// (cudaDeviceReset), after which this entry point must not be called.
 static float* g_static_scratch_address[64] = {};
 static std::mutex g_static_scratch_mutex;
 

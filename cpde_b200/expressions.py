@@ -223,6 +223,44 @@ def quadrature_inputs(points, t):
     return arrays
 
 
+def tanh_as_sigmoid(layers, linear, weights):
+    """Exact reparametrisation of a network with tanh layers as a sigmoid
+    network, through tanh(z) = 2 sigma(2z) - 1, so that a server without tanh
+    (the reference's, cuda/cpde_server.cu:457) computes the same outputs and
+    every derivative row of them.
+
+    Weight layer l maps layer l-1 to layer l; with c = 2 if layer l is tanh
+    (else 1) and t = "layer l-1 is tanh": W' = c * (2W if t else W) and
+    b' = c * (b - W 1 if t else b). Returns (linear', weights') with every
+    tanh flag (2) replaced by sigmoid (0)."""
+    out = []
+    for l, (width, height) in enumerate(zip(layers[:-1], layers[1:]), start=1):
+        flat = np.asarray(weights[l - 1], np.float64)
+        W = flat[:width * height].reshape(width, height).T  # column-major storage
+        b = flat[width * height:]
+        c = 2.0 if linear[l] == 2 else 1.0
+        if linear[l - 1] == 2:
+            W, b = 2.0 * W, b - W.sum(axis=1)
+        out.append(np.concatenate([(c * W).ravel(order='F'), c * b]).astype(np.float32))
+    return [0 if a == 2 else a for a in linear], out
+
+
+def sigmoid_gradients_to_tanh(layers, linear, gradients):
+    """Maps per-layer gradients of the tanh_as_sigmoid network back to the
+    tanh network's weights (the transpose of that linear map):
+    dE/dW = c * (2 G_W - G_b 1^T if t else G_W), dE/db = c * G_b."""
+    out = []
+    for l, (width, height) in enumerate(zip(layers[:-1], layers[1:]), start=1):
+        flat = np.asarray(gradients[l - 1], np.float64)
+        G = flat[:width * height].reshape(width, height).T
+        gb = flat[width * height:]
+        c = 2.0 if linear[l] == 2 else 1.0
+        if linear[l - 1] == 2:
+            G = 2.0 * G - gb[:, None]
+        out.append(np.concatenate([(c * G).ravel(order='F'), c * gb]))
+    return out
+
+
 def glorot_like(layers, seed=0):
     """Benchmark initialisation: per layer in order, N(0, 1/sqrt(fan_in)) weights
     stored column-major (Fortran ravel) followed by zero biases."""

@@ -155,19 +155,25 @@ int cpde_kernel_timing_report(cpde_engine* engine, cpde_sink report, void* conte
 int cpde_set_tier(cpde_engine* engine, int32_t tier);
 
 /* Weight gradient of one layer without any device allocation. No counterpart
- * in the reference: it serves callers that cannot call cudaMalloc (work issued
- * during CUDA-graph stream capture; hosts whose framework allocator owns the
- * device memory). Computes gradient = dZ [A; 1]^T, an outputs x (inputs+1)
+ * in the reference. It serves callers that cannot call cudaMalloc: hosts whose
+ * own allocator already owns the device memory (a framework's preallocated
+ * pool leaves no room for a second allocator, and an allocation that fails in
+ * the middle of their step cannot be recovered), and code on a latency-bound
+ * path that must not take cudaMalloc's or cudaFree's implicit device
+ * synchronisation. Computes gradient = dZ [A; 1]^T, an outputs x (inputs+1)
  * column-major matrix (weights, then the bias column = sum of dZ over the
  * value-row columns c with c % rows == 0), from device arrays in the
- * interleaved layout: column c = point*rows + row, `dz` outputs x (points*rows),
- * `activations` inputs x (points*rows), both 16-byte aligned, outputs and
- * inputs multiples of 4. Split partial sums live in a static 16 MiB device
- * array (4194304 floats, held by every GPU that loads the library until exit);
- * outputs*(inputs+1) beyond that is rejected. The first call on a device looks
- * up the array's device address, so make it before any stream capture. Calls
- * are asynchronous on `stream` (NULL: the engine's stream); calls that overlap
- * on the GPU race on the shared array. */
+ * interleaved layout: column c = point*rows + row, `dz` outputs x
+ * (points*rows), `activations` inputs x (points*rows), both 16-byte aligned,
+ * outputs and inputs multiples of 4. Split partial sums live in a static
+ * 16 MiB device array (4194304 floats, held by every GPU that loads the
+ * library until exit); outputs*(inputs+1) beyond that is rejected. The first
+ * call on a device looks up the array's device address once (with that device
+ * current) and keeps it for the life of the process, so make that first call
+ * before any stream capture, and do not call it again after resetting the
+ * device (cudaDeviceReset), which invalidates the address. Calls are
+ * asynchronous on `stream` (NULL: the engine's stream); calls that overlap on
+ * the GPU race on the shared array. */
 int cpde_layer_gradient_static(cpde_engine* engine, const float* dz, const float* activations, int32_t outputs,
                                int32_t inputs, int64_t points, int32_t rows, float* gradient, void* stream);
 
