@@ -320,7 +320,7 @@ def _row_errors(actual, expected):
 
 
 def same_gpu_comparison(device, w, warm=1, iterations=3, batches=1, reference_points=None, sample_points=4096,
-                        kernels=False):
+                        kernels=False, tier=0):
     """op-90 epochs (forward, cost, output adjoints, weight gradients) of one
     workload on this engine and on the reference CUDA server (built from the
     reference's sources for sm_100a by oracle/Makefile) on the same GPU, with
@@ -336,8 +336,9 @@ def same_gpu_comparison(device, w, warm=1, iterations=3, batches=1, reference_po
     R = len(w.t)
     sub = w.subset(reference_points or w.points)
     sample = w.subset(sample_points)
-    out = dict(workload=w.name, points=w.points, rows=R, layers=w.layers, chunk=w.chunk or w.points)
+    out = dict(workload=w.name, points=w.points, rows=R, layers=w.layers, chunk=w.chunk or w.points, tier=tier)
     with native.Engine(device) as e:
+        e.set_tier(tier)
         net, data, cost = w.own(e)
         _, dev, loss, grads = e.benchmark(net, cost, warm, iterations, batches, L)
         out.update(ms=float(np.median(dev)), loss=loss, points_derivs_per_s=w.points * R / (float(np.median(dev)) / 1e3))
@@ -813,11 +814,48 @@ def main():
     p.add_argument('--no-large-configs', action='store_true', help='skip the config-4 and config-5 legs')
     p.add_argument('--no-scaling-legs', action='store_true',
                    help='skip the order sweep and the config-3 training run (both run at every N)')
+    p.add_argument('--profile-workload', choices=sorted(WORKLOADS),
+                   help='only run --warmup + --steps plain epochs of one workload on GPU 0 (a short, '
+                        'self-contained command to profile) and print its ms per epoch')
     args = p.parse_args()
-    if args.impl == 'reference':
+    if args.profile_workload:
+        profile_workload(args)
+    elif args.impl == 'reference':
         run_reference(args)
     else:
         run_b200(args)
+
+
+WORKLOADS = {'config2': lambda points: config2_workload(points or POINTS),
+             'config3': lambda points: config3_workload(points or 262144),
+             'config4': lambda points: config4_workload(points or 1048576),
+             'config5': lambda points: config5_workload(points or 4194304)}
+
+
+def profile_workload(args):
+    """Plain fixed-weight epochs of one workload (the same engine calls as the
+    bench's timed loop) with device timing, nothing else: the command that
+    the kernel profiles under profiles/ are taken from. --points overrides
+    the workload's point count (its default otherwise)."""
+    import torch
+    from cpde_b200 import native
+    w = WORKLOADS[args.profile_workload](args.points if args.points != POINTS else 0)
+    with native.Engine(0) as e:
+        e.set_tier(args.tier)
+        net, data, cost = w.own(e)
+        for _ in range(args.warmup):
+            e.epoch(net, [cost])
+        stream = torch.cuda.ExternalStream(e.stream())
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        start.record(stream)
+        for _ in range(args.steps):
+            e.epoch(net, [cost])
+        stop.record(stream)
+        torch.cuda.synchronize()
+        loss, _ = e.epoch_result(net, sum(np.asarray(x).size for x in w.weights))
+    print(json.dumps(dict(workload=w.name, points=w.points, tier=args.tier, steps=args.steps,
+                          ms_per_epoch=start.elapsed_time(stop) / max(1, args.steps), loss=loss)))
 
 
 if __name__ == '__main__':

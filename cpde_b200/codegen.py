@@ -150,11 +150,29 @@ def generate():
     return '\n'.join(lines)
 
 
+SOURCE_OUT = OUT.with_name('jets_static_source.cuh')
+
+
+def generate_source_table():
+    """The same StaticJet code as C++ string literals, one per schema, for the
+    kernels the engine compiles at run time with NVRTC (the fused expression
+    head): the run-time source then carries exactly the jet code the
+    ahead-of-time kernels use."""
+    lines = ['// GENERATED by cpde_b200/codegen.py - do not edit.',
+             '// Source text of each StaticJet<SID> specialisation, for NVRTC-compiled kernels.', '#pragma once', '',
+             'namespace cpde {', '', 'static const char* const kStaticJetSource[] = {']
+    for sid, (name, rows) in enumerate(SCHEMAS):
+        body = '\n'.join(emit_schema(sid, name, rows))
+        lines.append(f'    R"JET({body})JET",')
+    lines += ['};', '', '}  // namespace cpde', '']
+    return '\n'.join(lines)
+
+
 def write():
     OUT.parent.mkdir(parents=True, exist_ok=True)
-    text = generate()
-    if not OUT.exists() or OUT.read_text() != text:
-        OUT.write_text(text)
+    for path, text in ((OUT, generate()), (SOURCE_OUT, generate_source_table())):
+        if not path.exists() or path.read_text() != text:
+            path.write_text(text)
     return OUT
 
 

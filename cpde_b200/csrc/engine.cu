@@ -626,6 +626,7 @@ void Engine::pass(NetRecord& n, CostRecord& c, int cost_index, bool bwd, bool co
     require(n.capacity >= long(c.width) * long(c.rows.size()) && n.dz[0].ptr && n.cost_totals.ptr,
             "internal error: network storage was not prepared for this cost");
     const bool fused = bwd && fused_head_ok(n, c, ctx);
+    const bool expr_head = bwd && !fused && c.has_components && expression_head_ok(n, c, ctx);
     for (int offset = begin; offset < end; offset += c.width) {
         int valid = std::min(c.width, input.w - offset);
         const bool tile_epoch = fused && !reuse_forward && c.has_components && point_epoch_ok(n, ctx, valid, target);
@@ -640,9 +641,15 @@ void Engine::pass(NetRecord& n, CostRecord& c, int cost_index, bool bwd, bool co
                 continue;
             }
             if (c.has_components) {
-                if (fused) fast_forward(n, ctx, valid, true);
+                if (fused || expr_head) fast_forward(n, ctx, valid, true);
                 else forward(n, ctx, valid);
             }
+        }
+        if (expr_head) {
+            CostReduce red{n.cost_partials.ptr, n.cost_ticket.ptr, n.cost_totals.ptr + cost_index};
+            expression_head(n, c, ctx, valid, offset, collect, multiplier, red, target);
+            fast_backward(n, ctx, valid, target, true);
+            continue;
         }
         if (fused) {
             CostReduce red{n.cost_partials.ptr, n.cost_ticket.ptr, n.cost_totals.ptr + cost_index};
@@ -746,6 +753,9 @@ uint64_t Engine::cost_matching(uint64_t ni, uint64_t in, uint64_t tgt, int chunk
     for (int r : tr) require(r >= 0 && r < t.d, "target derivative mismatch");
     for (float x : w) require(std::isfinite(x) && x >= 0, "invalid matching weight");
     if (ws > 1 && world > 1) {
+        // per-sample weights follow the samples into the shards; a rank whose
+        // shard is empty (more ranks than samples) keeps no weights and runs
+        // no chunk of this cost, so its weight_samples of 0 is never read
         w = shard_rows(w, rows.size(), ws, t.h, shard(ws));
         ws = d.w;
     }

@@ -62,6 +62,8 @@ struct CostRecord {
     DeviceBuffer<PolyTerm> terms;
     int term_count = 0;
     std::shared_ptr<ExpressionProgram> program;
+    std::shared_ptr<RuntimeKernel> head;  // fused expression head for the shape in head_key
+    std::string head_key;
     DeviceBuffer<double> fields, quadrature_weights;
     bool has_components = true, has_gradient = true;
 };
@@ -178,6 +180,7 @@ class Engine {
     std::unordered_map<uint64_t, std::unique_ptr<NetRecord>> nets;
     std::unordered_map<uint64_t, std::unique_ptr<CostRecord>> costs;
     std::unordered_map<std::string, std::shared_ptr<ExpressionProgram>> programs;
+    std::unordered_map<std::string, std::shared_ptr<RuntimeKernel>> heads;  // by source
     std::map<std::string, std::shared_ptr<Context>> contexts;
 
     // ops
@@ -226,6 +229,9 @@ class Engine {
     bool point_epoch_ok(NetRecord& n, Context& ctx, long points, float* target) const;
     void fused_head(NetRecord& n, CostRecord& c, Context& ctx, long points, int offset, bool collect,
                     const double* multiplier, CostReduce red, float* target);
+    bool expression_head_ok(NetRecord& n, CostRecord& c, Context& ctx) const;
+    void expression_head(NetRecord& n, CostRecord& c, Context& ctx, long points, int offset, bool collect,
+                         const double* multiplier, CostReduce red, float* target);
     void point_epoch(NetRecord& n, CostRecord& c, Context& ctx, long points, int offset, bool collect,
                      const double* multiplier, int cost_index, float* target);
     void fast_forward(NetRecord& n, Context& ctx, int points, bool hidden_only);

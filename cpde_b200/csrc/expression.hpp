@@ -13,6 +13,7 @@
 #include <cuda.h>
 #include <nvrtc.h>
 
+#include <algorithm>
 #include <iomanip>
 #include <map>
 #include <sstream>
@@ -65,20 +66,19 @@ __device__ inline void cs_finish(CostStats v, CostStats* partials, unsigned* tic
     *total = cs_combine(*total, acc); *ticket = 0; } }
 )PRELUDE";
 
-inline std::string expression_source(const std::vector<ScalarNode>& nodes) {
+// The per-sample program as a device function: the output components `yp`
+// (RO of them) of sample `sample` in, its loss added to `local` (times the
+// quadrature weight w), dE/dY (times w and the graph multiplier `scale`)
+// written to `gp`, and a bad entry recorded for a non-finite value or
+// adjoint.
+inline std::string expression_sample_function(const std::vector<ScalarNode>& nodes) {
     std::ostringstream s;
-    s << kExpressionPrelude;
-    s << "extern \"C\" __global__ void __launch_bounds__(256) cpde_integral(const float* __restrict__ y, "
-         "float* __restrict__ g, const double* __restrict__ fields, const double* __restrict__ weights, "
-         "int RO, int samples, int points, int offset, const double* __restrict__ multiplier, int collect, "
-         "int gradient, CostStats* partials, unsigned* ticket, CostStats* total) {\n";
-    s << "CostStats local = cs_empty();\n";
-    s << "for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < points; p += blockDim.x * gridDim.x) {\n";
-    s << "  const float* yp = y + (size_t)p * RO; float* gp = g + (size_t)p * RO;\n";
+    s << "__device__ __forceinline__ void cpde_sample(const float* __restrict__ yp, float* __restrict__ gp, int RO, "
+         "const double* __restrict__ fields, int samples, int sample, double w, double scale, int collect, "
+         "int gradient, CostStats& local) {\n";
     s << "  if (gradient) for (int i = 0; i < RO; ++i) gp[i] = 0.f;\n";
-    s << "  const double w = weights[offset + p]; if (w == 0) continue;\n";
-    s << "  const double scale = multiplier ? *multiplier : 1.0;\n";
-    s << "  if (gradient && scale == 0 && !collect) continue;\n";
+    s << "  if (w == 0) return;\n";
+    s << "  if (gradient && scale == 0 && !collect) return;\n";
     s << "  int bad = -2;\n";
     std::vector<bool> active;
     const int count = int(nodes.size());
@@ -88,7 +88,7 @@ inline std::string expression_source(const std::vector<ScalarNode>& nodes) {
         switch (n.op) {
             case kConstant: e = fmt_double(n.parameter); break;
             case kLeaf: e = "(double)yp[" + std::to_string(n.a) + "]"; break;
-            case kField: e = "fields[(size_t)" + std::to_string(n.a) + " * samples + offset + p]"; break;
+            case kField: e = "fields[(size_t)" + std::to_string(n.a) + " * samples + sample]"; break;
             case kAdd: e = a + " + " + b; break;
             case kSub: e = a + " - " + b; break;
             case kMul: e = a + " * " + b; break;
@@ -151,10 +151,158 @@ inline std::string expression_source(const std::vector<ScalarNode>& nodes) {
           << entry.first << "; }\n";
     }
     s << "  }\n";
-    s << "  if (bad != -2) { CostStats e; e.value = 0.0; e.bad_sample = offset + p; e.bad_component = bad; "
+    s << "  if (bad != -2) { CostStats e; e.value = 0.0; e.bad_sample = sample; e.bad_component = bad; "
          "local = cs_combine(local, e); }\n";
     s << "}\n";
-    s << "cs_finish(local, partials, ticket, total);\n}\n";
+    return s.str();
+}
+
+// The standalone cost kernel: one thread per sample over the engine's
+// interleaved output layout (point p's RO components at y + p RO), with the
+// block and grid reduction of the loss folded in.
+inline std::string expression_source(const std::vector<ScalarNode>& nodes) {
+    std::ostringstream s;
+    s << kExpressionPrelude << expression_sample_function(nodes);
+    s << "extern \"C\" __global__ void __launch_bounds__(256) cpde_integral(const float* __restrict__ y, "
+         "float* __restrict__ g, const double* __restrict__ fields, const double* __restrict__ weights, "
+         "int RO, int samples, int points, int offset, const double* __restrict__ multiplier, int collect, "
+         "int gradient, CostStats* partials, unsigned* ticket, CostStats* total) {\n"
+         "  CostStats local = cs_empty();\n"
+         "  const double scale = multiplier ? *multiplier : 1.0;\n"
+         "  for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < points; p += blockDim.x * gridDim.x)\n"
+         "    cpde_sample(y + (size_t)p * RO, g + (size_t)p * RO, RO, fields, samples, offset + p, "
+         "weights[offset + p], scale, collect, gradient, local);\n"
+         "  cs_finish(local, partials, ticket, total);\n"
+         "}\n";
+    return s.str();
+}
+
+// Activation structs of the NVRTC-compiled head: the same arithmetic as
+// Sigmoid and Tanh in kernels_generic.cuh (the jet adjoint uses only
+// slope_from_value and lead).
+static const char* kHeadActivations = R"ACT(
+struct Sigmoid {
+  __device__ static void value(float z, float& y, float& s) {
+    float e = __expf(-fabsf(z)); float big = 1.0f / (1.0f + e); float small = e * big;
+    y = z >= 0.f ? big : small; s = big * small; }
+  __device__ static float slope_from_value(float y) { return y * (1.0f - y); }
+  __device__ static float lead(float y) { return 1.0f - 2.0f * y; }
+};
+struct Tanh {
+  __device__ static void value(float z, float& y, float& s) { y = tanhf(z); s = (1.0f - y) * (1.0f + y); }
+  __device__ static float slope_from_value(float y) { return (1.0f - y) * (1.0f + y); }
+  __device__ static float lead(float y) { return -2.0f * y; }
+};
+template <int SID> struct StaticJet;
+)ACT";
+
+// The fused expression head (last hidden layer of K = NB neurons, K dividing
+// 128, O linear outputs): per point, the output jets Z = W_out Y + b from one
+// read of the layer's jets (warp butterflies, then a sum over the lane's
+// warps in shared memory), the per-sample program on them, dY = W_out^T
+// dE/dZ, the jet adjoint into dE/dZ of the last hidden layer, the output
+// layer's weight gradient (a partial per CTA) and the loss reduction. A CTA
+// of 128 threads has 128 / NB point lanes; each lane takes PB consecutive
+// points per round, whose programs PB threads of the lane evaluate at once,
+// so a round's two barriers serve LANES * PB points.
+static const char* kHeadKernel = R"HEAD(
+extern "C" __global__ void __launch_bounds__(128) cpde_head(
+    int K, int points, int offset, int samples, const float* __restrict__ W, const float* __restrict__ Y,
+    float* __restrict__ dZ, const double* __restrict__ fields, const double* __restrict__ weights,
+    const double* __restrict__ multiplier, int collect, float* __restrict__ partials,
+    CostStats* cost_partials, unsigned* ticket, CostStats* total) {
+  constexpr int R = HEAD_R, O = HEAD_O, NB = HEAD_NB, PB = HEAD_PB, LANES = 128 / NB, WPL = NB / 32, RO = R * O;
+  __shared__ float zsum[LANES][WPL][PB][RO];
+  __shared__ float comp[LANES][PB][RO];
+  __shared__ float gsh[LANES][PB][RO];
+  __shared__ float red[128];
+  const int t = threadIdx.x, ml = t % NB, lp = t / NB, wl = ml >> 5, lane = t & 31;
+  float w[O], gw[O], gb[O];
+#pragma unroll
+  for (int o = 0; o < O; ++o) { w[o] = W[o + (size_t)ml * O]; gw[o] = 0.f; gb[o] = 0.f; }
+  const float* bias = W + (size_t)O * K;
+  const double scale = multiplier ? *multiplier : 1.0;
+  CostStats local = cs_empty();
+  for (long base = (long)blockIdx.x * LANES * PB; base < points; base += (long)gridDim.x * LANES * PB) {
+    const long p0 = base + (long)lp * PB;  // this lane's first point of the round
+    float y[PB][R];
+#pragma unroll
+    for (int j = 0; j < PB; ++j)
+#pragma unroll
+      for (int r = 0; r < R; ++r) y[j][r] = p0 + j < points ? Y[((size_t)(p0 + j) * R + r) * K + ml] : 0.f;
+#pragma unroll
+    for (int j = 0; j < PB; ++j)
+#pragma unroll
+      for (int i = 0; i < RO; ++i) {
+        float v = w[i % O] * y[j][i / O];
+#pragma unroll
+        for (int s = 16; s; s >>= 1) v += __shfl_xor_sync(0xffffffffu, v, s);
+        if (lane == 0) zsum[lp][wl][j][i] = v;
+      }
+    __syncthreads();
+    if (ml < PB && p0 + ml < points) {
+      const int j = ml;
+      for (int i = 0; i < RO; ++i) {
+        float z = 0.f;
+        for (int q = 0; q < WPL; ++q) z += zsum[lp][q][j][i];
+        comp[lp][j][i] = z + (i < O ? bias[i] : 0.f);
+      }
+      const long p = p0 + j;
+      cpde_sample(comp[lp][j], gsh[lp][j], RO, fields, samples, offset + (int)p, weights[offset + p], scale, collect,
+                  1, local);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < PB; ++j) {
+      if (p0 + j >= points) break;
+      float dy[R];
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        float acc = 0.f;
+#pragma unroll
+        for (int o = 0; o < O; ++o) {
+          const float d = gsh[lp][j][r * O + o];
+          acc = fmaf(w[o], d, acc);
+          gw[o] = fmaf(d, y[j][r], gw[o]);
+        }
+        dy[r] = acc;
+      }
+      if (ml == 0)
+#pragma unroll
+        for (int o = 0; o < O; ++o) gb[o] += gsh[lp][j][o];
+      StaticJet<HEAD_SID>::template adjoint<HEAD_ACT>(y[j], dy);
+      float* out = dZ + (size_t)(p0 + j) * R * K + ml;
+#pragma unroll
+      for (int r = 0; r < R; ++r) out[(size_t)r * K] = dy[r];
+    }
+  }
+  float* out = partials + (size_t)blockIdx.x * O * (K + 1);
+  for (int o = 0; o < O; ++o) {
+    red[t] = gw[o];
+    __syncthreads();
+    if (lp == 0) { float s = 0.f; for (int l = 0; l < LANES; ++l) s += red[l * NB + ml]; out[o + (size_t)ml * O] = s; }
+    __syncthreads();
+    red[t] = gb[o];
+    __syncthreads();
+    if (t == 0) { float s = 0.f; for (int l = 0; l < LANES; ++l) s += red[l * NB]; out[o + (size_t)K * O] = s; }
+    __syncthreads();
+  }
+  cs_finish(local, cost_partials, ticket, total);
+}
+)HEAD";
+
+// Points per lane and round of the head: up to 8, while PB * R jet values
+// stay within about 40 registers.
+inline int head_points_per_lane(int R) { return std::max(1, std::min(8, 40 / R)); }
+
+inline std::string expression_head_source(const std::vector<ScalarNode>& nodes, const char* jet_source, int sid,
+                                          bool tanh_act, int R, int O, int K) {
+    std::ostringstream s;
+    s << kExpressionPrelude << kHeadActivations << jet_source << "\n" << expression_sample_function(nodes);
+    s << "#define HEAD_R " << R << "\n#define HEAD_O " << O << "\n#define HEAD_NB " << K << "\n#define HEAD_PB "
+      << head_points_per_lane(R) << "\n#define HEAD_SID " << sid << "\n#define HEAD_ACT "
+      << (tanh_act ? "Tanh" : "Sigmoid") << "\n";
+    s << kHeadKernel;
     return s.str();
 }
 
@@ -196,15 +344,15 @@ inline void driver_check(CUresult r, const char* what) {
     throw DeviceError(std::string(what) + ": " + (msg ? msg : "CUDA driver error"));
 }
 
-struct ExpressionProgram {
-    std::vector<ScalarNode> nodes;
-    std::string code, log;
+// A kernel compiled at run time with NVRTC for this device's sm_XXa target.
+struct RuntimeKernel {
+    std::string code, name, log;
     CUmodule module = nullptr;
     CUfunction kernel = nullptr;
 
-    explicit ExpressionProgram(std::vector<ScalarNode> ir) : nodes(std::move(ir)), code(expression_source(nodes)) {}
-    ExpressionProgram(const ExpressionProgram&) = delete;
-    ~ExpressionProgram() {
+    RuntimeKernel(std::string source, std::string entry) : code(std::move(source)), name(std::move(entry)) {}
+    RuntimeKernel(const RuntimeKernel&) = delete;
+    ~RuntimeKernel() {
         if (module) driver_api().module_unload(module);
     }
 
@@ -218,7 +366,7 @@ struct ExpressionProgram {
                            (prop.major >= 9 ? "a" : "");
         const char* options[] = {"--std=c++17", arch.c_str()};
         nvrtcProgram program;
-        nvrtcResult r = nvrtcCreateProgram(&program, code.c_str(), "cpde_integral.cu", 0, nullptr, nullptr);
+        nvrtcResult r = nvrtcCreateProgram(&program, code.c_str(), (name + ".cu").c_str(), 0, nullptr, nullptr);
         if (r != NVRTC_SUCCESS) throw DeviceError(nvrtcGetErrorString(r));
         r = nvrtcCompileProgram(program, 2, options);
         size_t size = 0;
@@ -235,8 +383,15 @@ struct ExpressionProgram {
         nvrtcGetCUBIN(program, cubin.data());
         nvrtcDestroyProgram(&program);
         driver_check(driver_api().module_load(&module, cubin.data()), "cuModuleLoadData");
-        driver_check(driver_api().get_function(&kernel, module, "cpde_integral"), "cuModuleGetFunction");
+        driver_check(driver_api().get_function(&kernel, module, name.c_str()), "cuModuleGetFunction");
     }
+};
+
+// An integral cost's program: its IR and the standalone cost kernel.
+struct ExpressionProgram : RuntimeKernel {
+    std::vector<ScalarNode> nodes;
+    explicit ExpressionProgram(std::vector<ScalarNode> ir)
+        : RuntimeKernel(expression_source(ir), "cpde_integral"), nodes(std::move(ir)) {}
 };
 
 }  // namespace cpde

@@ -52,13 +52,6 @@ struct FastBackward {
         float* cur = n.dz[1].ptr;
         const bool tensor = use_tensor;
         if (tensor) {
-            static bool tc_ready[64] = {};
-            if (!tc_ready[e.device & 63]) {
-                using TT = tcg::Tiling<R>;
-                allow_smem(tcg::k_backward_tc<SID, Act, false>, TT::SMEM);
-                allow_smem(tcg::k_backward_tc<SID, Act, true>, TT::SMEM);
-                tc_ready[e.device & 63] = true;
-            }
             n.wb_hi.reserve(n.params);
             n.wb_lo.reserve(n.params);
         }
@@ -68,7 +61,7 @@ struct FastBackward {
             // enough column splits to fill two CTAs per SM, but at least 64
             // columns (FFMA) or 128 columns (tensor cores) per split
             const int tiles = ((N + BM - 1) / BM) * ((M + BM - 1) / BM);
-            const bool tc_wgrad = tensor && M % tcg::BM == 0 && N % tcg::BM == 0;
+            const bool tc_wgrad = tensor && M % 32 == 0 && N % 32 == 0;  // slices past a narrow layer's end are zeros
             const long min_cols = tc_wgrad ? 128 : 64, align = tc_wgrad ? tcg::KS : BK;
             long splits = std::max(1L, std::min<long>((2L * 148 + tiles - 1) / tiles, (cols + min_cols - 1) / min_cols));
             long per = ((cols + splits - 1) / splits + align - 1) / align * align;
@@ -83,7 +76,7 @@ struct FastBackward {
                     allow_smem(ws::k_wgrad_ws, ws::kWgSmem);
                     wg_ready[e.device & 63] = true;
                 }
-                const int ny = N / tcg::BM, nz = M / tcg::BM;
+                const int ny = (N + tcg::BM - 1) / tcg::BM, nz = (M + tcg::BM - 1) / tcg::BM;
                 splits = std::max(1L, std::min<long>(std::max(1, 148 / (ny * nz)), (cols + 31) / 32));
                 n.partial.reserve(size_t(splits) * M * (N + 1));
                 const CUtensorMap md = mn32_map(cur, M, cols), ma = mn32_map(n.act[l - 1].ptr, N, cols);
@@ -113,7 +106,7 @@ struct FastBackward {
             const bool input = l - 1 == 1;
             float* next = cur == n.dz[0].ptr ? n.dz[1].ptr : n.dz[0].ptr;
             const int K0 = n.neurons[0];
-            if (tensor && N % tcg::BM == 0 && M % tcg::KS == 0 && M <= ws::kMaxK) {
+            if (tensor && N % 32 == 0 && M % tcg::KS == 0 && M <= ws::kMaxK) {
                 // warp-specialised: W^T resident in tensor memory, dZ slab ring in shared memory
                 using WT = ws::Tiling<R>;
                 static bool bw_ready[64] = {};
@@ -124,8 +117,9 @@ struct FastBackward {
                 }
                 const CUtensorMap mz = tensor_map(cur, M, cols, WT::N);
                 const long tt = (P + WT::PTS - 1) / WT::PTS;
-                const int bx = int(std::min<long>(tt, std::max(1, 148 / (N / tcg::BM))));
-                dim3 grid(bx, N / tcg::BM);
+                const int ny = (N + tcg::BM - 1) / tcg::BM;  // a narrower layer fills part of one slice
+                const int bx = int(std::min<long>(tt, std::max(1, 148 / ny)));
+                dim3 grid(bx, ny);
                 if (input) {
                     n.input_partial.reserve(size_t(2 * bx) * N * (K0 + 1));
                     CPDE_RUN(e, "backward_input_ws",
@@ -144,29 +138,36 @@ struct FastBackward {
                 continue;
             }
             if (tensor && N % tcg::BM == 0 && M % tcg::KS == 0) {
-                using TT = tcg::Tiling<R>;
+                // wider layers: the W^T slabs stream through the shared-memory ring with the dZ slabs
+                using WT = ws::WideTiling<R>;
+                static bool wide_ready[64] = {};
+                if (!wide_ready[e.device & 63]) {
+                    allow_smem(ws::k_backward_wide<SID, Act, false>, WT::SMEM);
+                    allow_smem(ws::k_backward_wide<SID, Act, true>, WT::SMEM);
+                    wide_ready[e.device & 63] = true;
+                }
                 float* hi = n.wb_hi.ptr + n.offset[l - 1];
                 float* lo = n.wb_lo.ptr + n.offset[l - 1];
                 CPDE_RUN(e, "split_weights", (tcg::k_split_tf32<<<grid_for(long(M) * N), 256, 0, e.stream>>>(
                                                  W, hi, lo, N, M, 0)));
                 const CUtensorMap mh = tensor_map(hi, M, N, tcg::BM), ml = tensor_map(lo, M, N, tcg::BM);
-                const CUtensorMap mz = tensor_map(cur, M, cols, TT::N);
-                const long tt = (P + TT::PTS - 1) / TT::PTS;
-                const int bx = int(std::min<long>(tt, std::max(1, 444 / (N / tcg::BM))));
+                const CUtensorMap mz = tensor_map(cur, M, cols, WT::N);
+                const long tt = (P + WT::PTS - 1) / WT::PTS;
+                const int bx = int(std::min<long>(tt, std::max(1, 148 / (N / tcg::BM))));
                 dim3 grid(bx, N / tcg::BM);
                 if (input) {
-                    n.input_partial.reserve(size_t(bx) * N * (K0 + 1));
-                    CPDE_RUN(e, "backward_input_tc",
-                             (tcg::k_backward_tc<SID, Act, true><<<grid, tcg::THREADS, TT::SMEM, e.stream>>>(
-                                 mh, ml, mz, N, M, P, n.act[1].ptr, nullptr, n.act[0].ptr, K0, n.input_partial.ptr,
+                    n.input_partial.reserve(size_t(2 * bx) * N * (K0 + 1));
+                    CPDE_RUN(e, "backward_input_wide",
+                             (ws::k_backward_wide<SID, Act, true><<<grid, ws::THREADS, WT::SMEM, e.stream>>>(
+                                 mz, mh, ml, M, N, P, n.act[1].ptr, nullptr, n.act[0].ptr, K0, n.input_partial.ptr,
                                  e.tc_error.ptr)));
                     long isize = long(N) * (K0 + 1);
                     CPDE_RUN(e, "sum_partials", (k_sum_partials<<<fast::sum_grid(isize), 256, 0, e.stream>>>(
-                                                    n.input_partial.ptr, bx, isize, n.gradient_base(0, target))));
+                                                    n.input_partial.ptr, 2 * bx, isize, n.gradient_base(0, target))));
                 } else {
-                    CPDE_RUN(e, "backward_tc",
-                             (tcg::k_backward_tc<SID, Act, false><<<grid, tcg::THREADS, TT::SMEM, e.stream>>>(
-                                 mh, ml, mz, N, M, P, n.act[l - 1].ptr, next, nullptr, 0, nullptr, e.tc_error.ptr)));
+                    CPDE_RUN(e, "backward_wide",
+                             (ws::k_backward_wide<SID, Act, false><<<grid, ws::THREADS, WT::SMEM, e.stream>>>(
+                                 mz, mh, ml, M, N, P, n.act[l - 1].ptr, next, nullptr, 0, nullptr, e.tc_error.ptr)));
                     cur = next;
                 }
                 continue;

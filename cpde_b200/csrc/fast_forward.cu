@@ -33,7 +33,7 @@ struct FastForward {
                 CPDE_RUN(e, "input_forward",
                          (k_input_forward<SID, Act><<<grid_for(long(M) * P, THREADS, 148 * 32), THREADS, 0,
                                                       e.stream>>>(M, K, P, W, b, n.act[0].ptr, n.act[1].ptr)));
-            } else if (tensor && M % tcg::BM == 0 && K % tcg::KS == 0 && K <= ws::kMaxK) {
+            } else if (tensor && M % 32 == 0 && K % tcg::KS == 0 && K <= ws::kMaxK) {
                 // warp-specialised: weights resident in tensor memory, slab ring in shared memory
                 using WT = ws::Tiling<R>;
                 static bool ws_ready[64] = {};
@@ -43,15 +43,17 @@ struct FastForward {
                 }
                 const CUtensorMap mx = tensor_map(n.act[l - 1].ptr, K, P * R, WT::N);
                 const long tiles = (P + WT::PTS - 1) / WT::PTS;
-                dim3 grid(unsigned(std::min<long>(tiles, std::max(1, 148 / (M / tcg::BM)))), unsigned(M / tcg::BM));
+                const int ny = (M + tcg::BM - 1) / tcg::BM;  // a narrower layer fills part of one slice
+                dim3 grid(unsigned(std::min<long>(tiles, std::max(1, 148 / ny))), unsigned(ny));
                 CPDE_RUN(e, "forward_ws", (ws::k_forward_ws<SID, Act><<<grid, ws::THREADS, WT::SMEM, e.stream>>>(
                                               mx, M, K, P, W, n.act[l].ptr, e.tc_error.ptr)));
             } else if (tensor && M % tcg::BM == 0 && K % tcg::KS == 0) {
-                using TT = tcg::Tiling<R>;
-                static bool tc_ready[64] = {};
-                if (!tc_ready[e.device & 63]) {
-                    allow_smem(tcg::k_forward_tc<SID, Act>, TT::SMEM);
-                    tc_ready[e.device & 63] = true;
+                // wider inputs: the weight slabs stream through the shared-memory ring with the activations
+                using WT = ws::WideTiling<R>;
+                static bool wide_ready[64] = {};
+                if (!wide_ready[e.device & 63]) {
+                    allow_smem(ws::k_forward_wide<SID, Act>, WT::SMEM);
+                    wide_ready[e.device & 63] = true;
                 }
                 n.w_hi.reserve(n.params);
                 n.w_lo.reserve(n.params);
@@ -60,12 +62,12 @@ struct FastForward {
                 CPDE_RUN(e, "split_weights", (tcg::k_split_tf32<<<grid_for(long(M) * K), 256, 0, e.stream>>>(
                                                  W, hi, lo, M, K, 1)));
                 const CUtensorMap mh = tensor_map(hi, K, M, tcg::BM), ml = tensor_map(lo, K, M, tcg::BM);
-                const CUtensorMap mx = tensor_map(n.act[l - 1].ptr, K, P * R, TT::N);
-                const long tiles = (P + TT::PTS - 1) / TT::PTS;
-                dim3 grid(unsigned(std::min<long>(tiles, std::max(1, 444 / (M / tcg::BM)))), unsigned(M / tcg::BM));
-                CPDE_RUN(e, "forward_tc",
-                         (tcg::k_forward_tc<SID, Act><<<grid, tcg::THREADS, TT::SMEM, e.stream>>>(
-                             mh, ml, mx, M, K, P, b, n.act[l].ptr, e.tc_error.ptr)));
+                const CUtensorMap mx = tensor_map(n.act[l - 1].ptr, K, P * R, WT::N);
+                const long tiles = (P + WT::PTS - 1) / WT::PTS;
+                dim3 grid(unsigned(std::min<long>(tiles, std::max(1, 148 / (M / tcg::BM)))), unsigned(M / tcg::BM));
+                CPDE_RUN(e, "forward_wide",
+                         (ws::k_forward_wide<SID, Act><<<grid, ws::THREADS, WT::SMEM, e.stream>>>(
+                             mx, mh, ml, M, K, P, b, n.act[l].ptr, e.tc_error.ptr)));
             } else if (M <= 64) {
                 dim3 grid(unsigned((P + T::PTS - 1) / T::PTS), 1);
                 CPDE_RUN(e, "forward",

@@ -1,6 +1,7 @@
 // Fused matching head and point-tile epoch dispatch (its own translation
 // unit, compiled in parallel with the rest of the library).
 #include "engine_internal.hpp"
+#include "generated/jets_static_source.cuh"
 
 namespace cpde {
 
@@ -121,6 +122,54 @@ struct PointEpoch {
 void Engine::fused_head(NetRecord& n, CostRecord& c, Context& ctx, long points, int offset, bool collect,
                         const double* multiplier, CostReduce red, float* target) {
     with_schema(ctx.static_id, FastHead{*this, n, c, points, offset, collect, multiplier, red, target});
+}
+
+// The fused expression head (an NVRTC kernel built from the cost's program
+// and the schema's jet code, expression.hpp) takes integral costs on fast-tier
+// networks whose last hidden layer has 32, 64 or 128 neurons and at most 4
+// outputs; other shapes run the output layer, the cost and the output
+// backward as three kernels.
+bool Engine::expression_head_ok(NetRecord& n, CostRecord& c, Context& ctx) const {
+    if (c.kind != 2 || !c.program || !fast_ok(n, ctx)) return false;
+    const int K = n.neurons[n.layers - 1], O = n.neurons.back();
+    return (K == 32 || K == 64 || K == 128) && O <= 4 && ctx.R() * O <= 128;
+}
+
+void Engine::expression_head(NetRecord& n, CostRecord& c, Context& ctx, long points, int offset, bool collect,
+                             const double* multiplier, CostReduce red, float* target) {
+    const int L = n.layers, K = n.neurons[L - 1], O = n.neurons.back(), R = ctx.R();
+    const bool tanh_act = n.linear[1] == kTanhAct;
+    const std::string key = std::to_string(ctx.static_id) + "|" + std::to_string(tanh_act) + "|" +
+                            std::to_string(O) + "|" + std::to_string(K);
+    if (!c.head || c.head_key != key) {
+        std::string source = expression_head_source(c.program->nodes, kStaticJetSource[ctx.static_id],
+                                                    ctx.static_id, tanh_act, R, O, K);
+        auto& h = heads[source];
+        if (!h) h = std::make_shared<RuntimeKernel>(std::move(source), "cpde_head");
+        c.head = h;
+        c.head_key = key;
+    }
+    c.head->compile();
+    const int per_round = (128 / K) * head_points_per_lane(R);  // points a CTA takes per round
+    const int grid = int(std::min<long>(148L * 8, std::max(1L, (points + per_round - 1) / per_round)));
+    n.partial.reserve(size_t(grid) * O * (K + 1));
+    int k = K, p = int(points), off = offset, samples = c.samples, col = collect;
+    const float* W = n.weights(L - 1);
+    const float* Y = n.act[L - 1].ptr;
+    float* dZ = n.dz[1].ptr;
+    const double* fields = c.fields.ptr;
+    const double* weights = c.quadrature_weights.ptr;
+    float* partials = n.partial.ptr;
+    void* args[] = {&k,        &p,      &off,          &samples,           (void*)&W,         (void*)&Y,
+                    &dZ,       (void*)&fields, (void*)&weights, (void*)&multiplier, &col, &partials,
+                    (void*)&red.partials, (void*)&red.ticket, (void*)&red.total};
+    CPDE_RUN(*this, "head_expression",
+             driver_check(driver_api().launch(c.head->kernel, unsigned(grid), 1, 1, 128, 1, 1, 0, stream, args, nullptr),
+                          "cuLaunchKernel"));
+    const long size = long(O) * (K + 1);
+    CPDE_RUN(*this, "sum_partials", (fast::k_sum_partials<<<fast::sum_grid(size), 256, 0, stream>>>(
+                                        n.partial.ptr, grid, size, n.gradient_base(L - 1, target))));
+    layer_done(L - 1);
 }
 
 void Engine::point_epoch(NetRecord& n, CostRecord& c, Context& ctx, long points, int offset, bool collect,

@@ -138,7 +138,9 @@ __device__ __forceinline__ void produce(const Ring& r, const CUtensorMap* map, l
             ++it;
         }
     }
-    for (uint32_t k = it > S ? it - S : 0; k < it; ++k) tc::mbar_wait(r.full + k % S, (k / S) & 1, tcg::kWaitCycles);
+    // a load that never lands must not go unnoticed: the CTA then reports an error
+    for (uint32_t k = it > S ? it - S : 0; k < it; ++k)
+        if (!tc::mbar_wait(r.full + k % S, (k / S) & 1, tcg::kWaitCycles)) *r.abort = 1;
 }
 
 // lo parts of float4 elements [0, count) of x4 into l4, strided over 128
@@ -183,20 +185,31 @@ __device__ __forceinline__ void split_all(const Ring& r, long tiles, int N, int 
         }
 }
 
-// MMA issuer `which` (0 or 1): for the CTA's tiles of local index
-// which, which + 2, ..., lo*hi + hi*hi + hi*lo over the K slabs into
-// accumulator `which`, once the split warps have written the slab's lo part
-// (issuing the two terms of the raw slab before that wait measured slower);
-// each slab's stage is released by a commit once its MMAs have read it. Slab counter `it` runs over all the CTA's slabs in ring
+// How many MMA issuers a ring of S stages supports for tiles of `slabs` K
+// slabs. An issuer that skips the other issuer's tile waits on a stage's
+// split barrier by phase parity; that is exact only if the stage's previous
+// phase (slab it - S) is already complete when the wait starts, which the
+// split warps' in-order progress guarantees when S > slabs (that slab then
+// precedes everything this issuer consumed before). With fewer stages one
+// issuer takes every tile, in ring order.
+__host__ __device__ constexpr int mma_issuers(int S, int slabs) { return S > slabs ? kMmaIssuers : 1; }
+
+// MMA issuer `which` of `issuers`: for the CTA's tiles of local index
+// which, which + issuers, ..., lo*hi + hi*hi + hi*lo over the K slabs into
+// accumulator (local tile index) & 1, once the split warps have written the
+// slab's lo part (issuing the two terms of the raw slab before that wait
+// measured slower); each slab's stage is released by a commit once its MMAs
+// have read it. Slab counter `it` runs over all the CTA's slabs in ring
 // order, the other issuer's included.
 template <int N, int SLAB, int S = STAGES>
 __device__ __forceinline__ void issue_mmas(const Ring& r, uint32_t tmem, long tiles, int slabs, int which) {
     constexpr uint32_t idesc = tc::idesc_tf32(128, N);
+    const int issuers = mma_issuers(S, slabs);
     bool ok = tc::mbar_wait_or_abort(r.a_ready, 0, tcg::kWaitCycles, r.abort);
     tc::tc_fence_after();
     uint32_t it = which * slabs, local = which;
-    for (long tile = blockIdx.x + which * gridDim.x; ok && tile < tiles;
-         tile += kMmaIssuers * gridDim.x, local += kMmaIssuers, it += (kMmaIssuers - 1) * slabs) {
+    for (long tile = blockIdx.x + which * gridDim.x; ok && which < issuers && tile < tiles;
+         tile += issuers * gridDim.x, local += issuers, it += (issuers - 1) * slabs) {
         const int a = local & 1;
         ok = tc::mbar_wait_or_abort(r.acc_empty + a, ((local >> 1) & 1) ^ 1, tcg::kWaitCycles, r.abort);
         tc::tc_fence_after();
@@ -220,22 +233,27 @@ __device__ __forceinline__ void issue_mmas(const Ring& r, uint32_t tmem, long ti
     }
     // every MMA this thread issued has completed once this commit arrives
     tc::mma_commit(r.drain + which);
-    tc::mbar_wait(r.drain + which, 0, tcg::kWaitCycles);
+    if (!tc::mbar_wait(r.drain + which, 0, tcg::kWaitCycles)) *r.abort = 1;
 }
 
 // Epilogue warps 6-9: the A operand's row `m` (K values) split into TF32 hi
 // and lo, into tensor memory columns [0, K) and [128, 128 + K) of the thread's
 // lane. The forward's A is W (column-major, leading dimension M: row m holds
 // W[m + k M]); the backward's is W^T (row n holds W[k + n K], contiguous).
+// Rows m >= M (a layer narrower than the tile's 128 rows) are zero, so those
+// accumulator lanes stay zero and the epilogue skips them.
 __device__ __forceinline__ void load_weights(const Ring& r, uint32_t tmem, const float* __restrict__ W, int M,
                                              int K, int m, bool transposed = false) {
     const int quarter = (threadIdx.x >> 5) & 3;
     const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
+    const bool live = m < M;
     for (int c0 = 0; c0 < K; c0 += 8) {
         float h[8], l[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            const float v = transposed ? __ldg(W + (size_t)m * K + c0 + j) : __ldg(W + m + (size_t)(c0 + j) * M);
+            const float v = !live ? 0.f
+                            : transposed ? __ldg(W + (size_t)m * K + c0 + j)
+                                         : __ldg(W + m + (size_t)(c0 + j) * M);
             h[j] = tc::tf32_round(v);
             l[j] = tc::tf32_round(v - h[j]);
         }
@@ -282,8 +300,9 @@ __global__ void __launch_bounds__(THREADS, 1) k_forward_ws(const __grid_constant
     } else {
         const int quarter = warp & 3, group = (warp - kEpilogueWarp) >> 2;
         const int m = blockIdx.y * 128 + quarter * 32 + lane;
+        const bool live = m < M;  // the same for the whole warp: M is a multiple of 32
         if (group == 0) load_weights(r, tmem, W, M, K, m);
-        const float b0 = __ldg(W + (size_t)M * K + m);
+        const float b0 = live ? __ldg(W + (size_t)M * K + m) : 0.f;
         const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
         uint32_t local = 0;
         for (long tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
@@ -291,7 +310,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_forward_ws(const __grid_constant
             if (!warp_wait(r.acc_full + a, (local >> 1) & 1, r.abort)) break;
             tc::tc_fence_after();
             const long p0 = tile * T::PTS;
-            for (int p = group; p < T::PTS; p += kEpilogueGroups) {
+            for (int p = group; live && p < T::PTS; p += kEpilogueGroups) {
                 if (p0 + p >= P) break;
                 float z[R], y[R];
                 tc::tmem_read<R>(lane_base + kAccColumn + a * 128 + p * R, z);
@@ -347,6 +366,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_backward_ws(const __grid_constan
         const int quarter = warp & 3, group = (warp - kEpilogueWarp) >> 2;
         const int et = threadIdx.x - kEpilogueWarp * 32;  // epilogue thread 0 .. 32 * 4 * groups - 1
         const int n = blockIdx.y * 128 + quarter * 32 + lane;
+        const bool live = n < N;  // the same for the whole warp: N is a multiple of 32
         if (group == 0) load_weights(r, tmem, W, N, Ml, n, true);
         const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
         constexpr int SLOT = R * 32 * 4 * kEpilogueGroups;  // floats of one slot: [q][epilogue thread]
@@ -371,8 +391,9 @@ __global__ void __launch_bounds__(THREADS, 1) k_backward_ws(const __grid_constan
                 ft += gridDim.x;
             }
         };
+        if (live)
 #pragma unroll
-        for (int k = 0; k < kStagingSlots - 1; ++k) stage(k);
+            for (int k = 0; k < kStagingSlots - 1; ++k) stage(k);
         int slot = 0;
         float gacc[9];
 #pragma unroll
@@ -383,7 +404,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_backward_ws(const __grid_constan
             if (!warp_wait(r.acc_full + a, (local >> 1) & 1, r.abort)) break;
             tc::tc_fence_after();
             const long p0 = tile * T::PTS;
-            for (int p = group; p < T::PTS; p += kEpilogueGroups) {
+            for (int p = group; live && p < T::PTS; p += kEpilogueGroups) {
                 if (p0 + p >= P) break;
                 stage(slot == 0 ? kStagingSlots - 1 : slot - 1);  // the slot read one item ago
                 float g[R], y[R];
@@ -406,6 +427,236 @@ __global__ void __launch_bounds__(THREADS, 1) k_backward_ws(const __grid_constan
             if (lane == 0) tc::mbar_arrive(r.acc_empty + a);
         }
         tc::copy_async_wait<0>();  // no copy may land after the CTA ends
+        if (INPUT_GRAD && live) {
+            float* out = input_partials + (size_t)(2 * blockIdx.x + group) * N * (K0 + 1);
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+                if (k < K0) out[n + (size_t)k * N] = gacc[k];
+            out[n + (size_t)K0 * N] = gacc[8];
+        }
+    }
+    teardown(r, tmem, error);
+}
+
+// ---------------------------------------------------------------------------
+// Layers of more than kMaxK inputs (the 256- and 512-neuron layers of configs
+// 4 and 5). The weights of a 128-neuron slice no longer fit in tensor memory
+// beside the two accumulators, so every stage of the ring carries the K slab
+// of the weights (TF32 hi and lo, split once per pass into K-major arrays in
+// global memory, where they stay in L2) beside the activation slab, and the
+// MMAs read A from shared memory. The roles are the kernels' above; the
+// epilogue warps load no weights, and the backward's epilogue reads Y_prev
+// directly instead of staging it (at these widths the layer is bound by the
+// tensor cores: a tile's MMAs take longer than its epilogue, which runs
+// while the other accumulator fills).
+
+constexpr int kWeightSlab = 128 * 128;  // bytes: 128 neurons x 32 fp32 of K
+
+template <int R>
+struct WideTiling {
+    using T = Tiling<R>;
+    static constexpr int PTS = T::PTS, COLS = T::COLS, N = T::N, SLAB = T::SLAB;
+    static constexpr int STAGE = 2 * SLAB + 2 * kWeightSlab;
+    static constexpr int S = (kSmemLimit - 1024 - 256) / STAGE;
+    static constexpr int SMEM = S * STAGE + 1024 + 256;
+    static_assert(S >= 3, "wide-layer ring too shallow");
+};
+
+// The ring of carve_ring<SLAB, S> with the weight slabs between the
+// activation slabs and the barriers: a_hi[S][kWeightSlab], a_lo[S][...].
+template <int SLAB, int S>
+__device__ __forceinline__ Ring carve_wide(uint8_t* raw, float*& a_hi, float*& a_lo) {
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
+    a_hi = reinterpret_cast<float*>(base + 2 * S * SLAB);
+    a_lo = reinterpret_cast<float*>(base + 2 * S * SLAB + S * kWeightSlab);
+    // carve_ring places its barriers right after 2 S SLAB bytes: hand it a base
+    // moved back by the weight slabs' size so they land after those instead
+    Ring r = carve_ring<SLAB, S>(base + 2 * S * kWeightSlab);
+    r.hi = reinterpret_cast<float*>(base);
+    r.lo = reinterpret_cast<float*>(base + S * SLAB);
+    return r;
+}
+
+// Producer of the wide layers: per K slab, the activation slab of the tile
+// and the weight slabs (hi, lo) of this CTA's neurons `a_row`..+127.
+template <int SLAB, int S>
+__device__ __forceinline__ void produce_wide(const Ring& r, float* a_hi, float* a_lo, const CUtensorMap* map,
+                                             const CUtensorMap* map_a_hi, const CUtensorMap* map_a_lo, int a_row,
+                                             long tiles, int tile_columns, int N, int slabs) {
+    uint32_t it = 0;
+    for (long tile = blockIdx.x; tile < tiles && !*r.abort; tile += gridDim.x) {
+        const int col0 = int(tile * tile_columns);
+        for (int s = 0; s < slabs; ++s) {
+            const int st = it % S;
+            if (!tc::mbar_wait_or_abort(r.empty + st, ((it / S) & 1) ^ 1, tcg::kWaitCycles, r.abort)) break;
+            tc::mbar_expect_tx(r.full + st, uint32_t(N) * 128 + 2 * kWeightSlab);
+            tc::tma_load_2d(r.hi + st * (SLAB / 4), map, r.full + st, s * 32, col0);
+            tc::tma_load_2d(a_hi + st * (kWeightSlab / 4), map_a_hi, r.full + st, s * 32, a_row);
+            tc::tma_load_2d(a_lo + st * (kWeightSlab / 4), map_a_lo, r.full + st, s * 32, a_row);
+            ++it;
+        }
+    }
+    // a load that never lands must not go unnoticed: the CTA then reports an error
+    for (uint32_t k = it > S ? it - S : 0; k < it; ++k)
+        if (!tc::mbar_wait(r.full + k % S, (k / S) & 1, tcg::kWaitCycles)) *r.abort = 1;
+}
+
+// MMA issuer of the wide layers: issue_mmas with A (hi, lo) from the stage's
+// weight slabs in shared memory.
+template <int N, int SLAB, int S>
+__device__ __forceinline__ void issue_mmas_wide(const Ring& r, const float* a_hi, const float* a_lo, uint32_t tmem,
+                                                long tiles, int slabs, int which) {
+    constexpr uint32_t idesc = tc::idesc_tf32(128, N);
+    const int issuers = mma_issuers(S, slabs);
+    bool ok = true;
+    uint32_t it = which * slabs, local = which;
+    for (long tile = blockIdx.x + which * gridDim.x; ok && which < issuers && tile < tiles;
+         tile += issuers * gridDim.x, local += issuers, it += (issuers - 1) * slabs) {
+        const int a = local & 1;
+        ok = tc::mbar_wait_or_abort(r.acc_empty + a, ((local >> 1) & 1) ^ 1, tcg::kWaitCycles, r.abort);
+        tc::tc_fence_after();
+        const uint32_t d = tmem + kAccColumn + a * 128;
+        for (int s = 0; ok && s < slabs; ++s, ++it) {
+            const int st = it % S;
+            ok = tc::mbar_wait_or_abort(r.split + st, (it / S) & 1, tcg::kWaitCycles, r.abort);
+            if (!ok) break;
+            tc::tc_fence_after();
+            const uint32_t bh = tc::smem_u32(r.hi + st * (SLAB / 4)), bl = tc::smem_u32(r.lo + st * (SLAB / 4));
+            const uint32_t ah = tc::smem_u32(a_hi + st * (kWeightSlab / 4));
+            const uint32_t al = tc::smem_u32(a_lo + st * (kWeightSlab / 4));
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+                const uint32_t off = kk * 32;  // 8 TF32 values along the 128-byte rows
+                tc::mma_tf32(d, tc::desc_k_sw128(al + off), tc::desc_k_sw128(bh + off), idesc, (s | kk) != 0);
+                tc::mma_tf32(d, tc::desc_k_sw128(ah + off), tc::desc_k_sw128(bl + off), idesc, 1);
+                tc::mma_tf32(d, tc::desc_k_sw128(ah + off), tc::desc_k_sw128(bh + off), idesc, 1);
+            }
+            tc::mma_commit(r.empty + st);
+        }
+        if (ok) tc::mma_commit(r.acc_full + a);
+    }
+    tc::mma_commit(r.drain + which);
+    if (!tc::mbar_wait(r.drain + which, 0, tcg::kWaitCycles)) *r.abort = 1;
+}
+
+// Hidden layer forward of more than kMaxK inputs: Y = f(W X + b). The
+// weights come as TF32 hi/lo arrays, row m of K values each (maps with
+// 32 x 128 boxes, 128-byte swizzle). grid = (CTAs over column tiles, M / 128).
+template <int SID, class Act>
+__global__ void __launch_bounds__(THREADS, 1) k_forward_wide(const __grid_constant__ CUtensorMap map_x,
+                                                             const __grid_constant__ CUtensorMap map_w_hi,
+                                                             const __grid_constant__ CUtensorMap map_w_lo, int M,
+                                                             int K, long P, const float* __restrict__ bias,
+                                                             float* __restrict__ Y, int* error) {
+    constexpr int R = StaticJet<SID>::R;
+    using T = WideTiling<R>;
+    extern __shared__ uint8_t smem_raw[];
+    float *a_hi, *a_lo;
+    Ring r = carve_wide<T::SLAB, T::S>(smem_raw, a_hi, a_lo);
+    ring_init<T::S>(r);
+    const uint32_t tmem = *r.tmem_slot;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long tiles = (P + T::PTS - 1) / T::PTS;
+    const int slabs = K / 32;
+    if (warp == kProducerWarp) {
+        if (lane == 0)
+            produce_wide<T::SLAB, T::S>(r, a_hi, a_lo, &map_x, &map_w_hi, &map_w_lo, blockIdx.y * 128, tiles, T::COLS,
+                                        T::N, slabs);
+    } else if (warp == kMmaWarp || warp == kSecondMmaWarp) {
+        if (lane == 0) issue_mmas_wide<T::N, T::SLAB, T::S>(r, a_hi, a_lo, tmem, tiles, slabs, warp == kMmaWarp ? 0 : 1);
+    } else if (warp < kEpilogueWarp) {
+        split_all<T::SLAB, T::S>(r, tiles, T::N, slabs);
+    } else {
+        const int quarter = warp & 3, group = (warp - kEpilogueWarp) >> 2;
+        const int m = blockIdx.y * 128 + quarter * 32 + lane;
+        const float b0 = __ldg(bias + m);
+        const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
+        uint32_t local = 0;
+        for (long tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
+            const int a = local & 1;
+            if (!warp_wait(r.acc_full + a, (local >> 1) & 1, r.abort)) break;
+            tc::tc_fence_after();
+            const long p0 = tile * T::PTS;
+            for (int p = group; p < T::PTS; p += kEpilogueGroups) {
+                if (p0 + p >= P) break;
+                float z[R], y[R];
+                tc::tmem_read<R>(lane_base + kAccColumn + a * 128 + p * R, z);
+                z[0] += b0;
+                StaticJet<SID>::template forward<Act>(z, y);
+                float* out = Y + ((size_t)(p0 + p) * R) * M + m;
+#pragma unroll
+                for (int q = 0; q < R; ++q) out[(size_t)q * M] = y[q];
+            }
+            tc::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(r.acc_empty + a);
+        }
+    }
+    teardown(r, tmem, error);
+}
+
+// Hidden layer backward of more than kMaxK inputs (Ml > kMaxK neurons in this
+// layer): dZ_prev = adjoint(W^T dZ; Y_prev), A = W^T from the TF32 hi/lo
+// arrays of W as stored (row n holds W[k + n Ml]). INPUT_GRAD as in
+// k_backward_ws. grid = (CTAs over column tiles, N / 128).
+template <int SID, class Act, bool INPUT_GRAD>
+__global__ void __launch_bounds__(THREADS, 1) k_backward_wide(const __grid_constant__ CUtensorMap map_dz,
+                                                              const __grid_constant__ CUtensorMap map_w_hi,
+                                                              const __grid_constant__ CUtensorMap map_w_lo, int Ml,
+                                                              int N, long P, const float* __restrict__ Yprev,
+                                                              float* __restrict__ dZprev, const float* __restrict__ X0,
+                                                              int K0, float* __restrict__ input_partials, int* error) {
+    constexpr int R = StaticJet<SID>::R;
+    using T = WideTiling<R>;
+    extern __shared__ uint8_t smem_raw[];
+    float *a_hi, *a_lo;
+    Ring r = carve_wide<T::SLAB, T::S>(smem_raw, a_hi, a_lo);
+    ring_init<T::S>(r);
+    const uint32_t tmem = *r.tmem_slot;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long tiles = (P + T::PTS - 1) / T::PTS;
+    const int slabs = Ml / 32;
+    if (warp == kProducerWarp) {
+        if (lane == 0)
+            produce_wide<T::SLAB, T::S>(r, a_hi, a_lo, &map_dz, &map_w_hi, &map_w_lo, blockIdx.y * 128, tiles, T::COLS,
+                                        T::N, slabs);
+    } else if (warp == kMmaWarp || warp == kSecondMmaWarp) {
+        if (lane == 0) issue_mmas_wide<T::N, T::SLAB, T::S>(r, a_hi, a_lo, tmem, tiles, slabs, warp == kMmaWarp ? 0 : 1);
+    } else if (warp < kEpilogueWarp) {
+        split_all<T::SLAB, T::S>(r, tiles, T::N, slabs);
+    } else {
+        const int quarter = warp & 3, group = (warp - kEpilogueWarp) >> 2;
+        const int n = blockIdx.y * 128 + quarter * 32 + lane;
+        const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
+        float gacc[9];
+#pragma unroll
+        for (int k = 0; k < 9; ++k) gacc[k] = 0.f;
+        uint32_t local = 0;
+        for (long tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
+            const int a = local & 1;
+            if (!warp_wait(r.acc_full + a, (local >> 1) & 1, r.abort)) break;
+            tc::tc_fence_after();
+            const long p0 = tile * T::PTS;
+            for (int p = group; p < T::PTS; p += kEpilogueGroups) {
+                if (p0 + p >= P) break;
+                float g[R], y[R];
+                const float* yp = Yprev + ((size_t)(p0 + p) * R) * N + n;
+#pragma unroll
+                for (int q = 0; q < R; ++q) y[q] = __ldg(yp + (size_t)q * N);
+                tc::tmem_read<R>(lane_base + kAccColumn + a * 128 + p * R, g);
+                StaticJet<SID>::template adjoint<Act>(y, g);
+                if (INPUT_GRAD) {
+                    fast::input_gradient<R>(g, X0 + (size_t)(p0 + p) * R * K0, K0, gacc);
+                } else {
+                    float* out = dZprev + ((size_t)(p0 + p) * R) * N + n;
+#pragma unroll
+                    for (int q = 0; q < R; ++q) out[(size_t)q * N] = g[q];
+                }
+            }
+            tc::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(r.acc_empty + a);
+        }
         if (INPUT_GRAD) {
             float* out = input_partials + (size_t)(2 * blockIdx.x + group) * N * (K0 + 1);
 #pragma unroll
@@ -502,12 +753,12 @@ static __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_
                 }
             }
             for (int k = it > kWgStages ? it - kWgStages : 0; k < it; ++k)
-                tc::mbar_wait(full + k % kWgStages, (k / kWgStages) & 1, tcg::kWaitCycles);
+                if (!tc::mbar_wait(full + k % kWgStages, (k / kWgStages) & 1, tcg::kWaitCycles)) *abort = 1;
         }
     } else if (warp == kMmaWarp || warp == kWgSecondMmaWarp) {
         // two issuers, the even and the odd chunks, each into its own accumulator
         if (lane == 0) {
-            constexpr uint32_t idesc = tc::idesc_tf32(M, 128) | (1u << 16);  // B (Y) MN-major, A (dZ) from TMEM
+            constexpr uint32_t idesc = tc::idesc_tf32(128, 128) | (1u << 16);  // B (Y) MN-major, A (dZ) from TMEM
             const int which = warp == kMmaWarp ? 0 : 1;
             const uint32_t acc = which ? tmem + kWgSecondAcc : tmem;
             for (int it = which; it < chunks; it += 2) {
@@ -527,7 +778,7 @@ static __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_
                 tc::mma_commit(empty + st);
             }
             tc::mma_commit(drain);
-            tc::mbar_wait(drain, 0, tcg::kWaitCycles);
+            if (!tc::mbar_wait(drain, 0, tcg::kWaitCycles)) *abort = 1;
         }
     } else if (warp < kWgEpilogueWarp) {
         // split warps: thread = neuron m (its TMEM lane); the stage's dZ row of
@@ -562,7 +813,7 @@ static __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(split + st);
         }
-        if (blockIdx.y == 0) out[(size_t)N * M + m_base + m] = bias;
+        if (blockIdx.y == 0 && m_base + m < M) out[(size_t)N * M + m_base + m] = bias;
     } else {
         // epilogue warps: the TF32 lo part of Y_prev of every stage (the raw
         // operand is its hi part; the columns past the end of the data arrive
@@ -590,7 +841,8 @@ static __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_
 #pragma unroll
                 for (int j = 0; j < 16; ++j) v[j] += odd[j];
 #pragma unroll
-                for (int j = 0; j < 16; ++j) out[m_base + m + (size_t)(n_base + c0 + j) * M] = v[j];
+                for (int j = 0; j < 16; ++j)  // the slices of layers narrower than 128 neurons end early
+                    if (m_base + m < M && n_base + c0 + j < N) out[m_base + m + (size_t)(n_base + c0 + j) * M] = v[j];
             }
         }
     }

@@ -8,7 +8,7 @@ short RPROP/Adam trajectories (op 8). The fixtures pin oracle/jets.py
 (tests/test_oracle_golden.py) and the CUDA engine (tests/test_gpu_parity.py)
 without needing the reference at test time.
 
-    python tests/golden/make_golden.py [path/to/cpde_ref_cpu_server]
+    python tests/golden/make_golden.py [path/to/cpde_ref_cpu_server] [--only-tanh]
 """
 import sys
 from pathlib import Path
@@ -131,7 +131,56 @@ def run_integral(s, name, rng):
     print(name, 'rows', len(t), 'loss', value)
 
 
-def main(exe):
+def run_tanh(s, name, rng, t, pts, layers, expression=None, chunk=0):
+    """A network with tanh hidden layers. The reference server has no tanh
+    (cuda/cpde_server.cu:457), so it evaluates the exact reparametrisation
+    tanh(z) = 2 sigma(2z) - 1 (cpde_b200.expressions.tanh_as_sigmoid): same
+    outputs and derivative rows; its weight gradients are mapped back through
+    the transpose of that linear map. Matching cost, or an integral cost when
+    `expression` is given. No optimizer trajectories: RPROP and Adam do not
+    commute with the reparametrisation."""
+    from cpde_b200.expressions import sigmoid_gradients_to_tanh, tanh_as_sigmoid
+    linear = [1] + [2] * (len(layers) - 2) + [1]
+    weights = random_weights(rng, layers, 0.6)
+    sig_linear, sig_weights = tanh_as_sigmoid(layers, linear, weights)
+    net = Network(s, layers, weights=sig_weights, linear=sig_linear)
+    x = quadrature_inputs(pts, t)
+    inp = Data(s, x, t)
+    y = net.eval(inp).to_numpy()
+    record = dict(table=t, points=pts, inputs=x, layers=np.array(layers), linear=np.array(linear), outputs=y)
+    if expression is None:
+        targets = (rng.normal(size=y.shape) * 0.1 + y).astype(np.float32)
+        mw = rng.uniform(0.5, 1.5, (layers[-1], len(t))).astype(np.float32)
+        cost = net.matching(inp, Data(s, targets, t), mw, chunk=chunk)
+        record.update(targets=targets, match_weights=mw)
+    else:
+        expr = Expression(expression, table=t, variables='xyz'[:t.shape[1] - 1], outputs='u', count=len(pts))
+        qw = np.full(len(pts), 1.0 / len(pts))
+        cost = net.integral(inp, expr, weights=qw, chunk=chunk)
+        record.update(quad_weights=qw, nodes=np.array(expr.nodes, np.int32), constants=np.array(expr.constants))
+    value, grads = net.evaluate([cost], gradient=True)
+    record['loss'] = np.float64(value)
+    for i, w in enumerate(weights):
+        record[f'w{i}'] = w
+    for i, g in enumerate(sigmoid_gradients_to_tanh(layers, linear, grads)):
+        record[f'g{i}'] = g
+    np.savez_compressed(OUT / f'{name}.npz', **record)
+    print(name, 'rows', len(t), 'loss', value)
+
+
+def tanh_cases(s):
+    rng = np.random.default_rng(20261202)
+    run_tanh(s, 'tanh_mixed2d_order4', rng, all_mixed(4, 'xy'), points_in(rng, 17, 2, -1, 1), [2, 12, 10, 2],
+             chunk=6)
+    run_tanh(s, 'tanh_biharmonic3d', rng, all_mixed(4, 'xyz'), points_in(rng, 11, 3), [3, 10, 8, 1],
+             expression='(u_xxxx+u_yyyy+u_zzzz+2*u_xxyy+2*u_xxzz+2*u_yyzz-1)**2', chunk=4)
+
+
+def main(exe, only=None):
+    if only == 'tanh':
+        with Session(exe) as s:
+            tanh_cases(s)
+        return
     rng = np.random.default_rng(20261201)
     with Session(exe) as s:
         grid = np.linspace(0, 1, 7)
@@ -153,7 +202,10 @@ def main(exe):
                      [6, 4, 3, 1], random_weights(rng, [6, 4, 3, 1], 0.6), rng)
         run_polynomial(s, 'pure4d_order6_polynomial', rng)
         run_integral(s, 'disk_poisson_integral', rng)
+        tanh_cases(s)
 
 
 if __name__ == '__main__':
-    main(sys.argv[1] if len(sys.argv) > 1 else ROOT / 'oracle' / '_ref' / 'cpde_ref_cpu_server')
+    args = [a for a in sys.argv[1:] if not a.startswith('--')]
+    main(args[0] if args else ROOT / 'oracle' / '_ref' / 'cpde_ref_cpu_server',
+         only='tanh' if '--only-tanh' in sys.argv else None)

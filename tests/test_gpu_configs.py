@@ -76,27 +76,29 @@ def test_config3_kernels(engine):
     """2 -> 64^3 -> 1 sigmoid, rows u, u_x, u_y, u_xx, u_yy, compiled integral
     of (u_xx + u_yy + 1)^2 over points in the disk."""
     w = bench.config3_workload(2048)
-    check(engine, w, ['input_forward', 'forward', 'output_forward', 'cost_integral', 'output_backward',
-                      'weight_gradient', 'backward', 'backward_input'], 1e-5)
+    check(engine, w, ['input_forward', 'forward', 'head_expression', 'weight_gradient', 'backward',
+                      'backward_input'], 1e-5)
 
 
 def test_config4_kernels(engine):
     """3 -> 256^3 -> 1 tanh (config 4's width, activation, rows and cost with
     two hidden layers fewer), the biharmonic residual integral over the 25-row
-    closure, several chunks."""
-    w = bench.config4_workload(256, chunk=100)
+    closure, two chunks of several column tiles per CTA."""
+    w = bench.config4_workload(2000, chunk=1100)
     w.layers = [3, 256, 256, 256, 1]
     w.linear = [1, 2, 2, 2, 1]
     w.weights = w.weights[:3] + w.weights[-1:]
-    check(engine, w, ['input_forward', 'cost_integral', 'output_backward'], 1e-4)
+    check(engine, w, ['input_forward', 'forward_wide', 'cost_integral', 'output_backward', 'weight_gradient_ws',
+                      'backward_wide', 'backward_input_wide'], 1e-4)
 
 
 def test_config5_kernels(engine):
     """4 -> 512^3 -> 1 sigmoid (config 5's width and rows with three hidden
     layers fewer), pure order-6 rows along 4 axes, polynomial residual with
-    per-point weights, several chunks."""
-    w = bench.config5_workload(200, chunk=96)
+    per-point weights, two chunks of several column tiles per CTA."""
+    w = bench.config5_workload(600, chunk=350)
     w.layers = [4, 512, 512, 512, 1]
     w.linear = [1, 0, 0, 0, 1]
     w.weights = w.weights[:3] + w.weights[-1:]
-    check(engine, w, ['input_forward', 'cost_polynomial', 'output_backward'], 1e-4)
+    check(engine, w, ['input_forward', 'forward_wide', 'cost_polynomial', 'output_backward', 'weight_gradient_ws',
+                      'backward_wide', 'backward_input_wide'], 1e-4)

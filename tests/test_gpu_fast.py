@@ -102,6 +102,77 @@ def test_fast_tier_wide_layers_and_single_output(engine):
     assert gc.layer_error(grads, expected) < 1e-4
 
 
+@pytest.mark.parametrize('sid', [8, 9, 10], ids=[codegen.SCHEMAS[i][0] for i in (8, 9, 10)])
+def test_tensor_tier_many_tiles_per_cta(engine, sid):
+    """Warp-specialised layers with several column tiles per CTA, for the
+    schemas whose backward ring has no more stages than a tile has K slabs
+    (25 and 35 rows at 128 neurons): one MMA issuer takes every tile there.
+    The network mixes 128-wide and 256-wide layers, so the wide kernels and
+    the wider weight gradient run the same way."""
+    rows = codegen.SCHEMAS[sid][1]
+    V = len(rows[0])
+    layers = [V, 128, 128, 256, 128, 1]
+    linear = [1, 0, 0, 0, 0, 1]
+    t, x, weights, net, data = setup(engine, rows, layers, linear, 1200, 60 + sid)
+    schema = jets.Schema(t[:, 1:])
+    pre, acts = jets.forward(schema, weights, layers, linear, x)
+    engine.set_tier(2)
+    try:
+        out = engine.download(engine.evaluate(net, data))
+        R = len(t)
+        tgt = engine.data(np.zeros_like(out), t)
+        cost = engine.matching(net, data, tgt, list(range(R)), list(range(R)), 1, np.ones((R, 1, 1), np.float32))
+        engine.timing(True)
+        engine.timing_report()
+        value, grads = engine.graph_evaluate(net, [cost], sum_graph(1))
+        report = engine.timing_report()
+    finally:
+        engine.timing(False)
+        engine.set_tier(0)
+    for k in ('forward_ws', 'forward_wide', 'backward_ws', 'backward_wide', 'weight_gradient_ws'):
+        assert k in report, (k, sorted(report))
+    assert gc.rowwise_error(out, acts[-1]).max() < 1e-4
+    loss, dout = jets.matching(acts[-1], np.zeros_like(out), 1.0)
+    expected = jets.backward(schema, weights, layers, linear, pre, acts, dout)
+    assert abs(value - loss) <= 1e-4 * loss
+    assert gc.layer_error(grads, expected) < 1e-4
+
+
+@pytest.mark.parametrize('sid', [2, 3, 7], ids=[codegen.SCHEMAS[i][0] for i in (2, 3, 7)])
+@pytest.mark.parametrize('width', [32, 64, 96])
+def test_tensor_tier_narrow_layers(engine, sid, width):
+    """Tensor-core (3xTF32) layers narrower than the 128-row tile: the rows
+    past the layer's width are zero weights, not stored. Orders <= 3, so the
+    exact-FP32 tolerance 1e-5 applies; several tiles per CTA."""
+    rows = codegen.SCHEMAS[sid][1]
+    layers = [2, width, width, width, 1]
+    linear = [1, 0, 0, 0, 1]
+    t, x, weights, net, data = setup(engine, rows, layers, linear, 4000, 80 + sid + width)
+    schema = jets.Schema(t[:, 1:])
+    pre, acts = jets.forward(schema, weights, layers, linear, x)
+    R = len(t)
+    targets = (acts[-1] * 0.5).astype(np.float32)
+    tgt = engine.data(targets, t)
+    cost = engine.matching(net, data, tgt, list(range(R)), list(range(R)), 1, np.ones((R, 1, 1), np.float32))
+    engine.set_tier(2)
+    try:
+        out = engine.download(engine.evaluate(net, data))
+        engine.timing(True)
+        engine.timing_report()
+        value, grads = engine.graph_evaluate(net, [cost], sum_graph(1))
+        report = engine.timing_report()
+    finally:
+        engine.timing(False)
+        engine.set_tier(0)
+    for k in ('forward_ws', 'backward_ws', 'backward_input_ws', 'weight_gradient_ws'):
+        assert k in report, (k, sorted(report))
+    assert gc.rowwise_error(out, acts[-1]).max() < 1e-5
+    loss, dout = jets.matching(acts[-1], targets, 1.0)
+    expected = jets.backward(schema, weights, layers, linear, pre, acts, dout)
+    assert abs(value - loss) <= 1e-5 * abs(loss)
+    assert gc.layer_error(grads, expected) < 1e-5
+
+
 @pytest.mark.parametrize('sid', [2, 6])
 @pytest.mark.parametrize('width,outputs', [(32, 1), (64, 3), (96, 2), (128, 3)])
 def test_output_layer_widths(engine, sid, width, outputs):
