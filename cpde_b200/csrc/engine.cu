@@ -954,23 +954,40 @@ void Engine::floor_steps(NetRecord& n, float value) {
                                                       value));
 }
 
-void Engine::optimizer_step(NetRecord& n, int method) {
+AdamStep Engine::adam_step(NetRecord& n, int step) {
+    return AdamStep{n.learning_rate, 0.9f, 0.999f, std::pow(0.9f, float(step)), std::pow(0.999f, float(step))};
+}
+
+// Gradient statistics, the update gate and the optimizer update in one launch
+// (k_inspect_update), then one download of the cost totals, the statistics
+// and the gate's decision. The caller validates with the reference's rules
+// and messages and commits the host side of the update with commit_update.
+bool Engine::inspect_and_update(NetRecord& n, int method, int costs, GraphRecord* g) {
     n.opt_layers.upload(opt_table(n), stream);
-    int widest = *std::max_element(n.count.begin(), n.count.end());
-    dim3 grid(grid_for(widest, 256, 256), n.layers);
-    if (method == 0) {
-        CPDE_RUN(*this, "rprop",
-                 k_rprop<<<grid, 256, 0, stream>>>(n.bank[0].ptr, n.bank[1].ptr, n.bank[2].ptr, n.bank[3].ptr,
-                                                   n.opt_layers.ptr));
+    n.update_applied.reserve(1);
+    n.host_applied.reserve(1);
+    require(method == 0 || n.adam_step < uint64_t(INT_MAX), "Adam counter exceeds supported range");
+    const int* graph_bad =
+        g ? reinterpret_cast<const int*>(reinterpret_cast<const char*>(g->summary.ptr) +
+                                         offsetof(GraphRecord::Summary, bad_node))
+          : nullptr;
+    CPDE_RUN(*this, "inspect_update",
+             k_inspect_update<<<1, 1024, 0, stream>>>(n.bank[0].ptr, n.bank[1].ptr, n.bank[2].ptr, n.bank[3].ptr,
+                                                      n.opt_layers.ptr, n.layers, n.grad_totals.ptr,
+                                                      n.cost_totals.ptr, costs, graph_bad, method,
+                                                      adam_step(n, int(n.adam_step + 1)), n.update_applied.ptr));
+    CPDE_CUDA(cudaMemcpyAsync(n.host_applied.ptr, n.update_applied.ptr, sizeof(int), cudaMemcpyDeviceToHost, stream));
+    download(n, costs, n.layers);
+    return n.host_applied.ptr[0] != 0;
+}
+
+// Host side of an update that k_inspect_update applied: RPROP's gradient
+// history alternates banks, Adam counts its step.
+void Engine::commit_update(NetRecord& n, int method) {
+    if (method == 0)
         for (int l = 0; l < n.layers; ++l) n.active[l] = 3 - n.active[l];
-    } else {
-        require(n.adam_step < uint64_t(INT_MAX), "Adam counter exceeds supported range");
-        int step = int(++n.adam_step);
-        float b1t = std::pow(0.9f, float(step)), b2t = std::pow(0.999f, float(step));
-        CPDE_RUN(*this, "adam",
-                 k_adam<<<grid, 256, 0, stream>>>(n.bank[0].ptr, n.bank[1].ptr, n.bank[2].ptr, n.bank[3].ptr,
-                                                  n.opt_layers.ptr, n.learning_rate, 0.9f, 0.999f, b1t, b2t));
-    }
+    else
+        ++n.adam_step;
 }
 
 Payload Engine::metadata(NetRecord& n) {
@@ -1414,8 +1431,7 @@ void Engine::train(Payload& b, bool graph_mode, const EventSink& emit, const vol
             reduce_gradient(n, nullptr);
             reduce_costs(n, ids);
         }
-        inspect_gradients(n, nullptr);
-        download(n, int(ids.size()), n.layers);
+        const bool applied = inspect_and_update(n, method, int(ids.size()), graph.get());
         bool bad_gradient = false;
         for (int i = 0; i < n.layers; ++i) bad_gradient = bad_gradient || n.host_grads.ptr[i].nonfinite != 0;
         if (bad_gradient || (diagnostics && ((completed + 1) % diagnostics == 0 || completed + 1 == epochs)))
@@ -1430,8 +1446,8 @@ void Engine::train(Payload& b, bool graph_mode, const EventSink& emit, const vol
                                        ", flattened index " + std::to_string(g.first_nonfinite) +
                                        "; no optimizer update performed for this iteration");
             }
-        optimizer_step(n, method);
-        CPDE_CUDA(cudaStreamSynchronize(stream));
+        if (!applied) throw DeviceError("internal error: the device update gate refused an update validation accepts");
+        commit_update(n, method);
         ++completed;
         ++n.updates;
         ++n.stage_done;

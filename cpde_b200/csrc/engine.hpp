@@ -126,6 +126,8 @@ struct NetRecord {
     PinnedBuffer<CostStats> host_costs;
     PinnedBuffer<GradStats> host_grads;
     DeviceBuffer<OptLayer> opt_layers;
+    DeviceBuffer<int> update_applied;  // decision of the fused update's gate
+    PinnedBuffer<int> host_applied;
 
     float* weights(int l) { return bank[0].ptr + offset[l]; }
     float* gradient(int l) { return bank[active[l]].ptr + offset[l]; }
@@ -251,7 +253,9 @@ class Engine {
     void reset_optimizer(NetRecord& n, int method);
     void set_steps(NetRecord& n, float value);
     void floor_steps(NetRecord& n, float value);
-    void optimizer_step(NetRecord& n, int method);
+    AdamStep adam_step(NetRecord& n, int step);
+    bool inspect_and_update(NetRecord& n, int method, int costs, GraphRecord* g);
+    void commit_update(NetRecord& n, int method);
     Payload metadata(NetRecord& n);
     void gradient_report(NetRecord& n, uint64_t epoch, const EventSink& emit);
     void report_values(NetRecord& n, uint64_t completed, int after, const std::vector<double>& values,

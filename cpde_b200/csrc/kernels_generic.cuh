@@ -491,9 +491,9 @@ static __global__ void k_inspect_gradients(const float* const* __restrict__ grad
 }
 
 // ---------------------------------------------------------------------------
-// Optimizers over every layer in one launch; blockIdx.y = layer. Banks hold
-// the flat parameters of all layers: 0 weights, 1/2 gradient history,
-// 3 RPROP steps or Adam first moment.
+// Optimizers over every layer. Banks hold the flat parameters of all layers:
+// 0 weights, 1/2 gradient history, 3 RPROP steps or Adam first moment; an
+// OptLayer gives a layer's offset, size and current-gradient bank.
 
 struct OptLayer {
     long offset;
@@ -503,54 +503,101 @@ struct OptLayer {
 
 // RPROP (cuda/derivative_kernels_v4.cu:752-778): grow x1.2 on agreeing signs,
 // roll back and halve on a sign change, |W| <= 20 guard restarting at 0.1.
-static __global__ void k_rprop(float* __restrict__ w, float* __restrict__ bank1, float* __restrict__ bank2,
-                        float* __restrict__ steps, const OptLayer* __restrict__ layers) {
-    const OptLayer L = layers[blockIdx.y];
-    float* cur = (L.active == 1 ? bank1 : bank2) + L.offset;
-    float* prev = (L.active == 1 ? bank2 : bank1) + L.offset;
-    float* W = w + L.offset;
-    float* D = steps + L.offset;
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < L.count; i += blockDim.x * gridDim.x) {
-        float a = cur[i], b = prev[i], d = D[i], wi = W[i];
-        if (a * b > 0) d *= 1.2f;
-        float nw = wi - copysignf(d, a);
-        if (a * b < 0) {
-            wi += copysignf(d, b);
-            d *= 0.5f;
+// One RPROP element: current gradient cur[i], previous prev[i], step D[i],
+// weight W[i].
+__device__ __forceinline__ void rprop_element(float* cur, const float* prev, float* D, float* W, int i) {
+    float a = cur[i], b = prev[i], d = D[i], wi = W[i];
+    if (a * b > 0) d *= 1.2f;
+    float nw = wi - copysignf(d, a);
+    if (a * b < 0) {
+        wi += copysignf(d, b);
+        d *= 0.5f;
+        cur[i] = 0.0f;
+    } else if (a != 0.0f) {
+        if (fabsf(nw) <= 20.0f) wi = nw;
+        else {
+            d = 0.1f;
             cur[i] = 0.0f;
-        } else if (a != 0.0f) {
-            if (fabsf(nw) <= 20.0f) wi = nw;
-            else {
-                d = 0.1f;
-                cur[i] = 0.0f;
-            }
         }
-        W[i] = wi;
-        D[i] = d;
     }
+    W[i] = wi;
+    D[i] = d;
 }
 
-// Adam (cuda/derivative_kernels_v4.cu:780-799), including the reference's
-// double-precision denominator from the 1e-8 literal.
-static __global__ void k_adam(float* __restrict__ w, float* __restrict__ bank1, float* __restrict__ bank2,
-                       float* __restrict__ first, const OptLayer* __restrict__ layers, float alpha, float beta1,
-                       float beta2, float beta1t, float beta2t) {
-    const OptLayer L = layers[blockIdx.y];
-    const float* grad = (L.active == 1 ? bank1 : bank2) + L.offset;
-    float* V = (L.active == 1 ? bank2 : bank1) + L.offset;
-    float* M = first + L.offset;
-    float* W = w + L.offset;
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < L.count; i += blockDim.x * gridDim.x) {
-        float g = grad[i];
-        float m = __fadd_rn(__fmul_rn(beta1, M[i]), __fmul_rn(1 - beta1, g));
-        float v = __fadd_rn(__fmul_rn(beta2, V[i]), __fmul_rn(__fmul_rn(1 - beta2, g), g));
-        M[i] = m;
-        V[i] = v;
-        float mh = __fdiv_rn(m, 1 - beta1t);
-        float vh = __fdiv_rn(v, 1 - beta2t);
-        double step = double(__fmul_rn(alpha, mh)) / (double(sqrtf(vh)) + 1e-8);
-        float nw = float(double(W[i]) - step);
-        if (fabsf(nw) <= 20.0f) W[i] = nw;
+// One Adam element (cuda/derivative_kernels_v4.cu:780-799), including the
+// reference's double-precision denominator from the 1e-8 literal.
+struct AdamStep {
+    float alpha, beta1, beta2, beta1t, beta2t;
+};
+__device__ __forceinline__ void adam_element(const float* grad, float* V, float* M, float* W, int i, AdamStep s) {
+    float g = grad[i];
+    float m = __fadd_rn(__fmul_rn(s.beta1, M[i]), __fmul_rn(1 - s.beta1, g));
+    float v = __fadd_rn(__fmul_rn(s.beta2, V[i]), __fmul_rn(__fmul_rn(1 - s.beta2, g), g));
+    M[i] = m;
+    V[i] = v;
+    float mh = __fdiv_rn(m, 1 - s.beta1t);
+    float vh = __fdiv_rn(v, 1 - s.beta2t);
+    double step = double(__fmul_rn(s.alpha, mh)) / (double(sqrtf(vh)) + 1e-8);
+    float nw = float(double(W[i]) - step);
+    if (fabsf(nw) <= 20.0f) W[i] = nw;
+}
+
+// The training update with its gradient diagnostics in one launch (one block
+// of 1024 threads): each layer's statistics (squared L2 norm, max |g|,
+// non-finite count and first index; cuda/reduction_kernels.cuh:81-98) into
+// totals[layer], then the gate the host applies before an update (every
+// gradient finite, every cost total finite with no bad sample, no bad graph
+// node), then the RPROP or Adam update of every layer only if the gate
+// passes. *applied records the decision for the host, which validates the
+// downloaded statistics with the same rules and reports the reference's
+// messages when the gate failed. method: 0 RPROP, 1 Adam.
+static __global__ void __launch_bounds__(1024) k_inspect_update(float* __restrict__ w, float* __restrict__ bank1,
+                                                                float* __restrict__ bank2, float* __restrict__ bank3,
+                                                                const OptLayer* __restrict__ layers, int count,
+                                                                GradStats* __restrict__ totals,
+                                                                const CostStats* __restrict__ costs, int cost_count,
+                                                                const int* __restrict__ graph_bad, int method,
+                                                                AdamStep adam, int* __restrict__ applied) {
+    __shared__ int gate;
+    if (threadIdx.x == 0) gate = 1;
+    __syncthreads();
+    for (int l = 0; l < count; ++l) {
+        const OptLayer L = layers[l];
+        const float* g = (L.active == 1 ? bank1 : bank2) + L.offset;
+        GradStats local = grad_empty();
+        for (int i = threadIdx.x; i < L.count; i += blockDim.x) {
+            double v = g[i];
+            if (!isfinite(v)) {
+                ++local.nonfinite;
+                if (i < local.first_nonfinite) local.first_nonfinite = i;
+            } else {
+                local.squared_norm += v * v;
+                double a = fabs(v);
+                if (a > local.max_abs) local.max_abs = a;
+            }
+        }
+        GradStats b = block_reduce(local, grad_empty);
+        if (threadIdx.x == 0) {
+            totals[l] = b;
+            if (b.nonfinite) gate = 0;
+        }
+    }
+    if (threadIdx.x == 0) {
+        for (int c = 0; c < cost_count; ++c)
+            if (costs[c].bad_sample != INT_MAX || !isfinite(costs[c].value)) gate = 0;
+        if (graph_bad && *graph_bad >= 0) gate = 0;
+        *applied = gate;
+    }
+    __syncthreads();
+    if (!gate) return;
+    for (int l = 0; l < count; ++l) {
+        const OptLayer L = layers[l];
+        float* cur = (L.active == 1 ? bank1 : bank2) + L.offset;
+        float* other = (L.active == 1 ? bank2 : bank1) + L.offset;
+        for (int i = threadIdx.x; i < L.count; i += blockDim.x) {
+            if (method == 0) rprop_element(cur, other, bank3 + L.offset, w + L.offset, i);
+            else adam_element(cur, other, bank3 + L.offset, w + L.offset, i, adam);
+        }
     }
 }
 

@@ -680,23 +680,46 @@ __global__ void __launch_bounds__(THREADS, 1) k_backward_wide(const __grid_const
 // raw operand (its hi part) as the MN-major B operand, so shared memory
 // carries each operand once per MMA term instead of also serving the A side.
 // Two MMA issuers take the even and the odd stages, each into its own
-// 128 x 128 accumulator, which stay in tensor memory for the whole kernel and
-// are summed in the epilogue. grid = (CTAs, N / 128, M / 128): CTAs that share
-// blockIdx.x take the same chunks at about the same time, so the slices of
-// dZ and Y_prev that several of them read come from L2.
+// 128 x 128 accumulator. The tensor core's FP32 accumulation does not round to
+// nearest, so a sum over thousands of column chunks in one accumulator drifts
+// (measured: 6e-4 normwise on config 5's gradients against the float64
+// oracle); each accumulator therefore sums only kWgSegment of its issuer's
+// chunks before four drain warps fold it into a round-to-nearest FP32 sum in
+// shared memory and release it. The second issuer's segments are offset by
+// half a segment, so the two drains do not stall both issuers at once.
+// grid = (CTAs, N / 128, M / 128): CTAs that share blockIdx.x take the same
+// chunks at about the same time, so the slices of dZ and Y_prev that several
+// of them read come from L2.
 
-constexpr int kWgStages = 4;
+constexpr int kWgStages = 3;
+constexpr int kWgSegment = 16;            // chunks one accumulator sums before a drain
 constexpr int kWgBox = 32 * 32 * 4;       // 32 neurons x 32 columns
 constexpr int kWgOperand = 4 * kWgBox;    // 128 neurons
 constexpr int kWgStage = 3 * kWgOperand;  // dZ raw, Y raw (= hi), Y lo
-constexpr int kWgSmem = kWgStages * kWgStage + 1024 + 256;
-constexpr int kWgEpilogueWarp = 6, kWgSecondMmaWarp = 10;
-constexpr int kWgThreads = 352;  // producer, MMA, 4 split warps, 4 epilogue warps, second MMA issuer
+constexpr int kWgSums = 128 * 128 * 4;    // FP32 sums [column n][neuron m]
+constexpr int kWgSmem = kWgStages * kWgStage + kWgSums + 1024 + 256;
+constexpr int kWgEpilogueWarp = 6, kWgSecondMmaWarp = 10, kWgDrainWarp = 11;
+constexpr int kWgThreads = 480;  // producer, MMA, 4 split warps, 4 lo warps, second MMA issuer, 4 drain warps
 constexpr uint32_t kWgAccColumns = 128, kWgTmemColumns = 512, kWgSecondAcc = 384;
 
 // element (mn, k) of such an operand, in floats from its start
 __device__ __forceinline__ int mn32_index(int mn, int k) {
     return (mn >> 5) * (kWgBox / 4) + k * 32 + ((((mn & 31) >> 3) ^ (k & 3)) << 3) + (mn & 7);
+}
+
+// Segment k of issuer w holds its chunks [start, start + length): issuer 1's
+// first segment is half as long.
+__device__ __forceinline__ int wg_segment_length(int w, int k) { return k == 0 && w ? kWgSegment / 2 : kWgSegment; }
+__device__ __forceinline__ int wg_segments(int w, int count) {
+    if (count <= 0) return 0;
+    const int first = wg_segment_length(w, 0);
+    return count <= first ? 1 : 1 + (count - first + kWgSegment - 1) / kWgSegment;
+}
+// ring index of the last chunk of segment k of issuer w (of `count` chunks)
+__device__ __forceinline__ int wg_segment_end(int w, int k, int count) {
+    const int first = wg_segment_length(w, 0);
+    const int last_local = min(count, k == 0 ? first : first + k * kWgSegment) - 1;
+    return 2 * last_local + w;
 }
 
 static __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_constant__ CUtensorMap map_dz,
@@ -705,9 +728,11 @@ static __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_
                                                             int* error) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* bars = reinterpret_cast<uint64_t*>(base + kWgStages * kWgStage);
+    float* sums = reinterpret_cast<float*>(base + kWgStages * kWgStage);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(base + kWgStages * kWgStage + kWgSums);
     uint64_t *full = bars, *split = bars + kWgStages, *empty = bars + 2 * kWgStages, *drain = bars + 3 * kWgStages;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    uint64_t *acc_full = drain + 1, *acc_empty = acc_full + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -717,6 +742,10 @@ static __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_
             tc::mbar_init(empty + s, 1);
         }
         tc::mbar_init(drain, 2);  // one commit per MMA issuer
+        for (int w = 0; w < 2; ++w) {
+            tc::mbar_init(acc_full + w, 1);   // the issuer's commit at a segment's end
+            tc::mbar_init(acc_empty + w, 4);  // the four drain warps
+        }
         *abort = 0;
         tc::fence_barrier_init();
     }
@@ -733,9 +762,10 @@ static __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_
     // streams through one region of both operands at a time
     const long total_chunks = (columns + 31) / 32;
     const int chunks = blockIdx.x < total_chunks ? int((total_chunks - 1 - blockIdx.x) / gridDim.x + 1) : 0;
+    const int mine[2] = {(chunks + 1) / 2, chunks / 2};  // chunks of issuer 0 (even) and 1 (odd)
     auto chunk_start = [&](int it) { return 32L * ((long)blockIdx.x + (long)it * gridDim.x); };
-    // stage st: [dZ raw][Y raw = hi][Y lo]; tensor memory: G of the even chunks [0, 128), stage st's dZ hi/lo at
-    // 128 + 64 st (+32), G of the odd chunks [384, 512)
+    // stage st: [dZ raw][Y raw = hi][Y lo]; tensor memory: issuer 0's accumulator [0, 128), stage st's dZ hi/lo
+    // at 128 + 64 st (+32), issuer 1's accumulator [384, 512)
     auto stage_ptr = [&](int st, int part) { return reinterpret_cast<float*>(base + st * kWgStage + part * kWgOperand); };
     auto dz_column = [](int st) { return kWgAccColumns + 64u * uint32_t(st); };
     float* out = partials + (size_t)blockIdx.x * M * (N + 1);
@@ -761,7 +791,16 @@ static __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_
             constexpr uint32_t idesc = tc::idesc_tf32(128, 128) | (1u << 16);  // B (Y) MN-major, A (dZ) from TMEM
             const int which = warp == kMmaWarp ? 0 : 1;
             const uint32_t acc = which ? tmem + kWgSecondAcc : tmem;
-            for (int it = which; it < chunks; it += 2) {
+            int seg = 0, in_seg = 0;
+            bool ok = true;
+            for (int it = which; ok && it < chunks; it += 2) {
+                if (in_seg == wg_segment_length(which, seg)) {
+                    // the drain warps have folded the previous segment out of the accumulator
+                    ok = tc::mbar_wait_or_abort(acc_empty + which, seg & 1, tcg::kWaitCycles, abort);
+                    if (!ok) break;
+                    ++seg;
+                    in_seg = 0;
+                }
                 const int st = it % kWgStages;
                 if (!tc::mbar_wait_or_abort(split + st, (it / kWgStages) & 1, tcg::kWaitCycles, abort)) break;
                 tc::tc_fence_after();
@@ -771,11 +810,13 @@ static __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_
                 for (int kk = 0; kk < 4; ++kk) {
                     const uint32_t off = kk * 1024;  // 8 columns of Y
                     tc::mma_tf32_ts(acc, al + kk * 8, tc::desc_mn32_sw128(yh + off, kWgBox), idesc,
-                                    it != which || kk != 0);
+                                    in_seg != 0 || kk != 0);
                     tc::mma_tf32_ts(acc, ah + kk * 8, tc::desc_mn32_sw128(yl + off, kWgBox), idesc, 1);
                     tc::mma_tf32_ts(acc, ah + kk * 8, tc::desc_mn32_sw128(yh + off, kWgBox), idesc, 1);
                 }
                 tc::mma_commit(empty + st);
+                ++in_seg;
+                if (in_seg == wg_segment_length(which, seg) || it + 2 >= chunks) tc::mma_commit(acc_full + which);
             }
             tc::mma_commit(drain);
             if (!tc::mbar_wait(drain, 0, tcg::kWaitCycles)) *abort = 1;
@@ -814,12 +855,11 @@ static __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_
             if (lane == 0) tc::mbar_arrive(split + st);
         }
         if (blockIdx.y == 0 && m_base + m < M) out[(size_t)N * M + m_base + m] = bias;
-    } else {
-        // epilogue warps: the TF32 lo part of Y_prev of every stage (the raw
-        // operand is its hi part; the columns past the end of the data arrive
-        // as zeros from the tensor map), then write the sum of the two
-        // accumulators (lane m, column n) into the partial
-        const int quarter = warp & 3, m = quarter * 32 + lane, tid = threadIdx.x - kWgEpilogueWarp * 32;
+    } else if (warp < kWgDrainWarp) {
+        // lo warps: the TF32 lo part of Y_prev of every stage (the raw operand
+        // is its hi part; the columns past the end of the data arrive as zeros
+        // from the tensor map)
+        const int tid = threadIdx.x - kWgEpilogueWarp * 32;
         for (int it = 0; it < chunks; ++it) {
             const int st = it % kWgStages;
             if (!warp_wait(full + st, (it / kWgStages) & 1, abort)) break;
@@ -829,22 +869,38 @@ static __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(split + st);
         }
-        if (warp_wait(drain, 0, abort)) {
+    } else {
+        // drain warps: thread = neuron m (its TMEM lane); every finished segment of
+        // either accumulator, in the order the segments end, added into sums[n][m]
+        const int quarter = warp & 3, m = quarter * 32 + lane;
+        const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
+        for (int c = 0; c < 128; ++c) sums[c * 128 + m] = 0.f;
+        const int total[2] = {wg_segments(0, mine[0]), wg_segments(1, mine[1])};
+        int next[2] = {0, 0};
+        bool ok = true;
+        while (ok && (next[0] < total[0] || next[1] < total[1])) {
+            int w;
+            if (next[0] >= total[0]) w = 1;
+            else if (next[1] >= total[1]) w = 0;
+            else w = wg_segment_end(0, next[0], mine[0]) < wg_segment_end(1, next[1], mine[1]) ? 0 : 1;
+            ok = warp_wait(acc_full + w, next[w] & 1, abort);
+            if (!ok) break;
             tc::tc_fence_after();
-            const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
+            const uint32_t acc = lane_base + (w ? kWgSecondAcc : 0u);
             for (int c0 = 0; c0 < 128; c0 += 16) {
-                float v[16], odd[16];
+                float v[16];
+                tc::tmem_read<16>(acc + c0, v);
 #pragma unroll
-                for (int j = 0; j < 16; ++j) v[j] = odd[j] = 0.f;
-                if (chunks > 0) tc::tmem_read<16>(lane_base + c0, v);
-                if (chunks > 1) tc::tmem_read<16>(lane_base + kWgSecondAcc + c0, odd);
-#pragma unroll
-                for (int j = 0; j < 16; ++j) v[j] += odd[j];
-#pragma unroll
-                for (int j = 0; j < 16; ++j)  // the slices of layers narrower than 128 neurons end early
-                    if (m_base + m < M && n_base + c0 + j < N) out[m_base + m + (size_t)(n_base + c0 + j) * M] = v[j];
+                for (int j = 0; j < 16; ++j) sums[(c0 + j) * 128 + m] += v[j];
             }
+            tc::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(acc_empty + w);
+            ++next[w];
         }
+        if (ok)
+            for (int c = 0; c < 128; ++c)  // the slices of layers narrower than 128 neurons end early
+                if (m_base + m < M && n_base + c < N) out[m_base + m + (size_t)(n_base + c) * M] = sums[c * 128 + m];
     }
     tc::tc_fence_before();
     __syncthreads();

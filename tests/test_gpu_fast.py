@@ -138,6 +138,35 @@ def test_tensor_tier_many_tiles_per_cta(engine, sid):
     assert gc.layer_error(grads, expected) < 1e-4
 
 
+@pytest.mark.parametrize('width', [128, 512])
+def test_tensor_weight_gradient_over_many_columns(engine, width):
+    """The tensor-core weight gradient sums hundreds of thousands of columns
+    per layer; its accumulators are folded into round-to-nearest FP32 sums
+    every few chunks, so the result stays as close to the exact-FP32 FFMA
+    kernels' as a short sum would (without the folding the drift grew with
+    the column count: 3e-5 on config 2, 6e-4 on config 5). Order 3 (tier 0
+    runs FFMA there), 65,536 and 16,384 points."""
+    rows = codegen.SCHEMAS[3][1]
+    layers = [2, width, width, width, 1]
+    linear = [1, 0, 0, 0, 1]
+    P = 65536 if width == 128 else 16384
+    t, x, weights, net, data = setup(engine, rows, layers, linear, P, 5)
+    R = len(t)
+    tgt = engine.data(np.zeros((R, 1, P), np.float32), t)
+    cost = engine.matching(net, data, tgt, list(range(R)), list(range(R)), 1, np.ones((R, 1, 1), np.float32))
+    exact_value, exact = engine.graph_evaluate(net, [cost], sum_graph(1))
+    engine.set_tier(2)
+    try:
+        value, grads = engine.graph_evaluate(net, [cost], sum_graph(1))
+    finally:
+        engine.set_tier(0)
+    err = [float(np.linalg.norm(a.astype(np.float64) - b) / np.linalg.norm(b)) for a, b in zip(grads, exact)]
+    assert abs(value - exact_value) <= 1e-5 * abs(exact_value)
+    # what remains is the GEMMs' own 3xTF32 error (accumulation over K = 512
+    # inputs in the wide layers), not the length of the column sums
+    assert max(err) < (5e-6 if width == 128 else 2e-5), err
+
+
 @pytest.mark.parametrize('sid', [2, 3, 7], ids=[codegen.SCHEMAS[i][0] for i in (2, 3, 7)])
 @pytest.mark.parametrize('width', [32, 64, 96])
 def test_tensor_tier_narrow_layers(engine, sid, width):
