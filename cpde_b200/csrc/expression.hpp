@@ -206,7 +206,7 @@ template <int SID> struct StaticJet;
 // points per round, whose programs PB threads of the lane evaluate at once,
 // so a round's two barriers serve LANES * PB points.
 static const char* kHeadKernel = R"HEAD(
-extern "C" __global__ void __launch_bounds__(128) cpde_head(
+extern "C" __global__ void __launch_bounds__(128, 4) cpde_head(
     int K, int points, int offset, int samples, const float* __restrict__ W, const float* __restrict__ Y,
     float* __restrict__ dZ, const double* __restrict__ fields, const double* __restrict__ weights,
     const double* __restrict__ multiplier, int collect, float* __restrict__ partials,
@@ -291,9 +291,10 @@ extern "C" __global__ void __launch_bounds__(128) cpde_head(
 }
 )HEAD";
 
-// Points per lane and round of the head: up to 8, while PB * R jet values
-// stay within about 40 registers.
-inline int head_points_per_lane(int R) { return std::max(1, std::min(8, 40 / R)); }
+// Points per lane and round of the head: up to 4, while PB * R jet values
+// stay within about 20 registers, so that four CTAs fit an SM (at 8 points
+// per lane the head took 255 registers and ran at 12% of the SM's warps).
+inline int head_points_per_lane(int R) { return std::max(1, std::min(4, 20 / R)); }
 
 inline std::string expression_head_source(const std::vector<ScalarNode>& nodes, const char* jet_source, int sid,
                                           bool tanh_act, int R, int O, int K) {

@@ -502,7 +502,15 @@ __device__ __forceinline__ void produce_wide(const Ring& r, float* a_hi, float* 
 }
 
 // MMA issuer of the wide layers: issue_mmas with A (hi, lo) from the stage's
-// weight slabs in shared memory.
+// weight slabs in shared memory. With no weights in tensor memory each tile
+// has two accumulators: hi*hi in columns [256 a, 256 a + 128) and the two
+// small lo terms in the next 128. The tensor core's FP32 accumulation does
+// not round to nearest, so each add costs up to an ulp of the accumulator;
+// the large accumulator then takes a third of the adds, and the epilogue sums
+// the pair in IEEE FP32 (measured: the wide layers' output error falls with
+// it).
+__host__ __device__ constexpr uint32_t wide_accumulator(int a) { return uint32_t(a) * 256u; }
+
 template <int N, int SLAB, int S>
 __device__ __forceinline__ void issue_mmas_wide(const Ring& r, const float* a_hi, const float* a_lo, uint32_t tmem,
                                                 long tiles, int slabs, int which) {
@@ -515,7 +523,7 @@ __device__ __forceinline__ void issue_mmas_wide(const Ring& r, const float* a_hi
         const int a = local & 1;
         ok = tc::mbar_wait_or_abort(r.acc_empty + a, ((local >> 1) & 1) ^ 1, tcg::kWaitCycles, r.abort);
         tc::tc_fence_after();
-        const uint32_t d = tmem + kAccColumn + a * 128;
+        const uint32_t d = tmem + wide_accumulator(a), d_lo = d + 128;
         for (int s = 0; ok && s < slabs; ++s, ++it) {
             const int st = it % S;
             ok = tc::mbar_wait_or_abort(r.split + st, (it / S) & 1, tcg::kWaitCycles, r.abort);
@@ -527,9 +535,9 @@ __device__ __forceinline__ void issue_mmas_wide(const Ring& r, const float* a_hi
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
                 const uint32_t off = kk * 32;  // 8 TF32 values along the 128-byte rows
-                tc::mma_tf32(d, tc::desc_k_sw128(al + off), tc::desc_k_sw128(bh + off), idesc, (s | kk) != 0);
-                tc::mma_tf32(d, tc::desc_k_sw128(ah + off), tc::desc_k_sw128(bl + off), idesc, 1);
-                tc::mma_tf32(d, tc::desc_k_sw128(ah + off), tc::desc_k_sw128(bh + off), idesc, 1);
+                tc::mma_tf32(d_lo, tc::desc_k_sw128(al + off), tc::desc_k_sw128(bh + off), idesc, (s | kk) != 0);
+                tc::mma_tf32(d_lo, tc::desc_k_sw128(ah + off), tc::desc_k_sw128(bl + off), idesc, 1);
+                tc::mma_tf32(d, tc::desc_k_sw128(ah + off), tc::desc_k_sw128(bh + off), idesc, (s | kk) != 0);
             }
             tc::mma_commit(r.empty + st);
         }
@@ -580,7 +588,10 @@ __global__ void __launch_bounds__(THREADS, 1) k_forward_wide(const __grid_consta
             for (int p = group; p < T::PTS; p += kEpilogueGroups) {
                 if (p0 + p >= P) break;
                 float z[R], y[R];
-                tc::tmem_read<R>(lane_base + kAccColumn + a * 128 + p * R, z);
+                tc::tmem_read<R>(lane_base + wide_accumulator(a) + p * R, z);
+                tc::tmem_read<R>(lane_base + wide_accumulator(a) + 128 + p * R, y);  // the lo terms
+#pragma unroll
+                for (int q = 0; q < R; ++q) z[q] += y[q];
                 z[0] += b0;
                 StaticJet<SID>::template forward<Act>(z, y);
                 float* out = Y + ((size_t)(p0 + p) * R) * M + m;
@@ -643,7 +654,13 @@ __global__ void __launch_bounds__(THREADS, 1) k_backward_wide(const __grid_const
                 const float* yp = Yprev + ((size_t)(p0 + p) * R) * N + n;
 #pragma unroll
                 for (int q = 0; q < R; ++q) y[q] = __ldg(yp + (size_t)q * N);
-                tc::tmem_read<R>(lane_base + kAccColumn + a * 128 + p * R, g);
+                {
+                    float lo[R];
+                    tc::tmem_read<R>(lane_base + wide_accumulator(a) + p * R, g);
+                    tc::tmem_read<R>(lane_base + wide_accumulator(a) + 128 + p * R, lo);  // the lo terms
+#pragma unroll
+                    for (int q = 0; q < R; ++q) g[q] += lo[q];
+                }
                 StaticJet<SID>::template adjoint<Act>(y, g);
                 if (INPUT_GRAD) {
                     fast::input_gradient<R>(g, X0 + (size_t)(p0 + p) * R * K0, K0, gacc);
