@@ -144,24 +144,47 @@ def hbm_roofline(kernels, steps, points, rows, peaks, source):
     return roofline, rows_out
 
 
-def cpu_baseline(points=128, steps=2):
-    """Reference CPU server (built from the reference's own sources) on a
-    bounded sample of the same workload; serial engine, 1 core."""
+def cpu_baseline(points=128, steps=2, processes=None):
+    """Reference CPU server (built from the reference's own sources; this
+    image has no system CBLAS, so its CMake default CPDE_CPU_BLAS=AUTO would
+    also pick the portable serial BLAS) on a bounded sample of the same
+    workload. The server is single-threaded, so it uses the host's cores the
+    way the path shards: one server process per core, each on its own
+    `points`-point slice, all running their op-90 epochs at once; the
+    throughput is the sum over processes (capped at 64 processes)."""
     exe = ROOT / 'oracle' / '_ref' / 'cpde_ref_cpu_server'
     if not exe.exists():
         return None
+    import threading
     from cpde_b200.client import Data, Network, Session
-    t, x, targets, weights = workload(points)
-    with Session(exe) as s:
-        net = Network(s, LAYERS, weights=weights)
-        inp = Data(s, x, t)
-        tgt = Data(s, targets, t)
-        cost = net.matching(inp, tgt, np.ones((1, len(t)), np.float32))
-        wall, _, _, _ = net.benchmark(cost, warm=0, iterations=1, batches=steps)
-    ms = float(np.median(wall))
-    return dict(value=points * len(t) / (ms / 1000), unit=UNIT, cores=1, kind='reference',
-                sample=f'{points} of the {POINTS} points, {steps} op-90 epochs, median; '
-                       'cpde_ref_cpu_server (oracle/Makefile), serial CPU backend',
+    if processes is None:
+        processes = max(1, min(64, len(os.sched_getaffinity(0))))
+    t, x, targets, weights = workload(points * processes)
+    R = len(t)
+    start = threading.Barrier(processes)
+    results = [None] * processes
+
+    def run(i):
+        sl = slice(i * points, (i + 1) * points)
+        with Session(exe) as s:
+            net = Network(s, LAYERS, weights=weights)
+            inp = Data(s, x[:, :, sl], t)
+            tgt = Data(s, targets[:, :, sl], t)
+            cost = net.matching(inp, tgt, np.ones((1, R), np.float32))
+            start.wait()
+            wall, _, _, _ = net.benchmark(cost, warm=0, iterations=1, batches=steps)
+        results[i] = float(np.median(wall))
+
+    threads = [threading.Thread(target=run, args=(i,)) for i in range(processes)]
+    for th in threads:
+        th.start()
+    for th in threads:
+        th.join()
+    ms = max(results)
+    return dict(value=sum(points * R / (r / 1000) for r in results), unit=UNIT, cores=processes, kind='reference',
+                sample=f'{processes} concurrent cpde_ref_cpu_server processes (oracle/Makefile, serial CPU '
+                       f'backend, one per core), each on its own {points} of the workload\'s points, {steps} op-90 '
+                       'epochs, median per process, throughput summed',
                 ms_per_epoch_sample=ms)
 
 
@@ -665,7 +688,7 @@ def run_reference(args):
                 dtype='f32', data='synthetic', impl='reference',
                 config=dict(workload='config 2 (65,536 pts, order 6, 2->128^4->1), bounded sample',
                             sample_points=args.reference_points),
-                cpu_baseline=dict(value=base['value'], unit=UNIT, cores=1, kind='reference',
+                cpu_baseline=dict(value=base['value'], unit=UNIT, cores=base['cores'], kind='reference',
                                   sample=base['sample']),
                 e2e=dict(value=base['value'], unit=UNIT, h2d_bytes_per_step=0, d2h_bytes_per_step=0))
     print(json.dumps(line))

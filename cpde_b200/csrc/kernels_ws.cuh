@@ -483,6 +483,20 @@ template <int SLAB, int S>
 __device__ __forceinline__ void produce_wide(const Ring& r, float* a_hi, float* a_lo, const CUtensorMap* map,
                                              const CUtensorMap* map_a_hi, const CUtensorMap* map_a_lo, int a_row,
                                              long tiles, int tile_columns, int N, int slabs) {
+    // The ring is only S stages deep and a slab's MMAs are short, so an
+    // activation slab fetched from HBM when its stage frees would arrive late:
+    // each slab's L2 prefetch goes out kPrefetch slabs ahead of its load (the
+    // weight slabs are L2-resident already).
+    constexpr int kPrefetch = 2 * S;
+    auto prefetch = [&](long tile, int s) {  // the slab kPrefetch after (tile, s)
+        s += kPrefetch;
+        while (s >= slabs) {
+            s -= slabs;
+            tile += gridDim.x;
+        }
+        if (tile < tiles) tc::tma_prefetch_2d(map, s * 32, int(tile * tile_columns));
+    };
+    for (int k = 0; k < kPrefetch && k < slabs; ++k) prefetch(blockIdx.x, k - kPrefetch);
     uint32_t it = 0;
     for (long tile = blockIdx.x; tile < tiles && !*r.abort; tile += gridDim.x) {
         const int col0 = int(tile * tile_columns);
@@ -493,6 +507,7 @@ __device__ __forceinline__ void produce_wide(const Ring& r, float* a_hi, float* 
             tc::tma_load_2d(r.hi + st * (SLAB / 4), map, r.full + st, s * 32, col0);
             tc::tma_load_2d(a_hi + st * (kWeightSlab / 4), map_a_hi, r.full + st, s * 32, a_row);
             tc::tma_load_2d(a_lo + st * (kWeightSlab / 4), map_a_lo, r.full + st, s * 32, a_row);
+            prefetch(tile, s);
             ++it;
         }
     }
@@ -788,6 +803,18 @@ static __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_
     float* out = partials + (size_t)blockIdx.x * M * (N + 1);
     if (warp == kProducerWarp) {
         if (lane == 0) {
+            // L2 prefetches run two ring depths ahead of the loads (the ring's
+            // three stages alone do not cover the HBM latency of a chunk)
+            constexpr int kPrefetch = 2 * kWgStages;
+            auto prefetch = [&](int it) {
+                if (it >= chunks) return;
+                const int c0 = int(chunk_start(it));
+                for (int j = 0; j < 4; ++j) {
+                    tc::tma_prefetch_2d(&map_dz, m_base + 32 * j, c0);
+                    tc::tma_prefetch_2d(&map_y, n_base + 32 * j, c0);
+                }
+            };
+            for (int k = 0; k < kPrefetch; ++k) prefetch(k);
             int it = 0;
             for (; it < chunks && !*abort; ++it) {
                 const int st = it % kWgStages;
@@ -798,6 +825,7 @@ static __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_
                     tc::tma_load_2d(stage_ptr(st, 0) + j * (kWgBox / 4), &map_dz, full + st, m_base + 32 * j, c0);
                     tc::tma_load_2d(stage_ptr(st, 1) + j * (kWgBox / 4), &map_y, full + st, n_base + 32 * j, c0);
                 }
+                prefetch(it + kPrefetch);
             }
             for (int k = it > kWgStages ? it - kWgStages : 0; k < it; ++k)
                 if (!tc::mbar_wait(full + k % kWgStages, (k / kWgStages) & 1, tcg::kWaitCycles)) *abort = 1;
