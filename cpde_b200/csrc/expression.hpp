@@ -216,6 +216,11 @@ extern "C" __global__ void __launch_bounds__(128, 4) cpde_head(
   __shared__ float comp[LANES][PB][RO];
   __shared__ float gsh[LANES][PB][RO];
   __shared__ float red[128];
+  // The last hidden layer's values of the next round are copied asynchronously
+  // into ybuf while this round runs (each thread copies and later reads only
+  // its own elements, so its own wait_group orders them; no barrier): one
+  // round's loads alone left the head bound on DRAM latency.
+  __shared__ float ybuf[2][PB][R][128];
   const int t = threadIdx.x, ml = t % NB, lp = t / NB, wl = ml >> 5, lane = t & 31;
   float w[O], gw[O], gb[O];
 #pragma unroll
@@ -223,13 +228,31 @@ extern "C" __global__ void __launch_bounds__(128, 4) cpde_head(
   const float* bias = W + (size_t)O * K;
   const double scale = multiplier ? *multiplier : 1.0;
   CostStats local = cs_empty();
-  for (long base = (long)blockIdx.x * LANES * PB; base < points; base += (long)gridDim.x * LANES * PB) {
+  const long stride = (long)gridDim.x * LANES * PB;
+  auto prefetch = [&](long base, int b) {
+    const long q0 = base + (long)lp * PB;
+#pragma unroll
+    for (int j = 0; j < PB; ++j)
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+        if (q0 + j < points) {
+          const unsigned dst = (unsigned)__cvta_generic_to_shared(&ybuf[b][j][r][t]);
+          asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(dst),
+                       "l"(Y + ((size_t)(q0 + j) * R + r) * K + ml) : "memory");
+        }
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+  };
+  int b = 0;
+  prefetch((long)blockIdx.x * LANES * PB, 0);
+  for (long base = (long)blockIdx.x * LANES * PB; base < points; base += stride, b ^= 1) {
     const long p0 = base + (long)lp * PB;  // this lane's first point of the round
+    prefetch(base + stride, b ^ 1);
+    asm volatile("cp.async.wait_group 1;\n" ::: "memory");
     float y[PB][R];
 #pragma unroll
     for (int j = 0; j < PB; ++j)
 #pragma unroll
-      for (int r = 0; r < R; ++r) y[j][r] = p0 + j < points ? Y[((size_t)(p0 + j) * R + r) * K + ml] : 0.f;
+      for (int r = 0; r < R; ++r) y[j][r] = p0 + j < points ? ybuf[b][j][r][t] : 0.f;
 #pragma unroll
     for (int j = 0; j < PB; ++j)
 #pragma unroll
@@ -276,6 +299,7 @@ extern "C" __global__ void __launch_bounds__(128, 4) cpde_head(
       for (int r = 0; r < R; ++r) out[(size_t)r * K] = dy[r];
     }
   }
+  asm volatile("cp.async.wait_group 0;\n" ::: "memory");  // no copy lands after the CTA ends
   float* out = partials + (size_t)blockIdx.x * O * (K + 1);
   for (int o = 0; o < O; ++o) {
     red[t] = gw[o];

@@ -109,30 +109,35 @@ struct FastBackward {
             if (tensor && N % 32 == 0 && M % tcg::KS == 0 && M <= ws::kMaxK) {
                 // warp-specialised: W^T resident in tensor memory, dZ slab ring in shared memory
                 using WT = ws::Tiling<R>;
+                using WTI = ws::Tiling<R, R * StaticJet<SID>::V>;  // with the input-jet rows
                 static bool bw_ready[64] = {};
                 if (!bw_ready[e.device & 63]) {
                     allow_smem(ws::k_backward_ws<SID, Act, false>, WT::BSMEM);
-                    allow_smem(ws::k_backward_ws<SID, Act, true>, WT::BSMEM);
+                    allow_smem(ws::k_backward_ws<SID, Act, true>, WTI::BSMEM);
                     bw_ready[e.device & 63] = true;
                 }
                 const CUtensorMap mz = tensor_map(cur, M, cols, WT::N);
                 const long tt = (P + WT::PTS - 1) / WT::PTS;
+                const int halves = ws::paired_tiles(N, M) ? 2 : 1;  // two column tiles per accumulator
+                const long items = (tt + halves - 1) / halves;
                 const int ny = (N + tcg::BM - 1) / tcg::BM;  // a narrower layer fills part of one slice
-                const int bx = int(std::min<long>(tt, std::max(1, 148 / ny)));
+                const int bx = int(std::min<long>(items, std::max(1, 148 / ny)));
                 dim3 grid(bx, ny);
                 if (input) {
-                    n.input_partial.reserve(size_t(2 * bx) * N * (K0 + 1));
+                    const int parts = 2 * halves * bx;  // one per epilogue group and tile half of each CTA
+                    n.input_partial.reserve(size_t(parts) * N * (K0 + 1));
                     CPDE_RUN(e, "backward_input_ws",
-                             (ws::k_backward_ws<SID, Act, true><<<grid, ws::THREADS, WT::BSMEM, e.stream>>>(
+                             (ws::k_backward_ws<SID, Act, true><<<grid, ws::THREADS, WTI::BSMEM, e.stream>>>(
                                  mz, M, N, P, W, n.act[1].ptr, nullptr, n.act[0].ptr, K0, n.input_partial.ptr,
-                                 e.tc_error.ptr)));
+                                 e.tc_error.ptr, halves)));
                     long isize = long(N) * (K0 + 1);
                     CPDE_RUN(e, "sum_partials", (k_sum_partials<<<fast::sum_grid(isize), 256, 0, e.stream>>>(
-                                                    n.input_partial.ptr, 2 * bx, isize, n.gradient_base(0, target))));
+                                                    n.input_partial.ptr, parts, isize, n.gradient_base(0, target))));
                 } else {
                     CPDE_RUN(e, "backward_ws",
                              (ws::k_backward_ws<SID, Act, false><<<grid, ws::THREADS, WT::BSMEM, e.stream>>>(
-                                 mz, M, N, P, W, n.act[l - 1].ptr, next, nullptr, 0, nullptr, e.tc_error.ptr)));
+                                 mz, M, N, P, W, n.act[l - 1].ptr, next, nullptr, 0, nullptr, e.tc_error.ptr,
+                                 halves)));
                     cur = next;
                 }
                 continue;

@@ -43,10 +43,12 @@ struct FastForward {
                 }
                 const CUtensorMap mx = tensor_map(n.act[l - 1].ptr, K, P * R, WT::N);
                 const long tiles = (P + WT::PTS - 1) / WT::PTS;
+                const int halves = ws::paired_tiles(M, K) ? 2 : 1;  // two column tiles per accumulator
+                const long items = (tiles + halves - 1) / halves;
                 const int ny = (M + tcg::BM - 1) / tcg::BM;  // a narrower layer fills part of one slice
-                dim3 grid(unsigned(std::min<long>(tiles, std::max(1, 148 / ny))), unsigned(ny));
+                dim3 grid(unsigned(std::min<long>(items, std::max(1, 148 / ny))), unsigned(ny));
                 CPDE_RUN(e, "forward_ws", (ws::k_forward_ws<SID, Act><<<grid, ws::THREADS, WT::SMEM, e.stream>>>(
-                                              mx, M, K, P, W, n.act[l].ptr, e.tc_error.ptr)));
+                                              mx, M, K, P, W, n.act[l].ptr, e.tc_error.ptr, halves)));
             } else if (tensor && M % tcg::BM == 0 && K % tcg::KS == 0) {
                 // wider inputs: the weight slabs stream through the shared-memory ring with the activations
                 using WT = ws::WideTiling<R>;

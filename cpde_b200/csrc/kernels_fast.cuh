@@ -41,21 +41,50 @@ struct Smem {
 };
 
 // ---------------------------------------------------------------------------
-// Main loop: acc[RM][TN] += A (BMT x K) * B (K x BN), RM = BMT / 16; thread
-// (ty, tx) owns rows ty*RM..ty*RM+RM-1 and columns tx + 16 j. A and B slabs
-// are staged through registers so the next slab's global loads overlap the
-// current FMAs.
+// Main loop: acc[RM][TN] += A (BMT x K) * B (K x BN), RM = BMT / 16. A and B
+// slabs are staged through registers so the next slab's global loads overlap
+// the current FMAs.
 //   A loader: a(m, k) for m < BMT, k < K (zero outside)
 //   B loader: b4(c, k4) returns float4 of b(k4*4 .. k4*4+3, c) (zero outside)
+//
+// Thread layout (Layout<BN, BMT>). When BN is a multiple of 64 the 8 warps
+// form a 2 x 4 grid of (BMT/2) x (BN/4) warp tiles and lane (tm, tn) =
+// (lane / 4, lane % 4) owns rows wm BMT/2 + 32 h + 4 tm + i and columns
+// wn BN/4 + 16 g + 4 tn + j (i, j < 4): every shared-memory read of a k step
+// is a float4, and the lanes of one read cover one contiguous 128-byte (A)
+// or 64-byte (B) span, one wavefront each: 3 wavefronts per 32 FMAs of a
+// 64-row tile, 4 per 64 of a 128-row tile. (A layout of scalar column reads,
+// 16 lanes apart, took 9 wavefronts per 32 FMAs and held the 64-row forward
+// at about half of the FMA pipe, bound on shared-memory bandwidth.)
+// Otherwise thread (ty, tx) = (t / 16, t % 16) owns rows ty RM + i and
+// columns tx + 16 j.
+template <int BN, int BMT>
+struct Layout {
+    static constexpr bool kWide = BN % 64 == 0;
+    static constexpr int RM = BMT / 16, TN = BN / 16;
+    // first row of the thread's row group h, first column of its column group g (kWide), or the
+    // row base and column of index j (otherwise)
+    __device__ static int row(int h) {
+        const int t = threadIdx.x;
+        if constexpr (kWide) return (t >> 7) * (BMT / 2) + 32 * h + 4 * ((t & 31) >> 2);
+        else return (t >> 4) * RM + 4 * h;
+    }
+    __device__ static int column(int g) {
+        const int t = threadIdx.x;
+        if constexpr (kWide) return ((t >> 5) & 3) * (BN / 4) + 16 * g + 4 * (t & 3);
+        else return (t & 15) + 16 * g;
+    }
+};
 
 template <int BN, int BMT = BM, class ALoad, class BLoad>
 __device__ __forceinline__ void gemm_main(float (&acc)[BMT / 16][BN / 16], float* smem, int K, const ALoad& aload,
                                           const BLoad& bload) {
     using S = Smem<BN, BMT>;
+    using Lo = Layout<BN, BMT>;
     constexpr int TN = BN / 16, RM = BMT / 16;
     float* As = smem;                   // [2][BK][LDA]
     float* Bs = smem + 2 * BK * S::LDA;  // [2][BK][LDB]
-    const int t = threadIdx.x, tx = t & 15, ty = t >> 4;
+    const int t = threadIdx.x;
     // A slab: 16 x BMT values, RM per thread: k = t/16 (0..15), m = (t%16)*RM + i
     constexpr int BLOADS = (BN * 4 + THREADS - 1) / THREADS;  // float4 loads of the B slab per thread
     float ra[RM];
@@ -76,7 +105,9 @@ __device__ __forceinline__ void gemm_main(float (&acc)[BMT / 16][BN / 16], float
         float* b = Bs + buf * BK * S::LDB;
         const int k = t >> 4, m0 = (t & 15) * RM;
 #pragma unroll
-        for (int i = 0; i < RM; ++i) a[k * S::LDA + m0 + i] = ra[i];
+        for (int i4 = 0; i4 < RM / 4; ++i4)
+            *reinterpret_cast<float4*>(a + k * S::LDA + m0 + 4 * i4) =
+                make_float4(ra[4 * i4], ra[4 * i4 + 1], ra[4 * i4 + 2], ra[4 * i4 + 3]);
 #pragma unroll
         for (int j = 0; j < BLOADS; ++j) {
             int idx = t + j * THREADS;
@@ -93,25 +124,40 @@ __device__ __forceinline__ void gemm_main(float (&acc)[BMT / 16][BN / 16], float
     fetch(0);
     store(0);
     __syncthreads();
+    // the thread's first row of A and first column of B in slab buffer 0
+    const float* a_base = As + Lo::row(0);
+    const float* b_base = Bs + Lo::column(0);
     for (int s = 0; s < slabs; ++s) {
         const int buf = s & 1;
         if (s + 1 < slabs) fetch((s + 1) * BK);
-        const float* a = As + buf * BK * S::LDA;
-        const float* b = Bs + buf * BK * S::LDB;
+        const float* a = a_base + buf * BK * S::LDA;
+        const float* b = b_base + buf * BK * S::LDB;
 #pragma unroll
         for (int k = 0; k < BK; ++k) {
             float av[RM];
 #pragma unroll
-            for (int i4 = 0; i4 < RM / 4; ++i4) {
-                const float4 a4 = *reinterpret_cast<const float4*>(a + k * S::LDA + ty * RM + 4 * i4);
-                av[4 * i4] = a4.x;
-                av[4 * i4 + 1] = a4.y;
-                av[4 * i4 + 2] = a4.z;
-                av[4 * i4 + 3] = a4.w;
+            for (int h = 0; h < RM / 4; ++h) {
+                // row group h starts 32 rows (kWide) or 4 rows further
+                const float4 a4 = *reinterpret_cast<const float4*>(a + k * S::LDA + (Lo::kWide ? 32 : 4) * h);
+                av[4 * h] = a4.x;
+                av[4 * h + 1] = a4.y;
+                av[4 * h + 2] = a4.z;
+                av[4 * h + 3] = a4.w;
             }
             float bv[TN];
+            if constexpr (Lo::kWide) {
 #pragma unroll
-            for (int j = 0; j < TN; ++j) bv[j] = b[k * S::LDB + tx + 16 * j];
+                for (int g = 0; g < TN / 4; ++g) {
+                    const float4 b4 = *reinterpret_cast<const float4*>(b + k * S::LDB + 16 * g);
+                    bv[4 * g] = b4.x;
+                    bv[4 * g + 1] = b4.y;
+                    bv[4 * g + 2] = b4.z;
+                    bv[4 * g + 3] = b4.w;
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < TN; ++j) bv[j] = b[k * S::LDB + 16 * j];
+            }
 #pragma unroll
             for (int i = 0; i < RM; ++i)
 #pragma unroll
@@ -128,15 +174,15 @@ __device__ __forceinline__ void gemm_main(float (&acc)[BMT / 16][BN / 16], float
 template <int BN, int BMT = BM>
 __device__ __forceinline__ void stage_tile(const float (&acc)[BMT / 16][BN / 16], float* smem) {
     using S = Smem<BN, BMT>;
+    using Lo = Layout<BN, BMT>;
     constexpr int RM = BMT / 16;
-    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
 #pragma unroll
     for (int j = 0; j < BN / 16; ++j) {
-        float* z = smem + (tx + 16 * j) * S::LDZ + ty * RM;
+        const int c = Lo::kWide ? Lo::column(j >> 2) + (j & 3) : Lo::column(j);
 #pragma unroll
-        for (int i4 = 0; i4 < RM / 4; ++i4)
-            *reinterpret_cast<float4*>(z + 4 * i4) =
-                make_float4(acc[4 * i4][j], acc[4 * i4 + 1][j], acc[4 * i4 + 2][j], acc[4 * i4 + 3][j]);
+        for (int h = 0; h < RM / 4; ++h)
+            *reinterpret_cast<float4*>(smem + c * S::LDZ + Lo::row(h)) =
+                make_float4(acc[4 * h][j], acc[4 * h + 1][j], acc[4 * h + 2][j], acc[4 * h + 3][j]);
     }
     __syncthreads();
 }
@@ -186,6 +232,31 @@ __device__ __forceinline__ void for_row(const float* x, F f) {
     }
 }
 
+// for_row over a row in shared memory (plain loads; x 16-byte aligned).
+template <int L, class F>
+__device__ __forceinline__ void for_row_shared(const float* x, F f) {
+    if constexpr (L % 4 == 0) {
+#pragma unroll
+        for (int i = 0; i < L / 4; ++i) {
+            const float4 v = reinterpret_cast<const float4*>(x)[i];
+            f(4 * i, v.x);
+            f(4 * i + 1, v.y);
+            f(4 * i + 2, v.z);
+            f(4 * i + 3, v.w);
+        }
+    } else if constexpr (L % 2 == 0) {
+#pragma unroll
+        for (int i = 0; i < L / 2; ++i) {
+            const float2 v = reinterpret_cast<const float2*>(x)[i];
+            f(2 * i, v.x);
+            f(2 * i + 1, v.y);
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < L; ++i) f(i, x[i]);
+    }
+}
+
 // z[r] = sum_k W[m + k M] x[r K + k]
 template <int R, int K>
 __device__ __forceinline__ void input_rows_k(const float* __restrict__ W, int M, int m, const float* x,
@@ -229,6 +300,12 @@ __device__ __forceinline__ void input_rows(const float* __restrict__ W, int M, i
 template <int R, int K>
 __device__ __forceinline__ void input_gradient_k(const float (&g)[R], const float* x, float (&gacc)[9]) {
     for_row<R * K>(x, [&](int e, float v) { gacc[e % K] = fmaf(g[e / K], v, gacc[e % K]); });
+    gacc[8] += g[0];
+}
+// input_gradient_k with the point's row x in shared memory
+template <int R, int K>
+__device__ __forceinline__ void input_gradient_row(const float (&g)[R], const float* x, float (&gacc)[9]) {
+    for_row_shared<R * K>(x, [&](int e, float v) { gacc[e % K] = fmaf(g[e / K], v, gacc[e % K]); });
     gacc[8] += g[0];
 }
 template <int R>

@@ -43,7 +43,9 @@ constexpr uint32_t kTmemColumns = 512, kAccColumn = 256;
 constexpr int kSmemLimit = 232448;  // dynamic shared memory of one CTA (227 KB)
 constexpr int kStagingSlots = 3;    // backward: Y_prev staged two work items ahead
 
-template <int R>
+// XV: input-jet floats of one point (R x inputs) that the backward into the
+// first hidden layer keeps per epilogue warp (0 elsewhere).
+template <int R, int XV = 0>
 struct Tiling {
     static constexpr int PTS = tcg::Tiling<R>::PTS;                // whole points per tile
     static constexpr int COLS = PTS * R;
@@ -54,10 +56,12 @@ struct Tiling {
     // the previous layer's values, copied asynchronously kStagingSlots - 1 work
     // items ahead; the slab ring gives up stages where both do not fit
     static constexpr int YBUF = kStagingSlots * R * 4 * 32 * 4 * kEpilogueGroups;
-    static constexpr int BSTAGES = (kSmemLimit - 1024 - 256 - YBUF) / (2 * SLAB) < STAGES
-                                       ? (kSmemLimit - 1024 - 256 - YBUF) / (2 * SLAB)
+    static constexpr int XROW = (XV + 3) / 4 * 4;                    // floats, 16-byte rows
+    static constexpr int XBUF = 4 * kEpilogueGroups * XROW * 4;      // one row per epilogue warp
+    static constexpr int BSTAGES = (kSmemLimit - 1024 - 256 - YBUF - XBUF) / (2 * SLAB) < STAGES
+                                       ? (kSmemLimit - 1024 - 256 - YBUF - XBUF) / (2 * SLAB)
                                        : STAGES;
-    static constexpr int BSMEM = 2 * BSTAGES * SLAB + 1024 + 256 + YBUF;
+    static constexpr int BSMEM = 2 * BSTAGES * SLAB + 1024 + 256 + YBUF + XBUF;
     static_assert(BSTAGES >= 3, "slab ring too shallow beside the staging slots");
 };
 
@@ -122,19 +126,24 @@ __device__ __forceinline__ void ring_init(Ring& r) {
     tc::tc_fence_after();
 }
 
-// Producer: the X slabs of every tile this CTA owns, in order. After the last
-// issue (or an abort) it waits for the loads still in flight.
+// Producer: the X slabs of every work item this CTA owns, in order. A work
+// item is one column tile, or with halves = 2 two adjacent tiles 2w, 2w + 1
+// whose K slabs follow one another (the layers of at most 64 neurons and 64
+// inputs, see PairedTiles); the second tile of the last pair may lie past the
+// end, and its load then reads the fill value (zeros). After the last issue
+// (or an abort) it waits for the loads still in flight.
 template <int SLAB, int S = STAGES>
-__device__ __forceinline__ void produce(const Ring& r, const CUtensorMap* map, long tiles, int tile_columns, int N,
-                                        int slabs) {
+__device__ __forceinline__ void produce(const Ring& r, const CUtensorMap* map, long items, int tile_columns, int N,
+                                        int kslabs, int halves = 1) {
     uint32_t it = 0;
-    for (long tile = blockIdx.x; tile < tiles && !*r.abort; tile += gridDim.x) {
-        const int col0 = int(tile * tile_columns);
-        for (int s = 0; s < slabs; ++s) {
+    for (long w = blockIdx.x; w < items && !*r.abort; w += gridDim.x) {
+        for (int s = 0; s < kslabs * halves; ++s) {
+            const int half = s >= kslabs, ks = s - half * kslabs;
+            const int col0 = int((w * halves + half) * tile_columns);
             const int st = it % S;
             if (!tc::mbar_wait_or_abort(r.empty + st, ((it / S) & 1) ^ 1, tcg::kWaitCycles, r.abort)) break;
             tc::mbar_expect_tx(r.full + st, uint32_t(N) * 128);
-            tc::tma_load_2d(r.hi + st * (SLAB / 4), map, r.full + st, s * 32, col0);
+            tc::tma_load_2d(r.hi + st * (SLAB / 4), map, r.full + st, ks * 32, col0);
             ++it;
         }
     }
@@ -242,18 +251,23 @@ __device__ __forceinline__ void issue_mmas(const Ring& r, uint32_t tmem, long ti
 // W[m + k M]); the backward's is W^T (row n holds W[k + n K], contiguous).
 // Rows m >= M (a layer narrower than the tile's 128 rows) are zero, so those
 // accumulator lanes stay zero and the epilogue skips them.
+// Paired tiles (halves = 2): the A operand is the block diagonal diag(W, W)
+// of 2K columns; lanes of half h (0: lanes 0-63, 1: lanes 64-127) hold row m
+// of W in columns [h K, h K + K) and zeros elsewhere.
 __device__ __forceinline__ void load_weights(const Ring& r, uint32_t tmem, const float* __restrict__ W, int M,
-                                             int K, int m, bool transposed = false) {
+                                             int K, int m, bool transposed = false, int halves = 1, int half = 0) {
     const int quarter = (threadIdx.x >> 5) & 3;
     const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
     const bool live = m < M;
-    for (int c0 = 0; c0 < K; c0 += 8) {
+    for (int c0 = 0; c0 < K * halves; c0 += 8) {
+        const int k0 = c0 - (c0 >= K ? K : 0);  // column within W's block (K is a multiple of 8)
+        const bool block = live && (c0 >= K) == (half == 1);
         float h[8], l[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            const float v = !live ? 0.f
-                            : transposed ? __ldg(W + (size_t)m * K + c0 + j)
-                                         : __ldg(W + m + (size_t)(c0 + j) * M);
+            const float v = !block ? 0.f
+                            : transposed ? __ldg(W + (size_t)m * K + k0 + j)
+                                         : __ldg(W + m + (size_t)(k0 + j) * M);
             h[j] = tc::tf32_round(v);
             l[j] = tc::tf32_round(v - h[j]);
         }
@@ -276,12 +290,30 @@ __device__ __forceinline__ void teardown(const Ring& r, uint32_t tmem, int* erro
     if (threadIdx.x == 0 && *r.abort) atomicExch(error, tcg::kErrMma);
 }
 
+// Paired tiles: a layer of at most 64 neurons fills only half of the 128
+// accumulator lanes, and half of the epilogue warps (those of lane quarters
+// 2 and 3) would idle. With halves = 2 one MMA chain computes two adjacent
+// column tiles at once: A = diag(W, W) (2K columns, K <= 64) against the K
+// slabs of tile 2w followed by those of tile 2w + 1, so lanes 0-63 hold
+// tile 2w and lanes 64-127 tile 2w + 1, and every epilogue warp has a tile.
+// The tensor cores do twice the (cheap) work; the epilogue, which sets the
+// pace of these layers, covers twice the columns per accumulator.
+__host__ __device__ constexpr bool paired_tiles(int rows, int K) { return rows <= 64 && K <= 64; }
+
+struct PairedTiles {
+    int halves;  // 1, or 2 for paired tiles
+    // lane quarter -> (half, first row of the quarter within the layer's 128-row slice)
+    __device__ int half(int quarter) const { return halves == 2 ? quarter >> 1 : 0; }
+    __device__ int row(int quarter) const { return (halves == 2 ? quarter & 1 : quarter) * 32; }
+};
+
 // Hidden layer forward: Y = f(W X + b) with the jet combine in the epilogue.
-// grid = (CTAs over column tiles, M / 128); K a multiple of 32, at most 128.
+// grid = (CTAs over work items, M / 128); K a multiple of 32, at most 128;
+// halves = 2 (paired tiles) needs M <= 64 and K <= 64.
 template <int SID, class Act>
 __global__ void __launch_bounds__(THREADS, 1) k_forward_ws(const __grid_constant__ CUtensorMap map_x, int M, int K,
                                                            long P, const float* __restrict__ W,
-                                                           float* __restrict__ Y, int* error) {
+                                                           float* __restrict__ Y, int* error, int halves) {
     constexpr int R = StaticJet<SID>::R;
     using T = Tiling<R>;
     extern __shared__ uint8_t smem_raw[];
@@ -289,27 +321,28 @@ __global__ void __launch_bounds__(THREADS, 1) k_forward_ws(const __grid_constant
     ring_init(r);
     const uint32_t tmem = *r.tmem_slot;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const long tiles = (P + T::PTS - 1) / T::PTS;
-    const int slabs = K / 32;
+    const long tiles = (P + T::PTS - 1) / T::PTS, items = (tiles + halves - 1) / halves;
+    const int kslabs = K / 32;
+    const PairedTiles pt{halves};
     if (warp == kProducerWarp) {
-        if (lane == 0) produce<T::SLAB>(r, &map_x, tiles, T::COLS, T::N, slabs);
+        if (lane == 0) produce<T::SLAB>(r, &map_x, items, T::COLS, T::N, kslabs, halves);
     } else if (warp == kMmaWarp || warp == kSecondMmaWarp) {
-        if (lane == 0) issue_mmas<T::N, T::SLAB>(r, tmem, tiles, slabs, warp == kMmaWarp ? 0 : 1);
+        if (lane == 0) issue_mmas<T::N, T::SLAB>(r, tmem, items, kslabs * halves, warp == kMmaWarp ? 0 : 1);
     } else if (warp < kEpilogueWarp) {
-        split_all<T::SLAB>(r, tiles, T::N, slabs);
+        split_all<T::SLAB>(r, items, T::N, kslabs * halves);
     } else {
-        const int quarter = warp & 3, group = (warp - kEpilogueWarp) >> 2;
-        const int m = blockIdx.y * 128 + quarter * 32 + lane;
+        const int quarter = warp & 3, group = (warp - kEpilogueWarp) >> 2, half = pt.half(quarter);
+        const int m = blockIdx.y * 128 + pt.row(quarter) + lane;
         const bool live = m < M;  // the same for the whole warp: M is a multiple of 32
-        if (group == 0) load_weights(r, tmem, W, M, K, m);
+        if (group == 0) load_weights(r, tmem, W, M, K, m, false, halves, half);
         const float b0 = live ? __ldg(W + (size_t)M * K + m) : 0.f;
         const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
         uint32_t local = 0;
-        for (long tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
+        for (long w = blockIdx.x; w < items; w += gridDim.x, ++local) {
             const int a = local & 1;
             if (!warp_wait(r.acc_full + a, (local >> 1) & 1, r.abort)) break;
             tc::tc_fence_after();
-            const long p0 = tile * T::PTS;
+            const long p0 = (w * halves + half) * T::PTS;
             for (int p = group; live && p < T::PTS; p += kEpilogueGroups) {
                 if (p0 + p >= P) break;
                 float z[R], y[R];
@@ -333,60 +366,94 @@ __global__ void __launch_bounds__(THREADS, 1) k_forward_ws(const __grid_constant
 // previous-layer neurons of this CTA's slice, K = Ml neurons of this layer)
 // and B = the dZ slabs. With INPUT_GRAD the previous layer is the first hidden
 // one: dZ_prev is not stored and the first layer's gradient is accumulated
-// per thread into input_partials[2 blockIdx.x + group][n + k N] (bias at
-// k = K0), one partial per epilogue group.
+// per thread into input_partials[(halves blockIdx.x + half) 2 + group]
+// [n + k N] (bias at k = K0), one partial per epilogue group and tile half.
 // The epilogue's reads of Y_prev (and, with INPUT_GRAD, of the inputs) do not
 // depend on the accumulator, so each thread copies those of the work item
 // (tile, point) two ahead of its current one into a shared-memory staging
 // slot, and the DRAM latency of the loads leaves the critical path.
-// grid = (CTAs over column tiles, N / 128); Ml a multiple of 32, at most 128.
+// grid = (CTAs over work items, N / 128); Ml a multiple of 32, at most 128;
+// halves = 2 (paired tiles, as in the forward) needs N <= 64 and Ml <= 64.
 template <int SID, class Act, bool INPUT_GRAD>
 __global__ void __launch_bounds__(THREADS, 1) k_backward_ws(const __grid_constant__ CUtensorMap map_dz, int Ml, int N,
                                                             long P, const float* __restrict__ W,
                                                             const float* __restrict__ Yprev,
                                                             float* __restrict__ dZprev, const float* __restrict__ X0,
-                                                            int K0, float* __restrict__ input_partials, int* error) {
-    constexpr int R = StaticJet<SID>::R;
-    using T = Tiling<R>;
+                                                            int K0, float* __restrict__ input_partials, int* error,
+                                                            int halves) {
+    constexpr int R = StaticJet<SID>::R, V = StaticJet<SID>::V;
+    constexpr int XV = INPUT_GRAD ? R * V : 0;  // input-jet floats of a point
+    using T = Tiling<R, XV>;
     constexpr int S = T::BSTAGES;
     extern __shared__ uint8_t smem_raw[];
     Ring r = carve_ring<T::SLAB, S>(smem_raw);
     ring_init<S>(r);
     const uint32_t tmem = *r.tmem_slot;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const long tiles = (P + T::PTS - 1) / T::PTS;
-    const int slabs = Ml / 32;
+    const long tiles = (P + T::PTS - 1) / T::PTS, items = (tiles + halves - 1) / halves;
+    const int kslabs = Ml / 32;
+    const PairedTiles pt{halves};
     if (warp == kProducerWarp) {
-        if (lane == 0) produce<T::SLAB, S>(r, &map_dz, tiles, T::COLS, T::N, slabs);
+        if (lane == 0) produce<T::SLAB, S>(r, &map_dz, items, T::COLS, T::N, kslabs, halves);
     } else if (warp == kMmaWarp || warp == kSecondMmaWarp) {
-        if (lane == 0) issue_mmas<T::N, T::SLAB, S>(r, tmem, tiles, slabs, warp == kMmaWarp ? 0 : 1);
+        if (lane == 0) issue_mmas<T::N, T::SLAB, S>(r, tmem, items, kslabs * halves, warp == kMmaWarp ? 0 : 1);
     } else if (warp < kEpilogueWarp) {
-        split_all<T::SLAB, S>(r, tiles, T::N, slabs);
+        split_all<T::SLAB, S>(r, items, T::N, kslabs * halves);
     } else {
-        const int quarter = warp & 3, group = (warp - kEpilogueWarp) >> 2;
+        const int quarter = warp & 3, group = (warp - kEpilogueWarp) >> 2, half = pt.half(quarter);
         const int et = threadIdx.x - kEpilogueWarp * 32;  // epilogue thread 0 .. 32 * 4 * groups - 1
-        const int n = blockIdx.y * 128 + quarter * 32 + lane;
+        const int n = blockIdx.y * 128 + pt.row(quarter) + lane;
         const bool live = n < N;  // the same for the whole warp: N is a multiple of 32
-        if (group == 0) load_weights(r, tmem, W, N, Ml, n, true);
+        if (group == 0) load_weights(r, tmem, W, N, Ml, n, true, halves, half);
         const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
         constexpr int SLOT = R * 32 * 4 * kEpilogueGroups;  // floats of one slot: [q][epilogue thread]
         float* staging = r.staging + et;
+        // With INPUT_GRAD the epilogue also needs the point's input jets
+        // (R x K0 floats, the same for every lane of the warp). When K0 is the
+        // schema's variable count they are loaded at staging time, one element
+        // per lane (xq, a three-deep queue that shifts with the slots), and
+        // shared through the warp's row of shared memory when consumed;
+        // reading them from global memory only then left an L2 round trip on
+        // the path of every work item.
+        constexpr int XR = XV > 0 ? (XV + 31) / 32 : 1;
+        const bool x_queue = INPUT_GRAD && K0 == V;
+        float xq[3][XR];
+#pragma unroll
+        for (int i = 0; i < 3; ++i)
+#pragma unroll
+            for (int c = 0; c < XR; ++c) xq[i][c] = 0.f;
+        float* xrow = r.staging + T::YBUF / 4 + (warp - kEpilogueWarp) * T::XROW;
         // The thread's work items in order: points group, group + groups, ...
-        // of each of the CTA's tiles. (ft, fp) is the next item to stage.
+        // of its tile (half) of each of the CTA's work items. (ft, fp) is the
+        // next item to stage. Only the last work item can hold a partial (or,
+        // paired, an empty) tile, so the slots a thread stages past its last
+        // real item are never read.
         long ft = blockIdx.x;
         int fp = group;
         auto stage = [&](int slot) {
-            if (ft < tiles && ft * T::PTS + fp < P) {
-                const long point = ft * T::PTS + fp;
+            const long first = (ft * halves + half) * T::PTS;  // first point of the thread's tile
+            const bool valid = ft < items && first + fp < P;
+            if (valid) {
+                const long point = first + fp;
                 const float* yp = Yprev + ((size_t)point * R) * N + n;
 #pragma unroll
                 for (int q = 0; q < R; ++q)
                     tc::copy_async4(staging + slot * SLOT + q * 32 * 4 * kEpilogueGroups, yp + (size_t)q * N);
-                if (INPUT_GRAD && lane * 32 < R * K0) tc::prefetch_l2(X0 + (size_t)point * R * K0 + lane * 32);
+                if (INPUT_GRAD && !x_queue && lane * 32 < R * K0)
+                    tc::prefetch_l2(X0 + (size_t)point * R * K0 + lane * 32);
+            }
+            if (INPUT_GRAD) {
+#pragma unroll
+                for (int c = 0; c < XR; ++c) {
+                    const int e = lane + 32 * c;
+                    xq[0][c] = xq[1][c];
+                    xq[1][c] = xq[2][c];
+                    xq[2][c] = x_queue && valid && e < XV ? __ldg(X0 + (size_t)(first + fp) * XV + e) : 0.f;
+                }
             }
             tc::copy_async_commit();
             fp += kEpilogueGroups;
-            if (fp >= T::PTS || ft * T::PTS + fp >= P) {
+            if (fp >= T::PTS || first + fp >= P) {
                 fp = group;
                 ft += gridDim.x;
             }
@@ -399,11 +466,11 @@ __global__ void __launch_bounds__(THREADS, 1) k_backward_ws(const __grid_constan
 #pragma unroll
         for (int k = 0; k < 9; ++k) gacc[k] = 0.f;
         uint32_t local = 0;
-        for (long tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++local) {
+        for (long w = blockIdx.x; w < items; w += gridDim.x, ++local) {
             const int a = local & 1;
             if (!warp_wait(r.acc_full + a, (local >> 1) & 1, r.abort)) break;
             tc::tc_fence_after();
-            const long p0 = tile * T::PTS;
+            const long p0 = (w * halves + half) * T::PTS;
             for (int p = group; live && p < T::PTS; p += kEpilogueGroups) {
                 if (p0 + p >= P) break;
                 stage(slot == 0 ? kStagingSlots - 1 : slot - 1);  // the slot read one item ago
@@ -414,7 +481,15 @@ __global__ void __launch_bounds__(THREADS, 1) k_backward_ws(const __grid_constan
                 for (int q = 0; q < R; ++q) y[q] = staging[slot * SLOT + q * 32 * 4 * kEpilogueGroups];
                 slot = slot + 1 == kStagingSlots ? 0 : slot + 1;
                 StaticJet<SID>::template adjoint<Act>(y, g);
-                if (INPUT_GRAD) {
+                if (INPUT_GRAD && x_queue) {
+                    // the item's input jets: staged two items ago, now the queue's head
+                    __syncwarp();  // the previous item's reads of the row are done
+#pragma unroll
+                    for (int c = 0; c < XR; ++c)
+                        if (lane + 32 * c < XV) xrow[lane + 32 * c] = xq[0][c];
+                    __syncwarp();
+                    fast::input_gradient_row<R, V>(g, xrow, gacc);
+                } else if (INPUT_GRAD) {
                     fast::input_gradient<R>(g, X0 + (size_t)(p0 + p) * R * K0, K0, gacc);
                 } else {
                     float* out = dZprev + ((size_t)(p0 + p) * R) * N + n;
@@ -428,7 +503,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_backward_ws(const __grid_constan
         }
         tc::copy_async_wait<0>();  // no copy may land after the CTA ends
         if (INPUT_GRAD && live) {
-            float* out = input_partials + (size_t)(2 * blockIdx.x + group) * N * (K0 + 1);
+            float* out = input_partials +
+                         (size_t)((blockIdx.x * halves + half) * kEpilogueGroups + group) * N * (K0 + 1);
 #pragma unroll
             for (int k = 0; k < 8; ++k)
                 if (k < K0) out[n + (size_t)k * N] = gacc[k];

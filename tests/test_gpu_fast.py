@@ -171,12 +171,15 @@ def test_tensor_weight_gradient_over_many_columns(engine, width):
 @pytest.mark.parametrize('width', [32, 64, 96])
 def test_tensor_tier_narrow_layers(engine, sid, width):
     """Tensor-core (3xTF32) layers narrower than the 128-row tile: the rows
-    past the layer's width are zero weights, not stored. Orders <= 3, so the
-    exact-FP32 tolerance 1e-5 applies; several tiles per CTA."""
+    past the layer's width are zero weights, not stored; layers of at most 64
+    neurons and inputs pair two column tiles per accumulator (an odd tile
+    count leaves the last pair's second tile empty: 12,001 points of 5 rows
+    are 481 tiles). Orders <= 3, so the exact-FP32 tolerance 1e-5 applies;
+    several tiles per CTA."""
     rows = codegen.SCHEMAS[sid][1]
     layers = [2, width, width, width, 1]
     linear = [1, 0, 0, 0, 1]
-    t, x, weights, net, data = setup(engine, rows, layers, linear, 4000, 80 + sid + width)
+    t, x, weights, net, data = setup(engine, rows, layers, linear, 12001, 80 + sid + width)
     schema = jets.Schema(t[:, 1:])
     pre, acts = jets.forward(schema, weights, layers, linear, x)
     R = len(t)
@@ -196,6 +199,40 @@ def test_tensor_tier_narrow_layers(engine, sid, width):
     for k in ('forward_ws', 'backward_ws', 'backward_input_ws', 'weight_gradient_ws'):
         assert k in report, (k, sorted(report))
     assert gc.rowwise_error(out, acts[-1]).max() < 1e-5
+    loss, dout = jets.matching(acts[-1], targets, 1.0)
+    expected = jets.backward(schema, weights, layers, linear, pre, acts, dout)
+    assert abs(value - loss) <= 1e-5 * abs(loss)
+    assert gc.layer_error(grads, expected) < 1e-5
+
+
+@pytest.mark.parametrize('sid', [1, 3, 11], ids=[codegen.SCHEMAS[i][0] for i in (1, 3, 11)])
+def test_ffma_tier_wide_tiles(engine, sid):
+    """Exact-FP32 FFMA layers (orders <= 3 at tier 0) with 128-neuron tiles
+    and a 160-neuron layer (a full and a 32-row slice), 6,001 points (above
+    the automatic tier's point-tile epoch limit of 16,384 columns) over many
+    column tiles, against the float64 oracle at 1e-5."""
+    rows = codegen.SCHEMAS[sid][1]
+    V = len(rows[0])
+    layers = [V, 128, 160, 128, 1]
+    linear = [1, 0, 0, 0, 1]
+    t, x, weights, net, data = setup(engine, rows, layers, linear, 6001, 90 + sid)
+    schema = jets.Schema(t[:, 1:])
+    pre, acts = jets.forward(schema, weights, layers, linear, x)
+    out = engine.download(engine.evaluate(net, data))
+    assert gc.rowwise_error(out, acts[-1]).max() < 1e-5
+    R = len(t)
+    targets = (acts[-1] * 0.5).astype(np.float32)
+    tgt = engine.data(targets, t)
+    cost = engine.matching(net, data, tgt, list(range(R)), list(range(R)), 1, np.ones((R, 1, 1), np.float32))
+    engine.timing(True)
+    engine.timing_report()
+    try:
+        value, grads = engine.graph_evaluate(net, [cost], sum_graph(1))
+        report = engine.timing_report()
+    finally:
+        engine.timing(False)
+    for k in ('forward', 'backward', 'backward_input', 'weight_gradient'):
+        assert k in report, (k, sorted(report))
     loss, dout = jets.matching(acts[-1], targets, 1.0)
     expected = jets.backward(schema, weights, layers, linear, pre, acts, dout)
     assert abs(value - loss) <= 1e-5 * abs(loss)
