@@ -57,35 +57,53 @@ def gemm_flops(points, rows):
 
 
 class Clocks:
-    """nvidia-smi sampling during the timed region."""
+    """nvidia-smi sampling (every 50 ms) around the timed region. The sampler
+    is started before the warm-up steps, so that nvidia-smi's own start-up
+    does not overlap the timed steps (it added about 0.3 ms per step when it
+    did); ``stop(window)`` keeps the samples whose timestamps fall inside the
+    host wall-clock window of the timed region (or the first one after its
+    start when the region is shorter than the sampling period)."""
 
     def __init__(self, index):
         self.path = Path(tempfile.mkstemp(suffix='.csv')[1])
-        query = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
+        query = ('timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
                  'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
                  'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
         try:
             self.proc = subprocess.Popen(['nvidia-smi', f'--id={index}', f'--query-gpu={query}',
-                                          '--format=csv,noheader,nounits', '-lms', '200'],
+                                          '--format=csv,noheader,nounits', '-lms', '50'],
                                          stdout=open(self.path, 'w'), stderr=subprocess.DEVNULL)
         except FileNotFoundError:
             self.proc = None
 
-    def stop(self):
+    def stop(self, window=None):
         if self.proc is None:
             return None
+        import datetime
         self.proc.terminate()
         self.proc.wait()
         rows = [line.split(', ') for line in self.path.read_text().splitlines() if line.strip()]
         self.path.unlink()
+
+        def when(r):
+            try:
+                return datetime.datetime.strptime(r[0].strip(), '%Y/%m/%d %H:%M:%S.%f').timestamp()
+            except ValueError:
+                return None
+        if window is not None:
+            t0, t1 = window
+            stamped = [(when(r), r) for r in rows]
+            inside = [r for t, r in stamped if t is not None and t0 <= t <= t1]
+            after = [r for t, r in stamped if t is not None and t >= t0]
+            rows = inside or after[:1] or rows
         if not rows:
             return None
-        sm = [float(r[1]) for r in rows if r[1].replace('.', '').isdigit()]
+        sm = [float(r[2]) for r in rows if r[2].replace('.', '').isdigit()]
         names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
-        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.strip() == 'Active'})
+        reasons = sorted({n for r in rows for n, v in zip(names, r[6:10]) if v.strip() == 'Active'})
         return dict(sm_mhz=statistics.median(sm) if sm else None,
-                    sm_max_mhz=float(rows[0][2]) if rows[0][2].replace('.', '').isdigit() else None,
-                    samples=len(rows), reasons=reasons)
+                    sm_max_mhz=float(rows[0][3]) if rows[0][3].replace('.', '').isdigit() else None,
+                    samples=len(rows), reasons=reasons, interval_ms=50)
 
 
 def measured_peaks():
@@ -725,21 +743,30 @@ def run_b200(args):
         if dist is not None:
             dist.barrier()
 
+    clocks = Clocks(local)
+    time.sleep(0.5)  # the sampler is running before the warm-up
     for _ in range(args.warmup):
         engine.epoch(net, [cost])
-    sync_all()
-    engine.timing(True)
-    engine.timing_report()
-    clocks = Clocks(local)
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     sync_all()
+    wall0 = time.time()
     start.record(stream)
     for _ in range(args.steps):
         engine.epoch(net, [cost])
     stop.record(stream)
     torch.cuda.synchronize()
-    clock = clocks.stop()
+    wall1 = time.time()
+    clock = clocks.stop((wall0, wall1))
     ms = start.elapsed_time(stop) / args.steps
+    # per-kernel CUDA-event times (launch counts, shares, rooflines) from a
+    # second pass of the same steps: the events recorded around every launch
+    # are kept out of the timed region above
+    sync_all()
+    engine.timing(True)
+    engine.timing_report()
+    for _ in range(args.steps):
+        engine.epoch(net, [cost])
+    torch.cuda.synchronize()
     kernels = engine.timing_report()
     engine.timing(False)
     if dist is not None:
@@ -807,6 +834,9 @@ def run_b200(args):
             line['parity'] = ref.get('parity')
             line['config3_integral'] = same_gpu_comparison(local, config3_workload(), warm=3, iterations=10,
                                                            batches=3, kernels=True)
+            # the same at tier 2: 3xTF32 tensor-core layers (tier 0 keeps exact FP32 at order 2)
+            line['config3_integral_tensor'] = same_gpu_comparison(local, config3_workload(), warm=3, iterations=10,
+                                                                   batches=3, kernels=True, tier=2)
             if not args.no_large_configs:
                 peaks, source = measured_peaks()
                 for key, make, ref_points in (('config4', config4_workload, 262144),
@@ -833,7 +863,8 @@ def main():
     p.add_argument('--reference-points', type=int, default=128)
     p.add_argument('--no-cpu-baseline', action='store_true')
     p.add_argument('--no-reference-cuda', action='store_true')
-    p.add_argument('--tier', type=int, default=0, help='0 automatic, 1 generic, 2 tensor cores')
+    p.add_argument('--tier', type=int, default=0,
+                   help='0 automatic, 1 generic, 2 tensor cores, 3 point-tile epochs, 4 exact-FP32 FFMA')
     p.add_argument('--no-large-configs', action='store_true', help='skip the config-4 and config-5 legs')
     p.add_argument('--no-scaling-legs', action='store_true',
                    help='skip the order sweep and the config-3 training run (both run at every N)')

@@ -292,8 +292,9 @@ int cpde_kernel_timing_report(cpde_engine* h, cpde_sink report, void* ctx) {
 
 int cpde_set_tier(cpde_engine* h, int32_t tier) {
     return guard(h, [&] {
-        cpde::require(tier >= 0 && tier <= 3,
-                      "tier must be 0 (automatic), 1 (generic), 2 (tensor cores) or 3 (point-tile epochs)");
+        cpde::require(tier >= 0 && tier <= 4,
+                      "tier must be 0 (automatic), 1 (generic), 2 (tensor cores), 3 (point-tile epochs) or 4 "
+                      "(exact-FP32 fast tier)");
         E(h).tier = tier;
     });
 }

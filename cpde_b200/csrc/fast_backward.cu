@@ -73,17 +73,25 @@ struct FastBackward {
                 // one CTA per SM over the (N/128) x (M/128) tiles
                 static bool wg_ready[64] = {};
                 if (!wg_ready[e.device & 63]) {
-                    allow_smem(ws::k_wgrad_ws, ws::kWgSmem);
+                    allow_smem(ws::k_wgrad_ws<128>, ws::kWgSmem);
+                    allow_smem(ws::k_wgrad_ws<64>, ws::kWgSmem64);
                     wg_ready[e.device & 63] = true;
                 }
-                const int ny = (N + tcg::BM - 1) / tcg::BM, nz = (M + tcg::BM - 1) / tcg::BM;
+                const bool narrow = M <= 64 && N <= 64;  // 64-neuron slices, a deeper ring
+                const int nb = narrow ? 64 : 128;
+                const int ny = (N + nb - 1) / nb, nz = (M + nb - 1) / nb;
                 splits = std::max(1L, std::min<long>(std::max(1, 148 / (ny * nz)), (cols + 31) / 32));
                 n.partial.reserve(size_t(splits) * M * (N + 1));
                 const CUtensorMap md = mn32_map(cur, M, cols), ma = mn32_map(n.act[l - 1].ptr, N, cols);
-                CPDE_RUN(e, "weight_gradient_ws",
-                         (ws::k_wgrad_ws<<<dim3(unsigned(splits), unsigned(ny), unsigned(nz)), ws::kWgThreads,
-                                           ws::kWgSmem, e.stream>>>(md, ma, M, N, cols, R, n.partial.ptr,
-                                                                    e.tc_error.ptr)));
+                const dim3 wgrid = dim3(unsigned(splits), unsigned(ny), unsigned(nz));
+                if (narrow)
+                    CPDE_RUN(e, "weight_gradient_ws",
+                             (ws::k_wgrad_ws<64><<<wgrid, ws::kWgThreads, ws::kWgSmem64, e.stream>>>(
+                                 md, ma, M, N, cols, R, n.partial.ptr, e.tc_error.ptr)));
+                else
+                    CPDE_RUN(e, "weight_gradient_ws",
+                             (ws::k_wgrad_ws<128><<<wgrid, ws::kWgThreads, ws::kWgSmem, e.stream>>>(
+                                 md, ma, M, N, cols, R, n.partial.ptr, e.tc_error.ptr)));
             } else if (M <= 64 && N <= 64) {
                 // 64 x 64 tiles of 64 threads, about eight CTAs per SM
                 splits = std::max(1L, std::min<long>(148L * 8, (cols + 63) / 64));
@@ -217,7 +225,7 @@ struct FastBackward {
 }  // namespace
 
 void Engine::fast_backward(NetRecord& n, Context& ctx, int points, float* target, bool skip_output) {
-    with_schema(ctx.static_id, FastBackward{*this, n, points, target, use_tensor_cores(tier, ctx), skip_output});
+    with_schema(ctx.static_id, FastBackward{*this, n, points, target, use_tensor_cores(tier, ctx, n), skip_output});
 }
 
 }  // namespace cpde

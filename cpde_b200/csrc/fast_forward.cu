@@ -104,7 +104,7 @@ struct FastForward {
 }  // namespace
 
 void Engine::fast_forward(NetRecord& n, Context& ctx, int points, bool hidden_only) {
-    with_schema(ctx.static_id, FastForward{*this, n, points, use_tensor_cores(tier, ctx), hidden_only});
+    with_schema(ctx.static_id, FastForward{*this, n, points, use_tensor_cores(tier, ctx, n), hidden_only});
 }
 
 }  // namespace cpde

@@ -777,9 +777,9 @@ __global__ void __launch_bounds__(THREADS, 1) k_backward_wide(const __grid_const
 }
 
 // ---------------------------------------------------------------------------
-// Weight gradient of a hidden layer: G (a 128-neuron slice of this layer x a
-// 128-neuron slice of the previous layer, plus the bias column) = sum over
-// this CTA's columns of dZ[:, c] Y_prev[:, c]^T. Per 32-column stage, TMA brings 4
+// Weight gradient of a hidden layer: G (an NB-neuron slice of this layer x an
+// NB-neuron slice of the previous layer, plus the bias column) = sum over
+// this CTA's columns of dZ[:, c] Y_prev[:, c]^T. Per 32-column stage, TMA brings NB/32
 // boxes of 32 neurons x 32 columns of each operand (128-byte swizzle with
 // 32-byte atoms, the layout of MN-major TF32 operands). The split warps move
 // dZ through registers into tensor memory as the K-major A operand (thread =
@@ -788,27 +788,49 @@ __global__ void __launch_bounds__(THREADS, 1) k_backward_wide(const __grid_const
 // raw operand (its hi part) as the MN-major B operand, so shared memory
 // carries each operand once per MMA term instead of also serving the A side.
 // Two MMA issuers take the even and the odd stages, each into its own
-// 128 x 128 accumulator. The tensor core's FP32 accumulation does not round to
+// 128 x NB accumulator. The tensor core's FP32 accumulation does not round to
 // nearest, so a sum over thousands of column chunks in one accumulator drifts
 // (measured: 6e-4 normwise on config 5's gradients against the float64
 // oracle); each accumulator therefore sums only kWgSegment of its issuer's
 // chunks before four drain warps fold it into a round-to-nearest FP32 sum in
 // shared memory and release it. The second issuer's segments are offset by
 // half a segment, so the two drains do not stall both issuers at once.
-// grid = (CTAs, N / 128, M / 128): CTAs that share blockIdx.x take the same
+// grid = (CTAs, N / NB, M / NB): CTAs that share blockIdx.x take the same
 // chunks at about the same time, so the slices of dZ and Y_prev that several
 // of them read come from L2.
+// Slices of NB = 64 neurons (layers of at most 64 x 64): each stage is half
+// as large, so the ring holds six stages instead of three; with 128-neuron
+// slices of a 64-neuron layer half of every stage was zeros and three
+// stages of 32 columns kept too few bytes in flight to cover the HBM
+// latency (0.32 ms for 0.67 GB on config 3, 2.1 TB/s). The MMAs keep
+// M = 128 (the A lanes 64-127 are never written and their accumulator rows
+// never read) with N = 64.
 
-constexpr int kWgStages = 3;
 constexpr int kWgSegment = 16;            // chunks one accumulator sums before a drain
 constexpr int kWgBox = 32 * 32 * 4;       // 32 neurons x 32 columns
-constexpr int kWgOperand = 4 * kWgBox;    // 128 neurons
-constexpr int kWgStage = 3 * kWgOperand;  // dZ raw, Y raw (= hi), Y lo
-constexpr int kWgSums = 128 * 128 * 4;    // FP32 sums [column n][neuron m]
-constexpr int kWgSmem = kWgStages * kWgStage + kWgSums + 1024 + 256;
-constexpr int kWgEpilogueWarp = 6, kWgSecondMmaWarp = 10, kWgDrainWarp = 11;
-constexpr int kWgThreads = 480;  // producer, MMA, 4 split warps, 4 lo warps, second MMA issuer, 4 drain warps
-constexpr uint32_t kWgAccColumns = 128, kWgTmemColumns = 512, kWgSecondAcc = 384;
+constexpr int kWgEpilogueWarp = 6, kWgSecondMmaWarp = 10, kWgDrainWarp = 11, kWgSecondSplitWarp = 15;
+// producer, MMA, 4 split warps (even chunks), 4 lo warps, second MMA issuer, 4 drain warps, 4 split warps (odd chunks)
+constexpr int kWgThreads = 608;
+constexpr uint32_t kWgTmemColumns = 512;
+
+template <int NB>
+struct WgShape {
+    static_assert(NB == 64 || NB == 128, "weight-gradient slices are 64 or 128 neurons");
+    static constexpr int kBoxes = NB / 32;
+    static constexpr int kOperand = kBoxes * kWgBox;  // bytes of one operand slice of a chunk
+    static constexpr int kStage = 3 * kOperand;       // dZ raw, Y raw (= hi), Y lo
+    static constexpr int kStages = NB == 128 ? 3 : 6;
+    static constexpr int kSums = NB * NB * 4;         // FP32 sums [column n][neuron m]
+    static constexpr int kBias = 2 * 128 * 4;         // the two split groups' bias sums
+    static constexpr int kSmem = kStages * kStage + kSums + kBias + 1024 + 256;
+    // tensor memory: accumulator 0 at column 0, accumulator 1 at kSecondAcc, the
+    // dZ hi/lo of stage st at kDz + 64 st (+32)
+    static constexpr uint32_t kSecondAcc = NB == 128 ? 384 : 64;
+    static constexpr uint32_t kDz = 128;
+    static_assert(kDz + 64 * kStages <= (NB == 128 ? kSecondAcc : kWgTmemColumns), "tensor memory overlap");
+};
+constexpr int kWgSmem = WgShape<128>::kSmem;
+constexpr int kWgSmem64 = WgShape<64>::kSmem;
 
 // element (mn, k) of such an operand, in floats from its start
 __device__ __forceinline__ int mn32_index(int mn, int k) {
@@ -830,21 +852,27 @@ __device__ __forceinline__ int wg_segment_end(int w, int k, int count) {
     return 2 * last_local + w;
 }
 
-static __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_constant__ CUtensorMap map_dz,
+template <int NB>
+__global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_constant__ CUtensorMap map_dz,
                                                             const __grid_constant__ CUtensorMap map_y, int M, int N,
                                                             long columns, int R, float* __restrict__ partials,
                                                             int* error) {
+    using G = WgShape<NB>;
+    constexpr int kStages = G::kStages;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    float* sums = reinterpret_cast<float*>(base + kWgStages * kWgStage);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(base + kWgStages * kWgStage + kWgSums);
-    uint64_t *full = bars, *split = bars + kWgStages, *empty = bars + 2 * kWgStages, *drain = bars + 3 * kWgStages;
+    float* sums = reinterpret_cast<float*>(base + kStages * G::kStage);
+    float* bias_sums = reinterpret_cast<float*>(base + kStages * G::kStage + G::kSums);  // [split group][neuron]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(base + kStages * G::kStage + G::kSums + G::kBias);
+    uint64_t *full = bars, *split = bars + kStages, *empty = bars + 2 * kStages, *drain = bars + 3 * kStages;
     uint64_t *acc_full = drain + 1, *acc_empty = acc_full + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    volatile int* split_count = abort + 1;  // split-warp arrivals so far (4 per chunk)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kWgStages; ++s) {
+        *split_count = 0;
+        for (int s = 0; s < kStages; ++s) {
             tc::mbar_init(full + s, 1);
             tc::mbar_init(split + s, 8);
             tc::mbar_init(empty + s, 1);
@@ -865,27 +893,27 @@ static __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_
     __syncthreads();
     tc::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const int n_base = blockIdx.y * 128, m_base = blockIdx.z * 128;
+    const int n_base = blockIdx.y * NB, m_base = blockIdx.z * NB;
     // 32-column chunks dealt round-robin over the CTAs, so the whole grid
     // streams through one region of both operands at a time
     const long total_chunks = (columns + 31) / 32;
     const int chunks = blockIdx.x < total_chunks ? int((total_chunks - 1 - blockIdx.x) / gridDim.x + 1) : 0;
     const int mine[2] = {(chunks + 1) / 2, chunks / 2};  // chunks of issuer 0 (even) and 1 (odd)
     auto chunk_start = [&](int it) { return 32L * ((long)blockIdx.x + (long)it * gridDim.x); };
-    // stage st: [dZ raw][Y raw = hi][Y lo]; tensor memory: issuer 0's accumulator [0, 128), stage st's dZ hi/lo
-    // at 128 + 64 st (+32), issuer 1's accumulator [384, 512)
-    auto stage_ptr = [&](int st, int part) { return reinterpret_cast<float*>(base + st * kWgStage + part * kWgOperand); };
-    auto dz_column = [](int st) { return kWgAccColumns + 64u * uint32_t(st); };
+    auto stage_ptr = [&](int st, int part) {
+        return reinterpret_cast<float*>(base + st * G::kStage + part * G::kOperand);
+    };
+    auto dz_column = [](int st) { return G::kDz + 64u * uint32_t(st); };
     float* out = partials + (size_t)blockIdx.x * M * (N + 1);
     if (warp == kProducerWarp) {
         if (lane == 0) {
-            // L2 prefetches run two ring depths ahead of the loads (the ring's
-            // three stages alone do not cover the HBM latency of a chunk)
-            constexpr int kPrefetch = 2 * kWgStages;
+            // L2 prefetches run two ring depths ahead of the loads (the ring
+            // alone does not cover the HBM latency of a chunk)
+            constexpr int kPrefetch = 2 * kStages;
             auto prefetch = [&](int it) {
                 if (it >= chunks) return;
                 const int c0 = int(chunk_start(it));
-                for (int j = 0; j < 4; ++j) {
+                for (int j = 0; j < G::kBoxes; ++j) {
                     tc::tma_prefetch_2d(&map_dz, m_base + 32 * j, c0);
                     tc::tma_prefetch_2d(&map_y, n_base + 32 * j, c0);
                 }
@@ -893,25 +921,25 @@ static __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_
             for (int k = 0; k < kPrefetch; ++k) prefetch(k);
             int it = 0;
             for (; it < chunks && !*abort; ++it) {
-                const int st = it % kWgStages;
-                if (!tc::mbar_wait_or_abort(empty + st, ((it / kWgStages) & 1) ^ 1, tcg::kWaitCycles, abort)) break;
-                tc::mbar_expect_tx(full + st, 2 * kWgOperand);
+                const int st = it % kStages;
+                if (!tc::mbar_wait_or_abort(empty + st, ((it / kStages) & 1) ^ 1, tcg::kWaitCycles, abort)) break;
+                tc::mbar_expect_tx(full + st, 2 * G::kOperand);
                 const int c0 = int(chunk_start(it));
-                for (int j = 0; j < 4; ++j) {
+                for (int j = 0; j < G::kBoxes; ++j) {
                     tc::tma_load_2d(stage_ptr(st, 0) + j * (kWgBox / 4), &map_dz, full + st, m_base + 32 * j, c0);
                     tc::tma_load_2d(stage_ptr(st, 1) + j * (kWgBox / 4), &map_y, full + st, n_base + 32 * j, c0);
                 }
                 prefetch(it + kPrefetch);
             }
-            for (int k = it > kWgStages ? it - kWgStages : 0; k < it; ++k)
-                if (!tc::mbar_wait(full + k % kWgStages, (k / kWgStages) & 1, tcg::kWaitCycles)) *abort = 1;
+            for (int k = it > kStages ? it - kStages : 0; k < it; ++k)
+                if (!tc::mbar_wait(full + k % kStages, (k / kStages) & 1, tcg::kWaitCycles)) *abort = 1;
         }
     } else if (warp == kMmaWarp || warp == kWgSecondMmaWarp) {
         // two issuers, the even and the odd chunks, each into its own accumulator
         if (lane == 0) {
-            constexpr uint32_t idesc = tc::idesc_tf32(128, 128) | (1u << 16);  // B (Y) MN-major, A (dZ) from TMEM
+            constexpr uint32_t idesc = tc::idesc_tf32(128, NB) | (1u << 16);  // B (Y) MN-major, A (dZ) from TMEM
             const int which = warp == kMmaWarp ? 0 : 1;
-            const uint32_t acc = which ? tmem + kWgSecondAcc : tmem;
+            const uint32_t acc = which ? tmem + G::kSecondAcc : tmem;
             int seg = 0, in_seg = 0;
             bool ok = true;
             for (int it = which; ok && it < chunks; it += 2) {
@@ -922,8 +950,8 @@ static __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_
                     ++seg;
                     in_seg = 0;
                 }
-                const int st = it % kWgStages;
-                if (!tc::mbar_wait_or_abort(split + st, (it / kWgStages) & 1, tcg::kWaitCycles, abort)) break;
+                const int st = it % kStages;
+                if (!tc::mbar_wait_or_abort(split + st, (it / kStages) & 1, tcg::kWaitCycles, abort)) break;
                 tc::tc_fence_after();
                 const uint32_t yh = tc::smem_u32(stage_ptr(st, 1)), yl = tc::smem_u32(stage_ptr(st, 2));
                 const uint32_t ah = tmem + dz_column(st), al = ah + 32;
@@ -942,50 +970,84 @@ static __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_
             tc::mma_commit(drain);
             if (!tc::mbar_wait(drain, 0, tcg::kWaitCycles)) *abort = 1;
         }
-    } else if (warp < kWgEpilogueWarp) {
-        // split warps: thread = neuron m (its TMEM lane); the stage's dZ row of
-        // that neuron into tensor memory (hi, lo) and its bias over value-row columns
+    } else if (warp < kWgEpilogueWarp || warp >= kWgSecondSplitWarp) {
+        // split warps, two groups of four (one warp per TMEM lane quarter) that
+        // take the even and the odd chunks: thread = neuron m (its TMEM lane);
+        // the stage's dZ row of that neuron into tensor memory (hi, lo) and its
+        // bias over value-row columns (the warps of lanes past the slice only
+        // keep the count). A chunk's round (shared-memory reads, conversion,
+        // tensor-memory stores and their wait, the barrier) took about 2,000
+        // cycles, longer than the chunk's MMAs or its HBM time, so one group
+        // alone set the kernel's pace; two groups overlap their rounds. (Taking
+        // two chunks per round in one group instead measured slower: config
+        // 2's weight gradient 0.42 -> 0.65 ms, as a batch's first MMAs then
+        // wait for its last chunk.) The groups still arrive in chunk order: an
+        // MMA issuer waits on a stage's barrier by phase parity, which is exact
+        // only if the stage's previous phase (chunk it - kStages, possibly the
+        // other group's) is complete when the wait starts; each warp therefore
+        // arrives for chunk it only once all 4 it arrivals of earlier chunks
+        // are in (split_count), while the groups' work overlaps.
+        const int group = warp >= kWgSecondSplitWarp ? 1 : 0;
         const int quarter = warp & 3, m = quarter * 32 + lane;
+        const bool mine_lane = quarter * 32 < NB;  // the same for the whole warp
         const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
         float bias = 0.f;
-        for (int it = 0; it < chunks; ++it) {
-            const int st = it % kWgStages;
-            if (!warp_wait(full + st, (it / kWgStages) & 1, abort)) break;
+        for (int it = group; it < chunks; it += 2) {
+            const int st = it % kStages;
+            if (!warp_wait(full + st, (it / kStages) & 1, abort)) break;
             tc::tc_fence_after();
-            const long c0 = chunk_start(it);
-            const int valid = int(min(32L, columns - c0));
-            const int first = int((R - c0 % R) % R);  // first value-row column of the stage
-            const float* z = stage_ptr(st, 0);
-            for (int c = first; c < valid; c += R) bias += z[mn32_index(m, c)];
+            if (mine_lane) {
+                const long c0 = chunk_start(it);
+                const int valid = int(min(32L, columns - c0));
+                const int first = int((R - c0 % R) % R);  // first value-row column of the stage
+                const float* z = stage_ptr(st, 0);
+                for (int c = first; c < valid; c += R) bias += z[mn32_index(m, c)];
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                float h[8], l[8];
+                for (int q = 0; q < 4; ++q) {
+                    float h[8], l[8];
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const int c = 8 * q + j;
-                    const float v = c < valid ? z[mn32_index(m, c)] : 0.f;
-                    h[j] = tc::tf32_round(v);
-                    l[j] = tc::tf32_round(v - h[j]);
+                    for (int j = 0; j < 8; ++j) {
+                        const int c = 8 * q + j;
+                        const float v = c < valid ? z[mn32_index(m, c)] : 0.f;
+                        h[j] = tc::tf32_round(v);
+                        l[j] = tc::tf32_round(v - h[j]);
+                    }
+                    tc::tmem_st8(lane_base + dz_column(st) + 8 * q, h);
+                    tc::tmem_st8(lane_base + dz_column(st) + 32 + 8 * q, l);
                 }
-                tc::tmem_st8(lane_base + dz_column(st) + 8 * q, h);
-                tc::tmem_st8(lane_base + dz_column(st) + 32 + 8 * q, l);
+                tc::tmem_wait_st();
             }
-            tc::tmem_wait_st();
             tc::tc_fence_before();
             __syncwarp();
-            if (lane == 0) tc::mbar_arrive(split + st);
+            if (lane == 0) {
+                bool in_order = true;
+                const long long start = clock64();
+                while (*split_count < 4 * it) {
+                    if (*abort || clock64() - start > tcg::kWaitCycles) {
+                        *abort = 1;
+                        in_order = false;
+                        break;
+                    }
+                }
+                if (in_order) {
+                    tc::mbar_arrive(split + st);
+                    __threadfence_block();  // the arrival before the count that releases the next chunk's
+                    atomicAdd(const_cast<int*>(split_count), 1);
+                }
+            }
+            if (!__shfl_sync(0xffffffffu, int(!*abort), 0)) break;
         }
-        if (blockIdx.y == 0 && m_base + m < M) out[(size_t)N * M + m_base + m] = bias;
+        if (mine_lane) bias_sums[group * 128 + m] = bias;
     } else if (warp < kWgDrainWarp) {
         // lo warps: the TF32 lo part of Y_prev of every stage (the raw operand
         // is its hi part; the columns past the end of the data arrive as zeros
         // from the tensor map)
         const int tid = threadIdx.x - kWgEpilogueWarp * 32;
         for (int it = 0; it < chunks; ++it) {
-            const int st = it % kWgStages;
-            if (!warp_wait(full + st, (it / kWgStages) & 1, abort)) break;
+            const int st = it % kStages;
+            if (!warp_wait(full + st, (it / kStages) & 1, abort)) break;
             split_lo_range(reinterpret_cast<const float4*>(stage_ptr(st, 1)), reinterpret_cast<float4*>(stage_ptr(st, 2)),
-                           kWgOperand / 16, tid);
+                           G::kOperand / 16, tid);
             tc::fence_proxy_async();
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(split + st);
@@ -994,8 +1056,10 @@ static __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_
         // drain warps: thread = neuron m (its TMEM lane); every finished segment of
         // either accumulator, in the order the segments end, added into sums[n][m]
         const int quarter = warp & 3, m = quarter * 32 + lane;
+        const bool mine_lane = quarter * 32 < NB;  // the same for the whole warp
         const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
-        for (int c = 0; c < 128; ++c) sums[c * 128 + m] = 0.f;
+        if (mine_lane)
+            for (int c = 0; c < NB; ++c) sums[c * NB + m] = 0.f;
         const int total[2] = {wg_segments(0, mine[0]), wg_segments(1, mine[1])};
         int next[2] = {0, 0};
         bool ok = true;
@@ -1007,21 +1071,23 @@ static __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_
             ok = warp_wait(acc_full + w, next[w] & 1, abort);
             if (!ok) break;
             tc::tc_fence_after();
-            const uint32_t acc = lane_base + (w ? kWgSecondAcc : 0u);
-            for (int c0 = 0; c0 < 128; c0 += 16) {
-                float v[16];
-                tc::tmem_read<16>(acc + c0, v);
+            if (mine_lane) {
+                const uint32_t acc = lane_base + (w ? G::kSecondAcc : 0u);
+                for (int c0 = 0; c0 < NB; c0 += 16) {
+                    float v[16];
+                    tc::tmem_read<16>(acc + c0, v);
 #pragma unroll
-                for (int j = 0; j < 16; ++j) sums[(c0 + j) * 128 + m] += v[j];
+                    for (int j = 0; j < 16; ++j) sums[(c0 + j) * NB + m] += v[j];
+                }
             }
             tc::tc_fence_before();
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(acc_empty + w);
             ++next[w];
         }
-        if (ok)
-            for (int c = 0; c < 128; ++c)  // the slices of layers narrower than 128 neurons end early
-                if (m_base + m < M && n_base + c < N) out[m_base + m + (size_t)(n_base + c) * M] = sums[c * 128 + m];
+        if (ok && mine_lane)
+            for (int c = 0; c < NB; ++c)  // the slices of layers narrower than the slice end early
+                if (m_base + m < M && n_base + c < N) out[m_base + m + (size_t)(n_base + c) * M] = sums[c * NB + m];
     }
     tc::tc_fence_before();
     __syncthreads();
@@ -1029,6 +1095,9 @@ static __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_
         tc::tc_fence_after();
         tc::tmem_dealloc(tmem, kWgTmemColumns);
     }
+    // the bias column: both split groups' sums (written before the barrier above)
+    if (blockIdx.y == 0 && threadIdx.x < NB && m_base + threadIdx.x < M)
+        out[(size_t)N * M + m_base + threadIdx.x] = bias_sums[threadIdx.x] + bias_sums[128 + threadIdx.x];
     if (threadIdx.x == 0 && *abort) atomicExch(error, tcg::kErrMma);
 }
 

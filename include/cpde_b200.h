@@ -150,8 +150,9 @@ int cpde_kernel_timing(cpde_engine* engine, int32_t enable);
 int cpde_kernel_timing_report(cpde_engine* engine, cpde_sink report, void* context);
 /* Selects the execution tier: 0 automatic, 1 generic kernels only, 2 tensor-core
  * (tcgen05 3xTF32) GEMMs wherever the layer shapes allow, 3 the single-launch
- * point-tile epoch wherever it applies (matching costs on the fused head). No
- * reference counterpart. */
+ * point-tile epoch wherever it applies (matching costs on the fused head), 4
+ * the fused fast-tier kernels with exact-FP32 FFMA GEMMs only. No reference
+ * counterpart. */
 int cpde_set_tier(cpde_engine* engine, int32_t tier);
 
 /* Weight gradient of one layer without any device allocation. No counterpart

@@ -72,12 +72,21 @@ def test_config2_kernels(engine):
                       'backward_input_ws'], 1e-4)
 
 
-def test_config3_kernels(engine):
+@pytest.mark.parametrize('tier', [0, 2], ids=['auto', 'tensor'])
+def test_config3_kernels(engine, tier):
     """2 -> 64^3 -> 1 sigmoid, rows u, u_x, u_y, u_xx, u_yy, compiled integral
-    of (u_xx + u_yy + 1)^2 over points in the disk."""
+    of (u_xx + u_yy + 1)^2 over points in the disk: the automatic tier's
+    exact-FP32 FFMA layers and the tensor-core layers (64 neurons: paired
+    column tiles, 64-neuron weight-gradient slices), both at 1e-5."""
     w = bench.config3_workload(2048)
-    check(engine, w, ['input_forward', 'forward', 'head_expression', 'weight_gradient', 'backward',
-                      'backward_input'], 1e-5)
+    kernels = (['input_forward', 'forward_ws', 'head_expression', 'weight_gradient_ws', 'backward_ws',
+                'backward_input_ws'] if tier == 2 else
+               ['input_forward', 'forward', 'head_expression', 'weight_gradient', 'backward', 'backward_input'])
+    engine.set_tier(tier)
+    try:
+        check(engine, w, kernels, 1e-5)
+    finally:
+        engine.set_tier(0)
 
 
 def test_config4_kernels(engine):
