@@ -199,7 +199,13 @@ void Engine::reduce_costs(NetRecord& n, const std::vector<uint64_t>& ids) {
         auto& c = cost(ids[i]);
         offsets[i] = c.input_id ? dat(c.input_id).lo : 0;
     }
-    shard_offsets.upload(offsets, stream);
+    // a copy from pageable memory may wait for the stream to drain, which at
+    // every epoch left the GPU idle while the host enqueued the next one; the
+    // offsets change only with the cost set
+    if (offsets != shard_offsets_host) {
+        shard_offsets.upload(offsets, stream);
+        shard_offsets_host = offsets;
+    }
     shard_values.reserve(count);
     shard_keys.reserve(count);
     CPDE_RUN(*this, "pack_costs", k_pack_costs<<<grid_for(count), 256, 0, stream>>>(

@@ -174,6 +174,7 @@ class Engine {
     DeviceBuffer<double> shard_values;
     DeviceBuffer<long long> shard_keys;
     DeviceBuffer<int> shard_offsets;
+    std::vector<int> shard_offsets_host;  // what shard_offsets holds
     DeviceBuffer<float> gather_send, gather_recv;
     void check_device_errors();
 
