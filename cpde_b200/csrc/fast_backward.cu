@@ -86,11 +86,11 @@ struct FastBackward {
                 const dim3 wgrid = dim3(unsigned(splits), unsigned(ny), unsigned(nz));
                 if (narrow)
                     CPDE_RUN(e, "weight_gradient_ws",
-                             (ws::k_wgrad_ws<64><<<wgrid, ws::kWgThreads, ws::kWgSmem64, e.stream>>>(
+                             (ws::k_wgrad_ws<64><<<wgrid, ws::WgShape<64>::kThreads, ws::kWgSmem64, e.stream>>>(
                                  md, ma, M, N, cols, R, n.partial.ptr, e.tc_error.ptr)));
                 else
                     CPDE_RUN(e, "weight_gradient_ws",
-                             (ws::k_wgrad_ws<128><<<wgrid, ws::kWgThreads, ws::kWgSmem, e.stream>>>(
+                             (ws::k_wgrad_ws<128><<<wgrid, ws::WgShape<128>::kThreads, ws::kWgSmem, e.stream>>>(
                                  md, ma, M, N, cols, R, n.partial.ptr, e.tc_error.ptr)));
             } else if (M <= 64 && N <= 64) {
                 // 64 x 64 tiles of 64 threads, about eight CTAs per SM

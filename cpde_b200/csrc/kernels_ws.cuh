@@ -152,25 +152,25 @@ __device__ __forceinline__ void produce(const Ring& r, const CUtensorMap* map, l
         if (!tc::mbar_wait(r.full + k % S, (k / S) & 1, tcg::kWaitCycles)) *r.abort = 1;
 }
 
-// lo parts of float4 elements [0, count) of x4 into l4, strided over 128
+// lo parts of float4 elements [0, count) of x4 into l4, strided over `threads`
 // threads, eight loads in flight per thread. The tensor core reads an fp32
 // operand of a kind::tf32 MMA as its top 19 bits (sign, exponent, 10 mantissa
 // bits), so the raw slab already is the hi part, hi = trunc(x), and
 // lo = RN_tf32(x - trunc(x)) leaves x - hi - lo below 2^-21 |x|, the accuracy
 // of a split that rounds both parts.
-__device__ __forceinline__ void split_lo_range(const float4* x4, float4* l4, int count, int tid) {
+__device__ __forceinline__ void split_lo_range(const float4* x4, float4* l4, int count, int tid, int threads = 128) {
     constexpr int U = 8;
     auto lo = [](float x) { return tc::tf32_round(x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u)); };
-    for (int base = 0; base < count; base += 128 * U) {
+    for (int base = 0; base < count; base += threads * U) {
         float4 v[U];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-            const int i = base + tid + 128 * u;
+            const int i = base + tid + threads * u;
             v[u] = i < count ? x4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
         }
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-            const int i = base + tid + 128 * u;
+            const int i = base + tid + threads * u;
             if (i >= count) break;
             l4[i] = make_float4(lo(v[u].x), lo(v[u].y), lo(v[u].z), lo(v[u].w));
         }
@@ -809,8 +809,6 @@ __global__ void __launch_bounds__(THREADS, 1) k_backward_wide(const __grid_const
 constexpr int kWgSegment = 16;            // chunks one accumulator sums before a drain
 constexpr int kWgBox = 32 * 32 * 4;       // 32 neurons x 32 columns
 constexpr int kWgEpilogueWarp = 6, kWgSecondMmaWarp = 10, kWgDrainWarp = 11, kWgSecondSplitWarp = 15;
-// producer, MMA, 4 split warps (even chunks), 4 lo warps, second MMA issuer, 4 drain warps, 4 split warps (odd chunks)
-constexpr int kWgThreads = 608;
 constexpr uint32_t kWgTmemColumns = 512;
 
 template <int NB>
@@ -821,7 +819,15 @@ struct WgShape {
     static constexpr int kStage = 3 * kOperand;       // dZ raw, Y raw (= hi), Y lo
     static constexpr int kStages = NB == 128 ? 3 : 6;
     static constexpr int kSums = NB * NB * 4;         // FP32 sums [column n][neuron m]
-    static constexpr int kBias = 2 * 128 * 4;         // the two split groups' bias sums
+    // split warps: kSplitGroups groups of kSplitWarps (one per TMEM lane quarter
+    // the slice uses) take chunks it = group, group + kSplitGroups, ...
+    // (a third group of four warps for 128-neuron slices measured no faster)
+    static constexpr int kSplitGroups = NB == 128 ? 2 : 3;
+    // producer, MMA issuer, 4 split warps, 4 lo warps, second issuer, 4 drain warps, 4 split warps
+    static constexpr int kThreads = 608;
+    static constexpr int kSplitWarps = NB / 32;
+    static constexpr int kLoWarps = NB == 128 ? 4 : 6;
+    static constexpr int kBias = kSplitGroups * 128 * 4;  // the split groups' bias sums
     static constexpr int kSmem = kStages * kStage + kSums + kBias + 1024 + 256;
     // tensor memory: accumulator 0 at column 0, accumulator 1 at kSecondAcc, the
     // dZ hi/lo of stage st at kDz + 64 st (+32)
@@ -852,8 +858,36 @@ __device__ __forceinline__ int wg_segment_end(int w, int k, int count) {
     return 2 * last_local + w;
 }
 
+// Warp roles of k_wgrad_ws: 0 producer, 1 and 10 MMA issuers, 11-14 drain;
+// with 128-neuron slices split groups {2-5} and {15-18} and lo warps 6-9; with
+// 64-neuron slices split groups {4, 5}, {16, 17} and {8, 9} (the warps of lane
+// quarters 0 and 1) and lo warps 2, 3, 6, 7, 15, 18.
 template <int NB>
-__global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_constant__ CUtensorMap map_dz,
+__device__ __forceinline__ int wg_split_group(int warp) {
+    if (NB == 128) return warp >= 2 && warp <= 5 ? 0 : warp >= kWgSecondSplitWarp ? 1 : -1;
+    switch (warp) {
+        case 4: case 5: return 0;
+        case 16: case 17: return 1;
+        case 8: case 9: return 2;
+        default: return -1;
+    }
+}
+template <int NB>
+__device__ __forceinline__ int wg_lo_warp(int warp) {  // index among the lo warps, or -1
+    if (NB == 128) return warp >= kWgEpilogueWarp && warp < kWgSecondMmaWarp ? warp - kWgEpilogueWarp : -1;
+    switch (warp) {
+        case 2: return 0;
+        case 3: return 1;
+        case 6: return 2;
+        case 7: return 3;
+        case 15: return 4;
+        case 18: return 5;
+        default: return -1;
+    }
+}
+
+template <int NB>
+__global__ void __launch_bounds__(WgShape<NB>::kThreads, 1) k_wgrad_ws(const __grid_constant__ CUtensorMap map_dz,
                                                             const __grid_constant__ CUtensorMap map_y, int M, int N,
                                                             long columns, int R, float* __restrict__ partials,
                                                             int* error) {
@@ -970,29 +1004,32 @@ __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_constan
             tc::mma_commit(drain);
             if (!tc::mbar_wait(drain, 0, tcg::kWaitCycles)) *abort = 1;
         }
-    } else if (warp < kWgEpilogueWarp || warp >= kWgSecondSplitWarp) {
-        // split warps, two groups of four (one warp per TMEM lane quarter) that
-        // take the even and the odd chunks: thread = neuron m (its TMEM lane);
+    } else if (wg_split_group<NB>(warp) >= 0) {
+        // split warps, in groups (one warp per TMEM lane quarter of the slice)
+        // that take alternate chunks: thread = neuron m (its TMEM lane);
         // the stage's dZ row of that neuron into tensor memory (hi, lo) and its
         // bias over value-row columns (the warps of lanes past the slice only
         // keep the count). A chunk's round (shared-memory reads, conversion,
         // tensor-memory stores and their wait, the barrier) took about 2,000
         // cycles, longer than the chunk's MMAs or its HBM time, so one group
-        // alone set the kernel's pace; two groups overlap their rounds. (Taking
+        // alone set the kernel's pace; the groups overlap their rounds (two of
+        // four warps for 128-neuron slices, three of two for 64-neuron slices,
+        // whose lane quarters 2 and 3 have no split work: 0.218 -> 0.177 ms on
+        // config 3's layers against two groups). (Taking
         // two chunks per round in one group instead measured slower: config
         // 2's weight gradient 0.42 -> 0.65 ms, as a batch's first MMAs then
         // wait for its last chunk.) The groups still arrive in chunk order: an
         // MMA issuer waits on a stage's barrier by phase parity, which is exact
         // only if the stage's previous phase (chunk it - kStages, possibly the
         // other group's) is complete when the wait starts; each warp therefore
-        // arrives for chunk it only once all 4 it arrivals of earlier chunks
-        // are in (split_count), while the groups' work overlaps.
-        const int group = warp >= kWgSecondSplitWarp ? 1 : 0;
+        // arrives for chunk it only once all kSplitWarps x it arrivals of
+        // earlier chunks are in (split_count), while the groups' work overlaps.
+        const int group = wg_split_group<NB>(warp);
         const int quarter = warp & 3, m = quarter * 32 + lane;
         const bool mine_lane = quarter * 32 < NB;  // the same for the whole warp
         const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
         float bias = 0.f;
-        for (int it = group; it < chunks; it += 2) {
+        for (int it = group; it < chunks; it += G::kSplitGroups) {
             const int st = it % kStages;
             if (!warp_wait(full + st, (it / kStages) & 1, abort)) break;
             tc::tc_fence_after();
@@ -1022,7 +1059,7 @@ __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_constan
             if (lane == 0) {
                 bool in_order = true;
                 const long long start = clock64();
-                while (*split_count < 4 * it) {
+                while (*split_count < G::kSplitWarps * it) {
                     if (*abort || clock64() - start > tcg::kWaitCycles) {
                         *abort = 1;
                         in_order = false;
@@ -1038,16 +1075,16 @@ __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_constan
             if (!__shfl_sync(0xffffffffu, int(!*abort), 0)) break;
         }
         if (mine_lane) bias_sums[group * 128 + m] = bias;
-    } else if (warp < kWgDrainWarp) {
+    } else if (wg_lo_warp<NB>(warp) >= 0) {
         // lo warps: the TF32 lo part of Y_prev of every stage (the raw operand
         // is its hi part; the columns past the end of the data arrive as zeros
         // from the tensor map)
-        const int tid = threadIdx.x - kWgEpilogueWarp * 32;
+        const int tid = wg_lo_warp<NB>(warp) * 32 + lane;
         for (int it = 0; it < chunks; ++it) {
             const int st = it % kStages;
             if (!warp_wait(full + st, (it / kStages) & 1, abort)) break;
             split_lo_range(reinterpret_cast<const float4*>(stage_ptr(st, 1)), reinterpret_cast<float4*>(stage_ptr(st, 2)),
-                           G::kOperand / 16, tid);
+                           G::kOperand / 16, tid, G::kLoWarps * 32);
             tc::fence_proxy_async();
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(split + st);
@@ -1096,8 +1133,11 @@ __global__ void __launch_bounds__(kWgThreads, 1) k_wgrad_ws(const __grid_constan
         tc::tmem_dealloc(tmem, kWgTmemColumns);
     }
     // the bias column: both split groups' sums (written before the barrier above)
-    if (blockIdx.y == 0 && threadIdx.x < NB && m_base + threadIdx.x < M)
-        out[(size_t)N * M + m_base + threadIdx.x] = bias_sums[threadIdx.x] + bias_sums[128 + threadIdx.x];
+    if (blockIdx.y == 0 && threadIdx.x < NB && m_base + threadIdx.x < M) {
+        float b = 0.f;
+        for (int g = 0; g < G::kSplitGroups; ++g) b += bias_sums[g * 128 + threadIdx.x];
+        out[(size_t)N * M + m_base + threadIdx.x] = b;
+    }
     if (threadIdx.x == 0 && *abort) atomicExch(error, tcg::kErrMma);
 }
 
