@@ -834,9 +834,10 @@ def run_b200(args):
             line['parity'] = ref.get('parity')
             line['config3_integral'] = same_gpu_comparison(local, config3_workload(), warm=3, iterations=10,
                                                            batches=3, kernels=True)
-            # the same at tier 2: 3xTF32 tensor-core layers (tier 0 keeps exact FP32 at order 2)
-            line['config3_integral_tensor'] = same_gpu_comparison(local, config3_workload(), warm=3, iterations=10,
-                                                                   batches=3, kernels=True, tier=2)
+            # the same at tier 4: exact-FP32 FFMA layers (the automatic tier runs this
+            # 64-wide order-2 network on the 3xTF32 tensor cores)
+            line['config3_integral_ffma'] = same_gpu_comparison(local, config3_workload(), warm=3, iterations=10,
+                                                                 batches=3, kernels=True, tier=4)
             if not args.no_large_configs:
                 peaks, source = measured_peaks()
                 for key, make, ref_points in (('config4', config4_workload, 262144),

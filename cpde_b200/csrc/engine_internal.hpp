@@ -135,14 +135,25 @@ inline CUtensorMap mn32_map(const float* base, int inner, long rows) {
 
 // Tier policy for the fast tier's GEMMs. Tier 2 forces tensor cores
 // (3xTF32), tier 4 exact-FP32 FFMA. The automatic tiers (0, and 3 for its
-// size limit) use tensor cores at derivative orders 4-6 (tolerance 1e-4) and
-// FFMA at orders 0-3 (tolerance 1e-5): 3xTF32 gradients sat at 4-5e-6 from
-// the reference's FP32 results on the benchmarked networks at orders 0-3, but
-// at 2.3e-5 from the float64 oracle on a polynomial cost of 517 points
-// (2 -> 128^3 -> 1, order 2), where the residual's gradient cancels; exact
-// FP32 stays inside 1e-5 there.
-inline bool use_tensor_cores(int tier, const Context& ctx, const NetRecord&) {
-    return tier == 2 || ((tier == 0 || tier == 3) && ctx.plan.max_order >= 4);
+// size limit) use tensor cores at derivative orders 4-6 (tolerance 1e-4). At
+// orders 0-3 (tolerance 1e-5) they use them only when every hidden layer has
+// at most kNarrowTensorWidth neurons, so that every tensor-core GEMM has at
+// most 64 inputs and takes the lo-first term order (ws::issue_mmas): over 96
+// integral and polynomial cases of orders 2-3 against the float64 oracle
+// (widths 32/64, 517 and 3,000 points) the worst 3xTF32 gradient error is
+// then 1.1e-6 (5.1e-6 with the interleaved order), and config 3 (2 -> 64^3
+// -> 1, 262,144 points) sits 2.5e-6 from the reference's FP32 gradients.
+// Wider layers keep FFMA at orders <= 3: with K = 128 a polynomial cost of
+// 517 points (2 -> 128^3 -> 1, order 2), where the residual's gradient
+// cancels, came to 2.3e-5 from the oracle, while exact FP32 stays inside 1e-5.
+constexpr int kNarrowTensorWidth = 64;
+inline bool use_tensor_cores(int tier, const Context& ctx, const NetRecord& n) {
+    if (tier == 2) return true;
+    if (tier != 0 && tier != 3) return false;
+    if (ctx.plan.max_order >= 4) return true;
+    for (int l = 1; l + 1 < int(n.neurons.size()); ++l)
+        if (n.neurons[l] > kNarrowTensorWidth) return false;
+    return true;
 }
 
 }  // namespace cpde

@@ -210,8 +210,24 @@ __host__ __device__ constexpr int mma_issuers(int S, int slabs) { return S > sla
 // measured slower); each slab's stage is released by a commit once its MMAs
 // have read it. Slab counter `it` runs over all the CTA's slabs in ring
 // order, the other issuer's included.
+//
+// Term order. The tensor core's FP32 accumulation truncates, so every MMA
+// into an accumulator that already holds the large hi*hi sum costs up to an
+// ulp of it, whatever it adds. With `group` = 0 each K step issues
+// lo*hi, hi*lo, hi*hi in turn (3 K/8 such adds). With `group` = g > 0 the
+// tile's slabs go in groups of g: first the two lo terms of all the group's
+// slabs, then its hi*hi terms, and only then are its stages released, so in
+// the first group the lo terms land on a small accumulator (K/8 adds at full
+// size when one group covers the tile). lo_first_group() uses one group per
+// tile (or per tile half: the slabs of the two halves of a paired work item
+// touch disjoint accumulator lanes) for layers of at most 64 inputs, whose
+// one or two slabs per group leave the rest of the ring to the loads ahead.
+// the term-order group of a layer with kslabs K slabs per tile (half)
+__device__ __forceinline__ int lo_first_group(int kslabs) { return kslabs <= 2 ? kslabs : 0; }
+
 template <int N, int SLAB, int S = STAGES>
-__device__ __forceinline__ void issue_mmas(const Ring& r, uint32_t tmem, long tiles, int slabs, int which) {
+__device__ __forceinline__ void issue_mmas(const Ring& r, uint32_t tmem, long tiles, int slabs, int which,
+                                           int group = 0) {
     constexpr uint32_t idesc = tc::idesc_tf32(128, N);
     const int issuers = mma_issuers(S, slabs);
     bool ok = tc::mbar_wait_or_abort(r.a_ready, 0, tcg::kWaitCycles, r.abort);
@@ -223,21 +239,51 @@ __device__ __forceinline__ void issue_mmas(const Ring& r, uint32_t tmem, long ti
         ok = tc::mbar_wait_or_abort(r.acc_empty + a, ((local >> 1) & 1) ^ 1, tcg::kWaitCycles, r.abort);
         tc::tc_fence_after();
         const uint32_t d = tmem + kAccColumn + a * 128;
-        for (int s = 0; ok && s < slabs; ++s, ++it) {
-            const int st = it % S;
-            ok = tc::mbar_wait_or_abort(r.split + st, (it / S) & 1, tcg::kWaitCycles, r.abort);
-            if (!ok) break;
-            tc::tc_fence_after();
-            const uint32_t bh = tc::smem_u32(r.hi + st * (SLAB / 4)), bl = tc::smem_u32(r.lo + st * (SLAB / 4));
+        const uint32_t first = it;
+        if (group == 0) {
+            for (int s = 0; ok && s < slabs; ++s) {
+                const int st = (first + s) % S;
+                ok = tc::mbar_wait_or_abort(r.split + st, ((first + s) / S) & 1, tcg::kWaitCycles, r.abort);
+                if (!ok) break;
+                tc::tc_fence_after();
+                const uint32_t bh = tc::smem_u32(r.hi + st * (SLAB / 4)), bl = tc::smem_u32(r.lo + st * (SLAB / 4));
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-                const uint32_t ah = tmem + s * 32 + kk * 8, al = ah + 128;
-                tc::mma_tf32_ts(d, al, tc::desc_k_sw128(bh + kk * 32), idesc, (s | kk) != 0);
-                tc::mma_tf32_ts(d, ah, tc::desc_k_sw128(bl + kk * 32), idesc, 1);
-                tc::mma_tf32_ts(d, ah, tc::desc_k_sw128(bh + kk * 32), idesc, 1);
+                for (int kk = 0; kk < 4; ++kk) {
+                    const uint32_t ah = tmem + s * 32 + kk * 8, al = ah + 128;
+                    tc::mma_tf32_ts(d, al, tc::desc_k_sw128(bh + kk * 32), idesc, (s | kk) != 0);
+                    tc::mma_tf32_ts(d, ah, tc::desc_k_sw128(bl + kk * 32), idesc, 1);
+                    tc::mma_tf32_ts(d, ah, tc::desc_k_sw128(bh + kk * 32), idesc, 1);
+                }
+                tc::mma_commit(r.empty + st);
             }
-            tc::mma_commit(r.empty + st);
+        } else {
+            for (int g0 = 0; ok && g0 < slabs; g0 += group) {
+                const int g1 = min(g0 + group, slabs);
+                for (int s = g0; ok && s < g1; ++s) {  // the lo terms of the group
+                    const int st = (first + s) % S;
+                    ok = tc::mbar_wait_or_abort(r.split + st, ((first + s) / S) & 1, tcg::kWaitCycles, r.abort);
+                    if (!ok) break;
+                    tc::tc_fence_after();
+                    const uint32_t bh = tc::smem_u32(r.hi + st * (SLAB / 4)),
+                                   bl = tc::smem_u32(r.lo + st * (SLAB / 4));
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk) {
+                        const uint32_t ah = tmem + s * 32 + kk * 8, al = ah + 128;
+                        tc::mma_tf32_ts(d, al, tc::desc_k_sw128(bh + kk * 32), idesc, (s | kk) != 0);
+                        tc::mma_tf32_ts(d, ah, tc::desc_k_sw128(bl + kk * 32), idesc, 1);
+                    }
+                }
+                for (int s = g0; ok && s < g1; ++s) {  // its hi*hi terms; then the stage is free
+                    const int st = (first + s) % S;
+                    const uint32_t bh = tc::smem_u32(r.hi + st * (SLAB / 4));
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        tc::mma_tf32_ts(d, tmem + s * 32 + kk * 8, tc::desc_k_sw128(bh + kk * 32), idesc, 1);
+                    tc::mma_commit(r.empty + st);
+                }
+            }
         }
+        it = first + slabs;
         if (ok) tc::mma_commit(r.acc_full + a);
     }
     // every MMA this thread issued has completed once this commit arrives
@@ -327,7 +373,9 @@ __global__ void __launch_bounds__(THREADS, 1) k_forward_ws(const __grid_constant
     if (warp == kProducerWarp) {
         if (lane == 0) produce<T::SLAB>(r, &map_x, items, T::COLS, T::N, kslabs, halves);
     } else if (warp == kMmaWarp || warp == kSecondMmaWarp) {
-        if (lane == 0) issue_mmas<T::N, T::SLAB>(r, tmem, items, kslabs * halves, warp == kMmaWarp ? 0 : 1);
+        if (lane == 0)
+            issue_mmas<T::N, T::SLAB>(r, tmem, items, kslabs * halves, warp == kMmaWarp ? 0 : 1,
+                                      lo_first_group(kslabs));
     } else if (warp < kEpilogueWarp) {
         split_all<T::SLAB>(r, items, T::N, kslabs * halves);
     } else {
@@ -396,7 +444,9 @@ __global__ void __launch_bounds__(THREADS, 1) k_backward_ws(const __grid_constan
     if (warp == kProducerWarp) {
         if (lane == 0) produce<T::SLAB, S>(r, &map_dz, items, T::COLS, T::N, kslabs, halves);
     } else if (warp == kMmaWarp || warp == kSecondMmaWarp) {
-        if (lane == 0) issue_mmas<T::N, T::SLAB, S>(r, tmem, items, kslabs * halves, warp == kMmaWarp ? 0 : 1);
+        if (lane == 0)
+            issue_mmas<T::N, T::SLAB, S>(r, tmem, items, kslabs * halves, warp == kMmaWarp ? 0 : 1,
+                                         lo_first_group(kslabs));
     } else if (warp < kEpilogueWarp) {
         split_all<T::SLAB, S>(r, items, T::N, kslabs * halves);
     } else {
@@ -791,7 +841,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_backward_wide(const __grid_const
 // 128 x NB accumulator. The tensor core's FP32 accumulation does not round to
 // nearest, so a sum over thousands of column chunks in one accumulator drifts
 // (measured: 6e-4 normwise on config 5's gradients against the float64
-// oracle); each accumulator therefore sums only kWgSegment of its issuer's
+// oracle); each accumulator therefore sums only kSegment of its issuer's
 // chunks before four drain warps fold it into a round-to-nearest FP32 sum in
 // shared memory and release it. The second issuer's segments are offset by
 // half a segment, so the two drains do not stall both issuers at once.
@@ -806,7 +856,6 @@ __global__ void __launch_bounds__(THREADS, 1) k_backward_wide(const __grid_const
 // M = 128 (the A lanes 64-127 are never written and their accumulator rows
 // never read) with N = 64.
 
-constexpr int kWgSegment = 16;            // chunks one accumulator sums before a drain
 constexpr int kWgBox = 32 * 32 * 4;       // 32 neurons x 32 columns
 constexpr int kWgEpilogueWarp = 6, kWgSecondMmaWarp = 10, kWgDrainWarp = 11, kWgSecondSplitWarp = 15;
 constexpr uint32_t kWgTmemColumns = 512;
@@ -819,6 +868,10 @@ struct WgShape {
     static constexpr int kStage = 3 * kOperand;       // dZ raw, Y raw (= hi), Y lo
     static constexpr int kStages = NB == 128 ? 3 : 6;
     static constexpr int kSums = NB * NB * 4;         // FP32 sums [column n][neuron m]
+    // chunks one accumulator sums before a drain: the 64-neuron slices (the
+    // layers of orders <= 3 networks, held to 1e-5) drain twice as often,
+    // halving the truncating adds of a segment's sum
+    static constexpr int kSegment = NB == 128 ? 16 : 8;
     // split warps: kSplitGroups groups of kSplitWarps (one per TMEM lane quarter
     // the slice uses) take chunks it = group, group + kSplitGroups, ...
     // (a third group of four warps for 128-neuron slices measured no faster)
@@ -845,16 +898,19 @@ __device__ __forceinline__ int mn32_index(int mn, int k) {
 
 // Segment k of issuer w holds its chunks [start, start + length): issuer 1's
 // first segment is half as long.
-__device__ __forceinline__ int wg_segment_length(int w, int k) { return k == 0 && w ? kWgSegment / 2 : kWgSegment; }
+template <int SEG>
+__device__ __forceinline__ int wg_segment_length(int w, int k) { return k == 0 && w ? SEG / 2 : SEG; }
+template <int SEG>
 __device__ __forceinline__ int wg_segments(int w, int count) {
     if (count <= 0) return 0;
-    const int first = wg_segment_length(w, 0);
-    return count <= first ? 1 : 1 + (count - first + kWgSegment - 1) / kWgSegment;
+    const int first = wg_segment_length<SEG>(w, 0);
+    return count <= first ? 1 : 1 + (count - first + SEG - 1) / SEG;
 }
 // ring index of the last chunk of segment k of issuer w (of `count` chunks)
+template <int SEG>
 __device__ __forceinline__ int wg_segment_end(int w, int k, int count) {
-    const int first = wg_segment_length(w, 0);
-    const int last_local = min(count, k == 0 ? first : first + k * kWgSegment) - 1;
+    const int first = wg_segment_length<SEG>(w, 0);
+    const int last_local = min(count, k == 0 ? first : first + k * SEG) - 1;
     return 2 * last_local + w;
 }
 
@@ -977,7 +1033,7 @@ __global__ void __launch_bounds__(WgShape<NB>::kThreads, 1) k_wgrad_ws(const __g
             int seg = 0, in_seg = 0;
             bool ok = true;
             for (int it = which; ok && it < chunks; it += 2) {
-                if (in_seg == wg_segment_length(which, seg)) {
+                if (in_seg == wg_segment_length<G::kSegment>(which, seg)) {
                     // the drain warps have folded the previous segment out of the accumulator
                     ok = tc::mbar_wait_or_abort(acc_empty + which, seg & 1, tcg::kWaitCycles, abort);
                     if (!ok) break;
@@ -999,7 +1055,7 @@ __global__ void __launch_bounds__(WgShape<NB>::kThreads, 1) k_wgrad_ws(const __g
                 }
                 tc::mma_commit(empty + st);
                 ++in_seg;
-                if (in_seg == wg_segment_length(which, seg) || it + 2 >= chunks) tc::mma_commit(acc_full + which);
+                if (in_seg == wg_segment_length<G::kSegment>(which, seg) || it + 2 >= chunks) tc::mma_commit(acc_full + which);
             }
             tc::mma_commit(drain);
             if (!tc::mbar_wait(drain, 0, tcg::kWaitCycles)) *abort = 1;
@@ -1097,14 +1153,15 @@ __global__ void __launch_bounds__(WgShape<NB>::kThreads, 1) k_wgrad_ws(const __g
         const uint32_t lane_base = tmem + (uint32_t(quarter * 32) << 16);
         if (mine_lane)
             for (int c = 0; c < NB; ++c) sums[c * NB + m] = 0.f;
-        const int total[2] = {wg_segments(0, mine[0]), wg_segments(1, mine[1])};
+        const int total[2] = {wg_segments<G::kSegment>(0, mine[0]), wg_segments<G::kSegment>(1, mine[1])};
         int next[2] = {0, 0};
         bool ok = true;
         while (ok && (next[0] < total[0] || next[1] < total[1])) {
             int w;
             if (next[0] >= total[0]) w = 1;
             else if (next[1] >= total[1]) w = 0;
-            else w = wg_segment_end(0, next[0], mine[0]) < wg_segment_end(1, next[1], mine[1]) ? 0 : 1;
+            else w = wg_segment_end<G::kSegment>(0, next[0], mine[0]) <
+                                                  wg_segment_end<G::kSegment>(1, next[1], mine[1]) ? 0 : 1;
             ok = warp_wait(acc_full + w, next[w] & 1, abort);
             if (!ok) break;
             tc::tc_fence_after();

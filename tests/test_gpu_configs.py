@@ -72,16 +72,19 @@ def test_config2_kernels(engine):
                       'backward_input_ws'], 1e-4)
 
 
-@pytest.mark.parametrize('tier', [0, 2], ids=['auto', 'tensor'])
+@pytest.mark.parametrize('tier', [0, 2, 4], ids=['auto', 'tensor', 'ffma'])
 def test_config3_kernels(engine, tier):
     """2 -> 64^3 -> 1 sigmoid, rows u, u_x, u_y, u_xx, u_yy, compiled integral
-    of (u_xx + u_yy + 1)^2 over points in the disk: the automatic tier's
-    exact-FP32 FFMA layers and the tensor-core layers (64 neurons: paired
-    column tiles, 64-neuron weight-gradient slices), both at 1e-5."""
+    of (u_xx + u_yy + 1)^2 over points in the disk: the tensor-core layers
+    (64 neurons: paired column tiles, lo-first term order, 64-neuron
+    weight-gradient slices), which the automatic tier takes at orders <= 3
+    when no hidden layer is wider than 64, and the exact-FP32 FFMA layers
+    (tier 4), both at 1e-5."""
     w = bench.config3_workload(2048)
-    kernels = (['input_forward', 'forward_ws', 'head_expression', 'weight_gradient_ws', 'backward_ws',
-                'backward_input_ws'] if tier == 2 else
-               ['input_forward', 'forward', 'head_expression', 'weight_gradient', 'backward', 'backward_input'])
+    kernels = (['input_forward', 'forward', 'head_expression', 'weight_gradient', 'backward', 'backward_input']
+               if tier == 4 else
+               ['input_forward', 'forward_ws', 'head_expression', 'weight_gradient_ws', 'backward_ws',
+                'backward_input_ws'])
     engine.set_tier(tier)
     try:
         check(engine, w, kernels, 1e-5)

@@ -10,9 +10,11 @@ costs against the float64 oracle, through the C ABI. B200 only.
 * The kind-5 gradient report of training (squared L2 norm, max |g|,
   non-finite count and first index per layer,
   cuda/reduction_kernels.cuh:81-98) against numpy on the gradient buffers.
-* Integral and polynomial costs on fast-tier networks of widths 64, 96 and
-  128: the fused expression head (integral costs, last hidden layer of 64 or
-  128 neurons) and the separate output-layer kernels (the other cases).
+* Integral and polynomial costs on fast-tier networks of widths 32, 64, 96
+  and 128: the fused expression head (integral costs, last hidden layer of
+  32, 64 or 128 neurons) and the separate output-layer kernels (the other
+  cases); at orders <= 3 the automatic tier runs widths 32 and 64 on the
+  3xTF32 tensor cores (lo-first term order) and 96 and 128 on exact-FP32 FFMA.
 
 Tolerances as in tests/golden_cases.py (1e-5 for orders <= 3, 1e-4 above).
 """
@@ -162,7 +164,7 @@ SCHEMA_CASES = [2, 4, 7]  # full 2D order 2, full 2D order 4, pure 2D order 2
 
 
 @pytest.mark.parametrize('sid', SCHEMA_CASES, ids=[codegen.SCHEMAS[i][0] for i in SCHEMA_CASES])
-@pytest.mark.parametrize('width', [64, 96, 128])
+@pytest.mark.parametrize('width', [32, 64, 96, 128])
 @pytest.mark.parametrize('kind', ['integral', 'polynomial'])
 def test_fast_tier_integral_and_polynomial_costs(engine, sid, width, kind):
     rows = codegen.SCHEMAS[sid][1]
@@ -196,7 +198,7 @@ def test_fast_tier_integral_and_polynomial_costs(engine, sid, width, kind):
         engine.timing(False)
     # integral costs on a last hidden layer of 32, 64 or 128 neurons take the
     # fused expression head; the others the fast tier's separate output layer
-    fused = kind == 'integral' and width in (64, 128)
+    fused = kind == 'integral' and width in (32, 64, 128)
     assert ('head_expression' if fused else 'output_backward') in report
     schema = jets.Schema(t[:, 1:])
     linear = [1, 0, 0, 0, 1]
