@@ -66,6 +66,20 @@ __device__ inline void cs_finish(CostStats v, CostStats* partials, unsigned* tic
     *total = cs_combine(*total, acc); *ticket = 0; } }
 )PRELUDE";
 
+// A power with a constant exponent: integer exponents 0-4 as products, the
+// rest through pow(). Double pow() is a long dependent chain, and in the fused
+// head the few sampling threads run it while the rest of the CTA waits at a
+// barrier; pow(x, 0) is 1 for every x (NaN included), as here, and the
+// products differ from pow() by at most an ulp or two of double.
+inline std::string power_expr(const std::string& a, double p) {
+    if (p == 0) return "1.0";
+    if (p == 1) return a;
+    if (p == 2) return "(" + a + " * " + a + ")";
+    if (p == 3) return "(" + a + " * " + a + " * " + a + ")";
+    if (p == 4) return "((" + a + " * " + a + ") * (" + a + " * " + a + "))";
+    return "pow(" + a + ", " + fmt_double(p) + ")";
+}
+
 // The per-sample program as a device function: the output components `yp`
 // (RO of them) of sample `sample` in, its loss added to `local` (times the
 // quadrature weight w), dE/dY (times w and the graph multiplier `scale`)
@@ -93,7 +107,7 @@ inline std::string expression_sample_function(const std::vector<ScalarNode>& nod
             case kSub: e = a + " - " + b; break;
             case kMul: e = a + " * " + b; break;
             case kDiv: e = "(" + b + " == 0 ? nan(\"\") : " + a + " / " + b + ")"; break;
-            case kPower: e = "pow(" + a + ", " + fmt_double(n.parameter) + ")"; break;
+            case kPower: e = power_expr(a, n.parameter); break;
             case kNeg: e = "-" + a; break;
             case kExp: e = "exp(" + a + ")"; break;
             case kLog: e = "log(" + a + ")"; break;
@@ -124,8 +138,8 @@ inline std::string expression_sample_function(const std::vector<ScalarNode>& nod
             case kPower:
                 da = n.parameter == 0 ? "0.0"
                                       : (n.parameter == 1 ? "1.0"
-                                                          : fmt_double(n.parameter) + " * pow(" + a + ", " +
-                                                                fmt_double(n.parameter - 1) + ")");
+                                                          : fmt_double(n.parameter) + " * " +
+                                                                power_expr(a, n.parameter - 1));
                 break;
             case kNeg: da = "-1.0"; break;
             case kExp: da = v; break;
