@@ -267,15 +267,32 @@ extern "C" __global__ void __launch_bounds__(128, 4) cpde_head(
     for (int j = 0; j < PB; ++j)
 #pragma unroll
       for (int r = 0; r < R; ++r) y[j][r] = p0 + j < points ? ybuf[b][j][r][t] : 0.f;
+    // the warp's partial output dot products of its PB points (component
+    // c = j RO + i), reduced over its 32 neurons by transposed butterflies: lane
+    // l ends with component g 32 + l, 31 shuffles per 32 components instead of
+    // 5 per component
+    constexpr int PV = PB * RO;
 #pragma unroll
-    for (int j = 0; j < PB; ++j)
+    for (int g = 0; g < (PV + 31) / 32; ++g) {
+      float v[32];
 #pragma unroll
-      for (int i = 0; i < RO; ++i) {
-        float v = w[i % O] * y[j][i / O];
-#pragma unroll
-        for (int s = 16; s; s >>= 1) v += __shfl_xor_sync(0xffffffffu, v, s);
-        if (lane == 0) zsum[lp][wl][j][i] = v;
+      for (int q = 0; q < 32; ++q) {
+        const int c = g * 32 + q, i = c % RO;
+        v[q] = c < PV ? w[i % O] * y[c / RO][i / O] : 0.f;
       }
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) {
+        const bool upper = lane & off;
+#pragma unroll
+        for (int q = 0; q < off; ++q) {
+          const float send = upper ? v[q] : v[q + off];
+          const float keep = upper ? v[q + off] : v[q];
+          v[q] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+        }
+      }
+      const int c = g * 32 + lane;
+      if (c < PV) (&zsum[lp][wl][0][0])[c] = v[0];
+    }
     __syncthreads();
     if (ml < PB && p0 + ml < points) {
       const int j = ml;
