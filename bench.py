@@ -306,6 +306,21 @@ def config2_workload(points=POINTS):
                     ('matching', targets, np.ones((len(t), 1, 1), np.float32)))
 
 
+def generic_workload(points=POINTS):
+    """A schema the fused tiers do not compile ahead of time (3D, all mixed
+    derivatives through order 2: 10 rows), on the config-2 widths: it runs the
+    generic tier (FFMA GEMMs plus table-driven jet kernels), the path every
+    user schema outside the generated ones takes. Matching against zero
+    targets, points uniform in [0,1]^3 (seed 5)."""
+    from cpde_b200.expressions import all_mixed, glorot_like, quadrature_inputs
+    t = all_mixed(2, 'xyz')
+    pts = np.random.default_rng(5).uniform(0, 1, (points, 3))
+    layers = [3, 128, 128, 128, 1]
+    return Workload('generic tier: 3->128^3->1 sigmoid, 3D order 2 all mixed (10 rows)', t,
+                    quadrature_inputs(pts, t), layers, [1, 0, 0, 0, 1], glorot_like(layers, seed=0),
+                    ('matching', np.zeros((len(t), 1, points), np.float32), np.ones((len(t), 1, 1), np.float32)))
+
+
 def config3_workload(points=262144):
     t, x, layers, weights, expr, qw = config3_inputs(points)
     return Workload('config 3 interior', t, x, layers, [1, 0, 0, 0, 1], weights,
@@ -838,6 +853,9 @@ def run_b200(args):
             # 64-wide order-2 network on the 3xTF32 tensor cores)
             line['config3_integral_ffma'] = same_gpu_comparison(local, config3_workload(), warm=3, iterations=10,
                                                                  batches=3, kernels=True, tier=4)
+            # a schema outside the generated fast-tier ones (generic tier)
+            line['generic_tier'] = same_gpu_comparison(local, generic_workload(), warm=2, iterations=5, batches=3,
+                                                       kernels=True)
             if not args.no_large_configs:
                 peaks, source = measured_peaks()
                 for key, make, ref_points in (('config4', config4_workload, 262144),
@@ -872,6 +890,9 @@ def main():
     p.add_argument('--profile-workload', choices=sorted(WORKLOADS),
                    help='only run --warmup + --steps plain epochs of one workload on GPU 0 (a short, '
                         'self-contained command to profile) and print its ms per epoch')
+    p.add_argument('--epoch-times', action='store_true',
+                   help='with --profile-workload: also time every epoch (CUDA events between epochs) and print '
+                        'the means of consecutive groups of 10, which show the GPU settling at its power cap')
     args = p.parse_args()
     if args.profile_workload:
         profile_workload(args)
@@ -882,6 +903,7 @@ def main():
 
 
 WORKLOADS = {'config2': lambda points: config2_workload(points or POINTS),
+             'generic': lambda points: generic_workload(points or POINTS),
              'config3': lambda points: config3_workload(points or 262144),
              'config4': lambda points: config4_workload(points or 1048576),
              'config5': lambda points: config5_workload(points or 4194304)}
@@ -901,16 +923,22 @@ def profile_workload(args):
         for _ in range(args.warmup):
             e.epoch(net, [cost])
         stream = torch.cuda.ExternalStream(e.stream())
-        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        events = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1 if args.epoch_times else 2)]
         torch.cuda.synchronize()
-        start.record(stream)
-        for _ in range(args.steps):
+        events[0].record(stream)
+        for i in range(args.steps):
             e.epoch(net, [cost])
-        stop.record(stream)
+            if args.epoch_times:
+                events[i + 1].record(stream)
+        events[-1].record(stream)
         torch.cuda.synchronize()
         loss, _ = e.epoch_result(net, sum(np.asarray(x).size for x in w.weights))
-    print(json.dumps(dict(workload=w.name, points=w.points, tier=args.tier, steps=args.steps,
-                          ms_per_epoch=start.elapsed_time(stop) / max(1, args.steps), loss=loss)))
+    line = dict(workload=w.name, points=w.points, tier=args.tier, steps=args.steps,
+                ms_per_epoch=events[0].elapsed_time(events[-1]) / max(1, args.steps), loss=loss)
+    if args.epoch_times:
+        ms = [events[i].elapsed_time(events[i + 1]) for i in range(args.steps)]
+        line['ms_per_epoch_by_10'] = [round(float(np.mean(ms[i:i + 10])), 3) for i in range(0, args.steps, 10)]
+    print(json.dumps(line))
 
 
 if __name__ == '__main__':
