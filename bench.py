@@ -310,15 +310,20 @@ def generic_workload(points=POINTS):
     """A schema the fused tiers do not compile ahead of time (3D, all mixed
     derivatives through order 2: 10 rows), on the config-2 widths: it runs the
     generic tier (FFMA GEMMs plus table-driven jet kernels), the path every
-    user schema outside the generated ones takes. Matching against zero
-    targets, points uniform in [0,1]^3 (seed 5)."""
+    user schema outside the generated ones takes. Matching against
+    f = sin(2 pi x) exp(-y) cos(pi z) and its derivatives, points uniform in
+    [0,1]^3 (seed 5)."""
     from cpde_b200.expressions import all_mixed, glorot_like, quadrature_inputs
     t = all_mixed(2, 'xyz')
     pts = np.random.default_rng(5).uniform(0, 1, (points, 3))
+    targets = np.zeros((len(t), 1, points), np.float32)
+    for i, (_, a, b, c) in enumerate(t):
+        targets[i, 0] = ((2 * np.pi) ** a * np.sin(2 * np.pi * pts[:, 0] + a * np.pi / 2) * (-1.0) ** b
+                         * np.exp(-pts[:, 1]) * np.pi ** c * np.cos(np.pi * pts[:, 2] + c * np.pi / 2))
     layers = [3, 128, 128, 128, 1]
     return Workload('generic tier: 3->128^3->1 sigmoid, 3D order 2 all mixed (10 rows)', t,
                     quadrature_inputs(pts, t), layers, [1, 0, 0, 0, 1], glorot_like(layers, seed=0),
-                    ('matching', np.zeros((len(t), 1, points), np.float32), np.ones((len(t), 1, 1), np.float32)))
+                    ('matching', targets, np.ones((len(t), 1, 1), np.float32)))
 
 
 def config3_workload(points=262144):
