@@ -492,7 +492,7 @@ void Engine::activate(NetRecord& n, uint64_t data_id, Context& ctx, int width, i
 template <bool TA, bool TB, bool BIAS, bool IND>
 static void launch_gemm(Engine& e, int M, int N, int K, const float* A, int lda, const float* B, int ldb, float* C,
                         int ldc, const float* bias, int R) {
-    dim3 grid((N + gemm::BN - 1) / gemm::BN, (M + gemm::BM - 1) / gemm::BM, 1);
+    dim3 grid(gemm::column_tiles(N, IND), (M + gemm::BM - 1) / gemm::BM, 1);
     CPDE_RUN(e, "gemm", (k_gemm<TA, TB, BIAS, IND><<<grid, gemm::THREADS, 0, e.stream>>>(M, N, K, A, lda, B, ldb, C,
                                                                                           ldc, bias, R, K)));
 }
@@ -532,12 +532,12 @@ void Engine::backward(NetRecord& n, Context& ctx, int points, float* target) {
         const int np = n.neurons[l - 1], nl = n.neurons[l];
         // weight gradient with the bias column appended: (nl x np+1) += dZ (nl x cols) . [A; 1_value]^T
         const int M = nl, N = np + 1;
-        long base = long((M + gemm::BM - 1) / gemm::BM) * ((N + gemm::BN - 1) / gemm::BN);
+        long base = long((M + gemm::BM - 1) / gemm::BM) * gemm::column_tiles(N, true);
         long splits = std::max(1L, std::min((2L * 148 + base - 1) / base, (cols + 255) / 256));
         long per = ((cols + splits - 1) / splits + gemm::BK - 1) / gemm::BK * gemm::BK;
         splits = (cols + per - 1) / per;
         n.partial.reserve(size_t(splits) * M * N);
-        dim3 grid((N + gemm::BN - 1) / gemm::BN, (M + gemm::BM - 1) / gemm::BM, unsigned(splits));
+        dim3 grid(gemm::column_tiles(N, true), (M + gemm::BM - 1) / gemm::BM, unsigned(splits));
         CPDE_RUN(*this, "gemm_wgrad",
                  (k_gemm<false, true, false, true><<<grid, gemm::THREADS, 0, stream>>>(
                      M, N, int(cols), cur, nl, n.act[l - 1].ptr, np, n.partial.ptr, M, nullptr, R, int(per))));
