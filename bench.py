@@ -1,6 +1,6 @@
 """Benchmark of the cPDE epoch on B200s (driver contract: one JSON line on rank 0).
 
-Workload: MLP 2->128->128->128->128->1 sigmoid,
+Workload (config 2, the headline configuration): MLP 2->128->128->128->128->1 sigmoid,
 float32, weights N(0, 1/fan_in) from seed 0 with zero biases, 65,536 points
 uniform in [0,1]^2 (seed 1), every pure and mixed derivative through order 6
 (28 rows), squared-error matching against sin(2 pi x) exp(-y) and its
