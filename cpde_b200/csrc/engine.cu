@@ -511,7 +511,17 @@ void Engine::forward(NetRecord& n, Context& ctx, int points) {
                                                W + long(nl) * np, R);
         if (!nonlin) continue;
         long total = long(nl) * points;
-        if (n.linear[l] == kSigmoid)
+        const int sg = grid_for(total, kJetStagedThreads);
+        const size_t sm = jet_staged_smem(R);
+        if (R <= kJetStagedRows && n.linear[l] == kSigmoid)
+            CPDE_RUN(*this, "jet_forward",
+                     k_jet_forward_staged<Sigmoid><<<sg, kJetStagedThreads, sm, stream>>>(
+                         Z, n.act[l].ptr, nl, points, R, ctx.tables.ptr));
+        else if (R <= kJetStagedRows)
+            CPDE_RUN(*this, "jet_forward",
+                     k_jet_forward_staged<Tanh><<<sg, kJetStagedThreads, sm, stream>>>(
+                         Z, n.act[l].ptr, nl, points, R, ctx.tables.ptr));
+        else if (n.linear[l] == kSigmoid)
             CPDE_RUN(*this, "jet_forward",
                      k_jet_forward_dyn<Sigmoid><<<grid_for(total), 256, 0, stream>>>(
                          Z, n.act[l].ptr, n.jet_scratch.ptr, nl, points, R, ctx.tables.ptr));
@@ -553,7 +563,17 @@ void Engine::backward(NetRecord& n, Context& ctx, int points, float* target) {
         } else {
             launch_gemm<true, false, false, false>(*this, np, int(cols), nl, W, nl, cur, nl, n.dy.ptr, np, nullptr, R);
             long total = long(np) * points;
-            if (n.linear[l - 1] == kSigmoid)
+            const int sg = grid_for(total, kJetStagedThreads);
+            const size_t sm = jet_staged_smem(R);
+            if (R <= kJetStagedRows && n.linear[l - 1] == kSigmoid)
+                CPDE_RUN(*this, "jet_adjoint",
+                         k_jet_adjoint_staged<Sigmoid><<<sg, kJetStagedThreads, sm, stream>>>(
+                             n.dy.ptr, n.act[l - 1].ptr, next, np, points, R, ctx.tables.ptr));
+            else if (R <= kJetStagedRows)
+                CPDE_RUN(*this, "jet_adjoint",
+                         k_jet_adjoint_staged<Tanh><<<sg, kJetStagedThreads, sm, stream>>>(
+                             n.dy.ptr, n.act[l - 1].ptr, next, np, points, R, ctx.tables.ptr));
+            else if (n.linear[l - 1] == kSigmoid)
                 CPDE_RUN(*this, "jet_adjoint",
                          k_jet_adjoint_dyn<Sigmoid><<<grid_for(total), 256, 0, stream>>>(
                              n.dy.ptr, n.act[l - 1].ptr, n.jet_scratch.ptr, next, np, points, R, ctx.tables.ptr));

@@ -402,6 +402,90 @@ __global__ void k_jet_adjoint_dyn(const float* __restrict__ dY, const float* __r
     }
 }
 
+// Staged variants for schemas of at most kJetStagedRows rows: each thread
+// keeps its element's rows of every jet it works on in its own column of
+// shared memory ([jet][row][thread]: consecutive threads, consecutive banks),
+// so the terms read shared memory instead of going back to the global arrays,
+// and the derivative jet s never leaves the SM. Three jets of 32 rows for 128
+// threads are 48 KB, the default shared-memory limit.
+constexpr int kJetStagedRows = 32, kJetStagedThreads = 128;
+inline size_t jet_staged_smem(int R) { return size_t(3) * R * kJetStagedThreads * sizeof(float); }
+
+template <class Act>
+__global__ void __launch_bounds__(kJetStagedThreads)
+k_jet_forward_staged(const float* __restrict__ Z, float* __restrict__ Y, int n, long points, int R,
+                     const int* __restrict__ tab) {
+    extern __shared__ float jet_stage[];
+    const int T = blockDim.x;
+    float* zs = jet_stage + threadIdx.x;  // row r of the thread's element at [r T]
+    float* ys = zs + R * T;
+    float* ss = ys + R * T;
+    const int* fwd = tab;
+    const int* sq = tab + (R + 1);
+    const long total = (long)n * points;
+    for (long e = blockIdx.x * (long)blockDim.x + threadIdx.x; e < total; e += (long)blockDim.x * gridDim.x) {
+        const int m = int(e % n);
+        const long p = e / n;
+        const size_t base = (size_t)p * R * n + m;
+        for (int r = 0; r < R; ++r) zs[r * T] = Z[base + (size_t)r * n];
+        float y0, s0;
+        Act::value(zs[0], y0, s0);
+        ys[0] = y0;
+        ss[0] = s0;
+        Y[base] = y0;
+        const float lead = Act::lead(y0);
+        for (int r = 1; r < R; ++r) {
+            float acc = 0.f;
+            for (int t = fwd[r]; t < fwd[r + 1]; t += 3)
+                acc = fmaf(tcoef(tab, t) * ss[tab[t + 1] * T], zs[tab[t + 2] * T], acc);
+            ys[r * T] = acc;
+            Y[base + (size_t)r * n] = acc;
+            float sacc = lead * acc;
+            for (int t = sq[r]; t < sq[r + 1]; t += 3)
+                sacc = fmaf(-tcoef(tab, t) * ys[tab[t + 1] * T], ys[tab[t + 2] * T], sacc);
+            ss[r * T] = sacc;
+        }
+    }
+}
+
+template <class Act>
+__global__ void __launch_bounds__(kJetStagedThreads)
+k_jet_adjoint_staged(const float* __restrict__ dY, const float* __restrict__ Y, float* __restrict__ dZ, int n,
+                     long points, int R, const int* __restrict__ tab) {
+    extern __shared__ float jet_stage[];
+    const int T = blockDim.x;
+    float* ys = jet_stage + threadIdx.x;
+    float* gs = ys + R * T;
+    float* ss = gs + R * T;
+    const int* sq = tab + (R + 1);
+    const int* adj = tab + 2 * (R + 1);
+    const long total = (long)n * points;
+    for (long e = blockIdx.x * (long)blockDim.x + threadIdx.x; e < total; e += (long)blockDim.x * gridDim.x) {
+        const int m = int(e % n);
+        const long p = e / n;
+        const size_t base = (size_t)p * R * n + m;
+        for (int r = 0; r < R; ++r) {
+            ys[r * T] = Y[base + (size_t)r * n];
+            gs[r * T] = dY[base + (size_t)r * n];
+        }
+        const float y0 = ys[0];
+        ss[0] = Act::slope_from_value(y0);
+        const float lead = Act::lead(y0);
+        for (int r = 1; r < R; ++r) {
+            float sacc = lead * ys[r * T];
+            for (int t = sq[r]; t < sq[r + 1]; t += 3)
+                sacc = fmaf(-tcoef(tab, t) * ys[tab[t + 1] * T], ys[tab[t + 2] * T], sacc);
+            ss[r * T] = sacc;
+        }
+        for (int r = 0; r < R; ++r) {
+            float acc = 0.f;
+            for (int t = adj[r]; t < adj[r + 1]; t += 3)
+                acc = fmaf(tcoef(tab, t) * ss[tab[t + 1] * T], gs[tab[t + 2] * T], acc);
+            dZ[base + (size_t)r * n] = acc;
+        }
+    }
+}
+
 // ---------------------------------------------------------------------------
 // Costs. One thread per point of the chunk; every output component of the
 // point is handled by that thread, so equations that share components add
