@@ -222,7 +222,11 @@ __host__ __device__ constexpr int mma_issuers(int S, int slabs) { return S > sla
 // tile (or per tile half: the slabs of the two halves of a paired work item
 // touch disjoint accumulator lanes) for layers of at most 64 inputs, whose
 // one or two slabs per group leave the rest of the ring to the loads ahead.
-// the term-order group of a layer with kslabs K slabs per tile (half)
+// Measured on 96 order-2/3 cost cases of 32- and 64-neuron networks: the
+// worst gradient error against the float64 oracle went 5.1e-6 -> 1.1e-6, for
+// about 8% more time in the paired forward (the stages are held longer).
+
+// The term-order group of a layer with kslabs K slabs per tile (or tile half).
 __device__ __forceinline__ int lo_first_group(int kslabs) { return kslabs <= 2 ? kslabs : 0; }
 
 template <int N, int SLAB, int S = STAGES>
