@@ -162,17 +162,26 @@ def hbm_roofline(kernels, steps, points, rows, peaks, source):
     return roofline, rows_out
 
 
-def cpu_baseline(points=128, steps=2, processes=None):
-    """Reference CPU server (built from the reference's own sources; this
-    image has no system CBLAS, so its CMake default CPDE_CPU_BLAS=AUTO would
-    also pick the portable serial BLAS) on a bounded sample of the same
-    workload. The server is single-threaded, so it uses the host's cores the
-    way the path shards: one server process per core, each on its own
-    `points`-point slice, all running their op-90 epochs at once; the
-    throughput is the sum over processes (capped at 64 processes)."""
-    exe = ROOT / 'oracle' / '_ref' / 'cpde_ref_cpu_server'
+def cpu_baseline(points=512, steps=2, processes=None):
+    """Reference CPU server (built from the reference's own sources by
+    oracle/Makefile) on a bounded sample of the same workload. The build used
+    is the one with the reference's CPDE_CPU_CBLAS option linked against the
+    OpenBLAS that numpy ships (this image has no system CBLAS; 6.4x faster
+    than the portable serial BLAS on a 256-point config-2 epoch, same loss);
+    the portable serial build stands in where that one is absent. The
+    server's jet, cost and reduction kernels are single-threaded, so it uses
+    the host's cores the way the path shards: one server process per core
+    (one BLAS thread each), each on its own `points`-point slice, all running
+    their op-90 epochs at once; the throughput is the sum over processes
+    (capped at 64 processes)."""
+    exe = ROOT / 'oracle' / '_ref' / 'cpde_ref_cpu_server_blas'
+    blas = exe.exists()
+    if not blas:
+        exe = ROOT / 'oracle' / '_ref' / 'cpde_ref_cpu_server'
     if not exe.exists():
         return None
+    env = dict(os.environ)
+    env['OPENBLAS_NUM_THREADS'] = '1'
     import threading
     from cpde_b200.client import Data, Network, Session
     if processes is None:
@@ -184,7 +193,7 @@ def cpu_baseline(points=128, steps=2, processes=None):
 
     def run(i):
         sl = slice(i * points, (i + 1) * points)
-        with Session(exe) as s:
+        with Session(exe, env=env) as s:
             net = Network(s, LAYERS, weights=weights)
             inp = Data(s, x[:, :, sl], t)
             tgt = Data(s, targets[:, :, sl], t)
@@ -200,8 +209,10 @@ def cpu_baseline(points=128, steps=2, processes=None):
         th.join()
     ms = max(results)
     return dict(value=sum(points * R / (r / 1000) for r in results), unit=UNIT, cores=processes, kind='reference',
-                sample=f'{processes} concurrent cpde_ref_cpu_server processes (oracle/Makefile, serial CPU '
-                       f'backend, one per core), each on its own {points} of the workload\'s points, {steps} op-90 '
+                sample=f'{processes} concurrent {exe.name} processes (oracle/Makefile, CPU backend, '
+                       + ('CPDE_CPU_CBLAS against numpy\'s OpenBLAS, one BLAS thread each' if blas else
+                          'portable serial BLAS') +
+                       f', one per core), each on its own {points} of the workload\'s points, {steps} op-90 '
                        'epochs, median per process, throughput summed',
                 ms_per_epoch_sample=ms)
 
@@ -884,7 +895,7 @@ def main():
     p.add_argument('--warmup', type=int, default=3)
     p.add_argument('--impl', default='b200', choices=['b200', 'reference'])
     p.add_argument('--points', type=int, default=POINTS)
-    p.add_argument('--reference-points', type=int, default=128)
+    p.add_argument('--reference-points', type=int, default=512)
     p.add_argument('--no-cpu-baseline', action='store_true')
     p.add_argument('--no-reference-cuda', action='store_true')
     p.add_argument('--tier', type=int, default=0,
