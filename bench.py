@@ -14,7 +14,6 @@ gradients with one NCCL all-reduce per epoch.
 """
 import argparse
 import json
-import math
 import os
 import statistics
 import subprocess

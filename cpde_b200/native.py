@@ -5,12 +5,11 @@ Importing this module never falls back to anything: if libcpde_b200.so is
 missing or fails to load, ``load()`` raises.
 """
 import ctypes
-import struct
 from pathlib import Path
 
 import numpy as np
 
-from .wire import Reader, Writer, decode_state, encode_state, read_metadata
+from .wire import Reader, Writer, decode_state, encode_state
 
 LIBRARY = Path(__file__).resolve().parent / 'libcpde_b200.so'
 SERVER = Path(__file__).resolve().parent / 'bin' / 'cpde_server'

@@ -10,7 +10,6 @@ relative error of the outputs and per-layer normwise relative error of the
 weight gradients below 1e-5 when the highest order is <= 3 and 1e-4 for
 orders 4-6; objectives within the same relative bound. B200 only.
 """
-import numpy as np
 import pytest
 
 import bench

@@ -11,7 +11,7 @@ import pytest
 import golden_cases as gc
 from cpde_b200 import native
 from cpde_b200.client import Data, Network, Session, sum_graph
-from cpde_b200.wire import Writer, decode_state
+from cpde_b200.wire import Writer
 
 pytestmark = pytest.mark.gpu
 
